@@ -1,0 +1,1047 @@
+// engine.cpp -- model loading into HBM, device state, per-frame enqueue
+// sequences and CUDA graphs.  See engine.h for the overall structure.
+#include "engine.h"
+
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "launch.h"
+
+extern "C" void bmo_quantize_q4_0_ref(const float *x, long long n, uint8_t *out);
+
+namespace bmo {
+
+namespace {
+
+void ck(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int env_int(const char *name, int fallback) {
+    const char *v = std::getenv(name);
+    return (v && *v) ? std::atoi(v) : fallback;
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+std::string fmt(const char *f, int i) {
+    char b[160];
+    std::snprintf(b, sizeof b, f, i);
+    return b;
+}
+std::string fmt2(const char *f, int i, int j) {
+    char b[160];
+    std::snprintf(b, sizeof b, f, i, j);
+    return b;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// construction
+// ---------------------------------------------------------------------------
+Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg) {
+    int n_dev = 0;
+    if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev <= 0) {
+        cudaGetLastError();
+        throw std::runtime_error("no CUDA device available: libbmo runs the decode step on the GPU only");
+    }
+    device = cfg.device >= 0 ? cfg.device : env_int("BMO_DEVICE", -1);
+    if (device < 0) ck(cudaGetDevice(&device), "cudaGetDevice");
+    if (device >= n_dev) throw std::runtime_error("BMO device index out of range");
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major < 10) throw std::runtime_error("libbmo is built for sm_100a (B200); this device is sm_" +
+                                                  std::to_string(prop.major * 10 + prop.minor));
+    sm_count = prop.multiProcessorCount;
+    ck(configure_kernels(), "configure kernels");
+    ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    cfg_.graphs = cfg.graphs && env_int("BMO_GRAPHS", 1) != 0;
+    cfg_.pdl = cfg.pdl && env_int("BMO_PDL", 1) != 0;
+    n_ctx = cfg.n_ctx > 0 ? cfg.n_ctx : 2048;
+    if (cfg.kv_type >= 0) {
+        kv_type = cfg.kv_type;
+    } else {
+        const char *kt = std::getenv("BMO_KV_TYPE");
+        kv_type = (kt && (std::strcmp(kt, "q4_0") == 0 || std::strcmp(kt, "q4") == 0)) ? kKvQ4_0 : kKvF16;
+    }
+    load(gguf_path);
+    alloc_state();
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    auto drop = [](cudaGraphExec_t &g) {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    };
+    drop(g_temporal_);
+    drop(g_layers_);
+    drop(g_cascade_);
+    drop(g_frame_);
+    for (auto &g : g_depth_) drop(g);
+    for (void *p : allocs_) cudaFree(p);
+    for (void *p : {(void *)fin_h_, (void *)z_h_, (void *)logits_h_, (void *)zin_h_, (void *)dlogits_h_,
+                    (void *)tok_h_, (void *)status_h_})
+        if (p) cudaFreeHost(p);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+void *Engine::arena(size_t bytes) {
+    const size_t off = round_up(arena_used_, 256);
+    if (off + bytes > arena_size_) throw std::runtime_error("internal: weight arena overflow");
+    arena_used_ = off + bytes;
+    return arena_ + off;
+}
+
+static size_t q4_tiled_bytes(int64_t rows, int64_t cols, int perm, int swiglu_f) {
+    const int64_t nbx = round_up(static_cast<size_t>(cols / 32), kChunkBlocks);
+    const int64_t tiles = perm == kPermSwiGLU ? swiglu_f / 16 : (rows + kTileRows - 1) / kTileRows;
+    return static_cast<size_t>(tiles * (nbx / kChunkBlocks) * kChunkBytes);
+}
+
+QMatDesc Engine::upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t row0, int64_t rows) {
+    if (!t) throw std::runtime_error("internal: null weight");
+    if (t->type != kTQ4_0) throw std::runtime_error("weight " + t->name + " is not Q4_0 (only Q4_0 GEMV weights are supported)");
+    const int64_t cols = t->ne[0];
+    if (cols % 32) throw std::runtime_error("weight " + t->name + ": row length not a multiple of 32");
+    if (rows < 0) rows = t->rows() - row0;
+    if (row0 + rows > t->rows()) throw std::runtime_error("weight " + t->name + ": row slice out of range");
+    QMatDesc m{};
+    m.rows = static_cast<int>(perm == kPermSwiGLU ? 2 * swiglu_f : rows);
+    m.cols = static_cast<int>(cols);
+    m.nbx = static_cast<int>(round_up(static_cast<size_t>(cols / 32), kChunkBlocks));
+    m.cpt = m.nbx / kChunkBlocks;
+    m.perm = perm;
+    m.swiglu_f = swiglu_f;
+    m.n_tiles = static_cast<int>(perm == kPermSwiGLU ? swiglu_f / 16 : (rows + kTileRows - 1) / kTileRows);
+    if (m.nbx > gemv_max_nbx()) throw std::runtime_error("weight " + t->name + ": row length exceeds the GEMV limit");
+    const size_t bytes = static_cast<size_t>(m.n_tiles) * m.cpt * kChunkBytes;
+    void *dst = arena(bytes);
+    m.tiles = static_cast<const uint8_t *>(dst);
+    const size_t row_bytes = static_cast<size_t>(cols / 32) * 18;
+    const size_t raw = row_bytes * static_cast<size_t>(rows);
+    if (raw > staging_bytes_) throw std::runtime_error("internal: staging buffer too small");
+    ck(cudaMemcpyAsync(staging_d_, t->data + static_cast<size_t>(row0) * row_bytes, raw, cudaMemcpyHostToDevice, stream),
+       "upload weight");
+    ck(launch_repack_q4_0(staging_d_, dst, static_cast<int>(rows), static_cast<int>(cols), m, stream), "repack");
+    ck(cudaStreamSynchronize(stream), "repack sync");
+    return m;
+}
+
+float *Engine::upload_f32(const GgufTensor *t, int64_t n) {
+    if (!t) return nullptr;
+    if (t->type != kTF32) throw std::runtime_error("tensor " + t->name + " must be F32");
+    if (static_cast<int64_t>(t->nbytes / 4) < n) throw std::runtime_error("tensor " + t->name + " is too short");
+    float *d = static_cast<float *>(arena(static_cast<size_t>(n) * 4));
+    ck(cudaMemcpy(d, t->data, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "upload f32");
+    return d;
+}
+
+EmbTable Engine::upload_table(const GgufTensor *t) {
+    EmbTable e{};
+    if (!t) return e;
+    switch (t->type) {
+    case kTF32: case kTF16: case kTBF16: case kTQ4_0: case kTQ8_0: break;
+    default: throw std::runtime_error("embedding table " + t->name + " has an unsupported type");
+    }
+    void *d = arena(t->nbytes);
+    ck(cudaMemcpy(d, t->data, t->nbytes, cudaMemcpyHostToDevice), "upload table");
+    e.data = d;
+    e.type = t->type;
+    e.rows = static_cast<int>(t->rows());
+    e.dim = static_cast<int>(t->ne[0]);
+    e.row_bytes = ggml_row_bytes(t->type, t->ne[0]);
+    return e;
+}
+
+// Tensor-name contract and hyperparameters of the reference loader
+// (src/bmo.cpp:285-568).
+void Engine::load(const std::string &path) {
+    file_.open(path);
+    const GgufFile &g = file_;
+    auto any = [&](std::initializer_list<std::string> names) -> const GgufTensor * {
+        for (const auto &n : names)
+            if (const GgufTensor *t = g.find(n)) return t;
+        return nullptr;
+    };
+
+    n_layers = g.scalar_i32("n_layers", 0);
+    if (n_layers <= 0) n_layers = g.scalar_i32("n_layer", 32);
+    n_heads = g.scalar_i32("n_heads", 0);
+    if (n_heads <= 0) n_heads = g.scalar_i32("n_head", 0);
+    n_embd = g.scalar_i32("n_embd", 0);
+    if (n_embd <= 0) n_embd = g.scalar_i32("hidden_size", 0);
+    head_dim = g.scalar_i32("head_dim", 0);
+    if (head_dim <= 0) head_dim = g.scalar_i32("n_embd_head_k", 0);
+    rope_theta = g.scalar_f32("rope_theta", 0.0f);
+    if (rope_theta <= 0.0f) rope_theta = g.scalar_f32("rope_freq_base", 0.0f);
+    if (rope_theta <= 0.0f) rope_theta = 10000.0f;
+    norm_eps = g.scalar_f32("norm_eps", 0.0f);
+    if (norm_eps <= 0.0f) norm_eps = g.scalar_f32("rms_norm_eps", 0.0f);
+    if (norm_eps <= 0.0f) norm_eps = 1e-8f;
+    if (n_heads <= 0) n_heads = 32;
+    if (n_embd <= 0) n_embd = 4096;
+    if (head_dim <= 0) head_dim = n_embd / n_heads;
+    if (n_layers <= 0 || n_layers > 1024) throw std::runtime_error("implausible n_layers");
+
+    struct Names { const GgufTensor *qkv, *wo, *fin, *fout, *n1, *n2; };
+    std::vector<Names> ln(n_layers);
+    for (int i = 0; i < n_layers; ++i) {
+        const std::string b = "transformer_layers_" + std::to_string(i);
+        ln[i].qkv = any({b + "_self_attn_in_proj_weight", b + "_self_attn_in_proj"});
+        ln[i].wo = any({b + "_self_attn_out_proj_weight", b + "_self_attn_out_proj"});
+        ln[i].fin = any({b + "_gating_linear_in_weight", b + "_gating_linear_in"});
+        ln[i].fout = any({b + "_gating_linear_out_weight", b + "_gating_linear_out"});
+        ln[i].n1 = any({b + "_norm1_weight", b + "_attn_norm.weight", b + "_norm1.weight"});
+        ln[i].n2 = any({b + "_norm2_weight", b + "_ffn_norm.weight", b + "_norm2.weight"});
+        if (!ln[i].qkv || !ln[i].wo || !ln[i].fin || !ln[i].fout)
+            throw std::runtime_error("missing temporal weights for " + b);
+        if (!ln[i].n1 || !ln[i].n2) throw std::runtime_error("missing per-layer norm weights for " + b);
+    }
+    const int q_dim = n_heads * head_dim;
+    if (ln[0].qkv->ne[0] != n_embd) throw std::runtime_error("QKV width does not match n_embd");
+    const int64_t qkv_w = ln[0].qkv->rows();
+    if (qkv_w <= q_dim || (qkv_w - q_dim) % 2) throw std::runtime_error("invalid QKV width");
+    n_kv_heads = static_cast<int>((qkv_w - q_dim) / 2 / head_dim);
+    ffn = static_cast<int>(ln[0].fin->rows() / 2);
+    if (n_kv_heads <= 0 || n_heads % n_kv_heads) throw std::runtime_error("invalid KV head count");
+    if (head_dim != 64 && head_dim != 128) throw std::runtime_error("head_dim must be 64 or 128");
+    if (n_embd % 32 || ffn % 32 || ffn % 16) throw std::runtime_error("n_embd and FFN width must be multiples of 32");
+
+    // depformer (bmo.cpp:376-433)
+    const GgufTensor *dep_in_t[kDepQMax] = {}, *dep_emb_t[kDepQMax] = {}, *dep_head_t[kDepQMax] = {};
+    for (int k = 0; k < kDepQMax; ++k) {
+        dep_in_t[k] = g.find(fmt("depformer_in.%d.weight", k));
+        dep_emb_t[k] = g.find(fmt("depformer_emb.%d.weight", k));
+        dep_head_t[k] = g.find(fmt("linears.%d.weight", k));
+    }
+    const GgufTensor *dep_text_t = g.find("depformer_text_emb.weight");
+    const GgufTensor *tl = g.find("text_linear.weight");
+    const GgufTensor *tb = g.find("text_linear.bias");
+    const GgufTensor *on = g.find("out_norm_weight");
+
+    // temporal embeddings (bmo.cpp:491-508): emb.{k} trimmed after the last present
+    std::vector<const GgufTensor *> aemb(32, nullptr);
+    int last = -1;
+    for (int k = 0; k < 32; ++k) {
+        aemb[k] = g.find(fmt("emb.%d.weight", k));
+        if (aemb[k]) last = k;
+    }
+    aemb.resize(static_cast<size_t>(last + 1));
+    const GgufTensor *temb = g.find("text_emb.weight");
+
+    // geometry (bmo.cpp:510-568)
+    int nq = 0, in_vocab = 0;
+    for (auto *t : aemb)
+        if (t) {
+            ++nq;
+            if (!in_vocab) in_vocab = static_cast<int>(t->rows());
+        }
+    if (nq == 0)
+        for (auto *t : dep_emb_t)
+            if (t) {
+                ++nq;
+                if (!in_vocab) in_vocab = static_cast<int>(t->rows());
+            }
+    int dq = 0, out_vocab = 0;
+    for (int k = 0; k < kDepQMax; ++k) {
+        if (dep_in_t[k]) ++dq;
+        if (!out_vocab && dep_head_t[k]) out_vocab = static_cast<int>(dep_head_t[k]->rows());
+    }
+    n_q = nq;
+    num_codebooks = nq > 0 ? nq + 1 : 0;
+    dep_q = dq;
+    audio_vocab = out_vocab > 0 ? out_vocab : in_vocab;
+    text_vocab = tl ? static_cast<int>(tl->rows()) : temb ? static_cast<int>(temb->rows())
+               : dep_text_t ? static_cast<int>(dep_text_t->rows()) : 0;
+    if (num_codebooks > kMaxTokens) throw std::runtime_error("too many codebooks");
+
+    // depformer geometry: heads from an optional scalar, else the reference's 16
+    dep_heads = g.scalar_i32("depformer_num_heads", 16);
+    dep_dim = dep_in_t[0] ? static_cast<int>(dep_in_t[0]->rows()) : 0;
+    dep_hd = dep_heads > 0 ? dep_dim / dep_heads : 0;
+    dep_n_ctx = std::min(dep_q, kDepQMax);
+    struct DNames { const GgufTensor *in, *out, *n1, *n2, *gin[kDepQMax], *gout[kDepQMax]; };
+    std::vector<DNames> dn(kDepLayers);
+    bool dep_ok = dep_q > 0 && dep_dim > 0;
+    for (int i = 0; i < kDepLayers && dep_ok; ++i) {
+        const std::string dp = "depformer.layers." + std::to_string(i);
+        const std::string ub = "depformer_layers_" + std::to_string(i);
+        dn[i].n1 = any({dp + ".norm1.weight", ub + "_norm1_weight"});
+        dn[i].n2 = any({dp + ".norm2.weight", ub + "_norm2_weight"});
+        dn[i].in = any({dp + ".self_attn.in_proj_weight", ub + "_self_attn_in_proj_weight"});
+        dn[i].out = any({dp + ".self_attn.out_proj.weight", ub + "_self_attn_out_proj_weight"});
+        for (int s = 0; s < kDepQMax; ++s) {
+            dn[i].gin[s] = any({fmt2("depformer_layers_%d_gating_%d_linear_in_weight", i, s),
+                                fmt2("depformer_layers_%d_gating_%d_linear_in", i, s)});
+            dn[i].gout[s] = any({fmt2("depformer_layers_%d_gating_%d_linear_out_weight", i, s),
+                                 fmt2("depformer_layers_%d_gating_%d_linear_out", i, s)});
+        }
+        if (!dn[i].n1 || !dn[i].n2 || !dn[i].in || !dn[i].out) dep_ok = false;
+        for (int s = 0; s < dep_q && dep_ok; ++s)
+            if (!dn[i].gin[s] || !dn[i].gout[s]) dep_ok = false;
+    }
+    if (dep_ok) {
+        if (dep_hd != 64 && dep_hd != 128) throw std::runtime_error("depformer head_dim must be 64 or 128");
+        dep_ffn = static_cast<int>(dn[0].gin[0]->rows() / 2);
+        if (dep_ffn % 32) throw std::runtime_error("depformer FFN width must be a multiple of 32");
+    } else {
+        dep_q = dq;  // geometry still reported; depth calls fail with a clear error
+    }
+
+    // ---- size the weight arena ----
+    size_t total = 0, staging = 0;
+    auto plan_q4 = [&](const GgufTensor *t, int perm, int f, int64_t rows) {
+        if (!t) return;
+        const int64_t r = rows < 0 ? t->rows() : rows;
+        total += round_up(q4_tiled_bytes(r, t->ne[0], perm, f), 256);
+        staging = std::max(staging, static_cast<size_t>(r * (t->ne[0] / 32) * 18));
+    };
+    auto plan_bytes = [&](const GgufTensor *t) {
+        if (t) total += round_up(t->nbytes, 256);
+    };
+    for (int i = 0; i < n_layers; ++i) {
+        plan_q4(ln[i].qkv, kPermIdentity, 0, -1);
+        plan_q4(ln[i].wo, kPermIdentity, 0, -1);
+        plan_q4(ln[i].fin, kPermSwiGLU, ffn, -1);
+        plan_q4(ln[i].fout, kPermIdentity, 0, -1);
+        plan_bytes(ln[i].n1);
+        plan_bytes(ln[i].n2);
+    }
+    plan_q4(tl, kPermIdentity, 0, -1);
+    plan_bytes(tb);
+    plan_bytes(on);
+    plan_bytes(temb);
+    for (auto *t : aemb) plan_bytes(t);
+    if (dep_ok) {
+        for (int k = 0; k < dep_q; ++k) {
+            plan_q4(dep_in_t[k], kPermIdentity, 0, -1);
+            plan_q4(dep_head_t[k], kPermIdentity, 0, -1);
+            plan_bytes(dep_emb_t[k]);
+        }
+        plan_bytes(dep_text_t);
+        for (int i = 0; i < kDepLayers; ++i) {
+            for (int s = 0; s < dep_q; ++s) {
+                plan_q4(dn[i].in, kPermIdentity, 0, 3LL * dep_dim);
+                plan_q4(dn[i].out, kPermIdentity, 0, dep_dim);
+                plan_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, -1);
+                plan_q4(dn[i].gout[s], kPermIdentity, 0, -1);
+            }
+            plan_bytes(dn[i].n1);
+            plan_bytes(dn[i].n2);
+        }
+    }
+    arena_size_ = total + 4096;
+    ck(cudaMalloc(&arena_, arena_size_), "cudaMalloc weights");
+    allocs_.push_back(arena_);
+    staging_bytes_ = std::max<size_t>(staging, 16);
+    ck(cudaMalloc(&staging_d_, staging_bytes_), "cudaMalloc staging");
+
+    // ---- upload ----
+    L_.resize(n_layers);
+    for (int i = 0; i < n_layers; ++i) {
+        L_[i].qkv = upload_q4(ln[i].qkv, kPermIdentity, 0, 0, -1);
+        L_[i].wo = upload_q4(ln[i].wo, kPermIdentity, 0, 0, -1);
+        if (ln[i].fin->rows() != 2LL * ffn) throw std::runtime_error("FFN-in width differs between layers");
+        L_[i].ffn_in = upload_q4(ln[i].fin, kPermSwiGLU, ffn, 0, -1);
+        L_[i].ffn_out = upload_q4(ln[i].fout, kPermIdentity, 0, 0, -1);
+        L_[i].norm1 = upload_f32(ln[i].n1, n_embd);
+        L_[i].norm2 = upload_f32(ln[i].n2, n_embd);
+        if (L_[i].qkv.rows != qkv_w || L_[i].wo.rows != n_embd || L_[i].wo.cols != q_dim ||
+            L_[i].ffn_out.cols != ffn || L_[i].ffn_out.rows != n_embd)
+            throw std::runtime_error("inconsistent temporal weight shapes in layer " + std::to_string(i));
+    }
+    if (tl) {
+        if (tl->ne[0] != n_embd) throw std::runtime_error("text_linear width does not match n_embd");
+        text_head_ = upload_q4(tl, kPermIdentity, 0, 0, -1);
+        has_text_head = true;
+    }
+    text_bias_ = (tb && tb->type == kTF32 && static_cast<int64_t>(tb->nbytes / 4) >= text_vocab) ? upload_f32(tb, text_vocab)
+                                                                                                  : nullptr;
+    out_norm_ = on ? upload_f32(on, n_embd) : nullptr;
+    std::vector<EmbTable> tt(1 + aemb.size());
+    tt[0] = upload_table(temb);
+    for (size_t k = 0; k < aemb.size(); ++k) tt[1 + k] = upload_table(aemb[k]);
+    n_ttables_ = static_cast<int>(tt.size());
+    ttables_d_ = static_cast<EmbTable *>(arena(sizeof(EmbTable) * tt.size()));
+    ck(cudaMemcpy(ttables_d_, tt.data(), sizeof(EmbTable) * tt.size(), cudaMemcpyHostToDevice), "upload tables");
+
+    if (dep_ok) {
+        for (int k = 0; k < dep_q; ++k) {
+            if (dep_in_t[k]) dep_in_[k] = upload_q4(dep_in_t[k], kPermIdentity, 0, 0, -1);
+            if (dep_head_t[k]) {
+                dep_head_[k] = upload_q4(dep_head_t[k], kPermIdentity, 0, 0, -1);
+                has_dep_head[k] = dep_head_[k].cols == dep_dim;
+            }
+            dep_emb_[k] = upload_table(dep_emb_t[k]);
+        }
+        dep_text_emb_ = upload_table(dep_text_t);
+        has_dep_tables = dep_text_t != nullptr;
+        for (int i = 0; i < kDepLayers; ++i) {
+            for (int s = 0; s < dep_q; ++s) {
+                // per-step row slices of the stacked projections (bmo_compute.cpp:2908-2932)
+                D_[i].qkv[s] = upload_q4(dn[i].in, kPermIdentity, 0, 3LL * dep_dim * s, 3LL * dep_dim);
+                D_[i].wo[s] = upload_q4(dn[i].out, kPermIdentity, 0, static_cast<int64_t>(dep_dim) * s, dep_dim);
+                D_[i].ffn_in[s] = upload_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, 0, -1);
+                D_[i].ffn_out[s] = upload_q4(dn[i].gout[s], kPermIdentity, 0, 0, -1);
+            }
+            D_[i].norm1 = upload_f32(dn[i].n1, dep_dim);
+            D_[i].norm2 = upload_f32(dn[i].n2, dep_dim);
+        }
+    } else {
+        dep_dim = 0;
+    }
+    cudaFree(staging_d_);
+    staging_d_ = nullptr;
+    device_bytes += arena_size_;
+}
+
+void Engine::alloc_state() {
+    auto dalloc = [&](size_t bytes) -> void * {
+        void *p = nullptr;
+        ck(cudaMalloc(&p, std::max<size_t>(bytes, 16)), "cudaMalloc state");
+        ck(cudaMemset(p, 0, std::max<size_t>(bytes, 16)), "cudaMemset state");
+        allocs_.push_back(p);
+        device_bytes += bytes;
+        return p;
+    };
+    const size_t kv_elems = static_cast<size_t>(n_layers) * n_kv_heads * n_ctx * head_dim;
+    if (kv_type == kKvF16) {
+        kv_plane_bytes_ = kv_elems * 2;
+        kv_scale_bytes_ = 0;
+    } else {
+        kv_plane_bytes_ = kv_elems / 2;
+        kv_scale_bytes_ = kv_elems / 32 * 2;
+        k_scale_ = static_cast<uint8_t *>(dalloc(kv_scale_bytes_));
+        v_scale_ = static_cast<uint8_t *>(dalloc(kv_scale_bytes_));
+    }
+    k_cache_ = dalloc(kv_plane_bytes_);
+    v_cache_ = dalloc(kv_plane_bytes_);
+
+    const int q_dim = n_heads * head_dim, kv_dim = n_kv_heads * head_dim;
+    resid_ = static_cast<float *>(dalloc(sizeof(float) * n_embd * (n_layers + 1)));
+    xmid_ = static_cast<float *>(dalloc(sizeof(float) * n_embd));
+    q_ = static_cast<float *>(dalloc(sizeof(float) * q_dim));
+    vraw_ = static_cast<float *>(dalloc(sizeof(float) * kv_dim));
+    attn_ = static_cast<float *>(dalloc(sizeof(float) * q_dim));
+    act_ = static_cast<float *>(dalloc(sizeof(float) * ffn));
+    z_ = static_cast<float *>(dalloc(sizeof(float) * n_embd));
+    logits_ = static_cast<float *>(dalloc(sizeof(float) * std::max(text_vocab, 1)));
+    rope_ = static_cast<float2 *>(dalloc(sizeof(float2) * head_dim / 2));
+    tpairs_ = static_cast<float2 *>(dalloc(sizeof(float2) * std::max(text_head_.n_tiles, 1)));
+
+    const int ddim = std::max(dep_dim, 32);
+    dkv_bytes_ = static_cast<size_t>(kDepLayers) * dep_heads * std::max(dep_n_ctx, 1) * std::max(dep_hd, 1) * 2;
+    dk_cache_ = static_cast<__half *>(dalloc(dkv_bytes_));
+    dv_cache_ = static_cast<__half *>(dalloc(dkv_bytes_));
+    dz_ = static_cast<float *>(dalloc(sizeof(float) * n_embd));
+    dxa_ = static_cast<float *>(dalloc(sizeof(float) * ddim));
+    dxb_ = static_cast<float *>(dalloc(sizeof(float) * ddim));
+    dq_ = static_cast<float *>(dalloc(sizeof(float) * ddim));
+    dvraw_ = static_cast<float *>(dalloc(sizeof(float) * ddim));
+    dattn_ = static_cast<float *>(dalloc(sizeof(float) * ddim));
+    dact_ = static_cast<float *>(dalloc(sizeof(float) * std::max(dep_ffn, 32)));
+    dlogits_ = static_cast<float *>(dalloc(sizeof(float) * kDepQMax * std::max(audio_vocab, 1)));
+    dpairs_stride_ = 1;
+    for (int k = 0; k < kDepQMax; ++k) dpairs_stride_ = std::max(dpairs_stride_, dep_head_[k].n_tiles);
+    dpairs_ = static_cast<float2 *>(dalloc(sizeof(float2) * kDepQMax * dpairs_stride_));
+    dep_pos_ = static_cast<int *>(dalloc(sizeof(int) * kDepQMax));
+    int dp[kDepQMax];
+    for (int k = 0; k < kDepQMax; ++k) dp[k] = k;
+    ck(cudaMemcpy(dep_pos_, dp, sizeof dp, cudaMemcpyHostToDevice), "dep pos");
+    tok_out_ = static_cast<int *>(dalloc(sizeof(int) * (1 + kDepQMax)));
+
+    // stream-K scratch sized for the largest matrix
+    size_t gp = 0, gc = 0;
+    auto acc = [&](const QMatDesc &m) {
+        if (!m.tiles) return;
+        gp = std::max(gp, static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float));
+        gc = std::max(gc, static_cast<size_t>(m.n_tiles) * sizeof(int));
+    };
+    for (auto &l : L_) { acc(l.qkv); acc(l.wo); acc(l.ffn_in); acc(l.ffn_out); }
+    acc(text_head_);
+    for (int k = 0; k < kDepQMax; ++k) { acc(dep_in_[k]); acc(dep_head_[k]); }
+    for (auto &d : D_)
+        for (int s = 0; s < kDepQMax; ++s) { acc(d.qkv[s]); acc(d.wo[s]); acc(d.ffn_in[s]); acc(d.ffn_out[s]); }
+    gpart_bytes_ = gp;
+    gcount_bytes_ = gc;
+    gpart_ = static_cast<float *>(dalloc(gp));
+    gcount_ = static_cast<int *>(dalloc(gc));
+
+    attn_splits_ = std::max(1, (n_ctx + attn_max_per_split() - 1) / attn_max_per_split());
+    const int maxh = std::max(n_heads, dep_heads);
+    apart_bytes_ = static_cast<size_t>(maxh) * attn_splits_ * (std::max(head_dim, dep_hd) + 2) * sizeof(float);
+    acount_bytes_ = static_cast<size_t>(maxh) * sizeof(int);
+    apart_ = static_cast<float *>(dalloc(apart_bytes_));
+    acount_ = static_cast<int *>(dalloc(acount_bytes_));
+    status_ = static_cast<int *>(dalloc(sizeof(int)));
+    fin_d_ = static_cast<FrameIn *>(dalloc(sizeof(FrameIn)));
+
+    auto halloc = [&](size_t bytes) -> void * {
+        void *p = nullptr;
+        ck(cudaHostAlloc(&p, std::max<size_t>(bytes, 16), cudaHostAllocDefault), "cudaHostAlloc");
+        std::memset(p, 0, std::max<size_t>(bytes, 16));
+        return p;
+    };
+    fin_h_ = static_cast<FrameIn *>(halloc(sizeof(FrameIn)));
+    z_h_ = static_cast<float *>(halloc(sizeof(float) * n_embd));
+    zin_h_ = static_cast<float *>(halloc(sizeof(float) * n_embd));
+    logits_h_ = static_cast<float *>(halloc(sizeof(float) * std::max(text_vocab, 1)));
+    dlogits_h_ = static_cast<float *>(halloc(sizeof(float) * std::max(audio_vocab, 1)));
+    tok_h_ = static_cast<int *>(halloc(sizeof(int) * (1 + kDepQMax)));
+    status_h_ = static_cast<int *>(halloc(sizeof(int)));
+    ck(cudaDeviceSynchronize(), "alloc sync");
+}
+
+// ---------------------------------------------------------------------------
+// enqueue sequences
+// ---------------------------------------------------------------------------
+int Engine::gemv_grid(const QMatDesc &m) const {
+    const long long nc = static_cast<long long>(m.n_tiles) * m.cpt;
+    long long g = std::min<long long>(sm_count, nc);
+    // keep the tiles one CTA touches within the shared-memory partial table
+    const long long need = (static_cast<long long>(m.n_tiles) + gemv_max_tiles_per_cta() - 3) /
+                           (gemv_max_tiles_per_cta() - 2);
+    g = std::max(g, std::min(need, nc));
+    return static_cast<int>(std::max<long long>(g, 1));
+}
+
+GemvArgs Engine::gemv_base(const QMatDesc &m) const {
+    GemvArgs a{};
+    a.W = m;
+    a.gpart = gpart_;
+    a.gcount = gcount_;
+    a.status = status_;
+    a.argmax_limit = INT_MAX;
+    return a;
+}
+
+void Engine::gemv(const GemvArgs &a, int pro, int epi, cudaStream_t s) {
+    ck(launch_gemv(a, pro, epi, gemv_grid(a.W), s, cfg_.pdl), "launch gemv");
+}
+
+void Engine::enqueue_temporal(cudaStream_t s) {
+    ck(launch_embed(ttables_d_, n_ttables_, fin_d_->tokens, &fin_d_->n_tok, n_embd, resid_, &fin_d_->pos, rope_theta,
+                    head_dim, rope_, s),
+       "launch embed");
+    for (int l = 0; l < n_layers; ++l) enqueue_layer(s, l);
+    if (has_text_head) {
+        GemvArgs h = gemv_base(text_head_);
+        h.x = resid_ + static_cast<size_t>(n_layers) * n_embd;
+        h.gamma = out_norm_;
+        h.eps = norm_eps;
+        h.xn_out = z_;
+        h.y = logits_;
+        h.bias = text_bias_;
+        h.argmax_pairs = tpairs_;
+        h.argmax_limit = text_vocab;
+        gemv(h, out_norm_ ? kProNorm : kProPlain, kEpiLogits, s);
+    }
+}
+
+// One temporal layer (bmo_compute.cpp:2188-2640): reads resid[l], writes resid[l+1].
+void Engine::enqueue_layer(cudaStream_t s, int l) {
+    const int q_dim = n_heads * head_dim, kv_dim = n_kv_heads * head_dim;
+    {
+        float *x_in = resid_ + static_cast<size_t>(l) * n_embd;
+        float *x_out = x_in + n_embd;
+        const long long layer_off = static_cast<long long>(l) * n_kv_heads * n_ctx * head_dim;
+
+        GemvArgs a = gemv_base(L_[l].qkv);
+        a.x = x_in;
+        a.gamma = L_[l].norm1;
+        a.eps = norm_eps;
+        a.y = q_;
+        a.q_dim = q_dim;
+        a.kv_dim = kv_dim;
+        a.head_dim = head_dim;
+        a.rope_cs = rope_;
+        a.k_cache = k_cache_;
+        a.v_cache = v_cache_;
+        a.k_scale = k_scale_;
+        a.v_scale = v_scale_;
+        a.kv_type = kv_type;
+        a.n_ctx = n_ctx;
+        a.pos = &fin_d_->pos;
+        a.kv_layer_off = layer_off;
+        a.v_out = vraw_;
+        gemv(a, kProNorm, kEpiQKV, s);
+
+        AttnArgs at{};
+        at.q = q_;
+        at.v_raw = vraw_;
+        at.k_cache = k_cache_;
+        at.v_cache = v_cache_;
+        at.k_scale = k_scale_;
+        at.v_scale = v_scale_;
+        at.kv_layer_off = layer_off;
+        at.n_heads = n_heads;
+        at.n_kv_heads = n_kv_heads;
+        at.n_ctx = n_ctx;
+        at.kv_type = kv_type;
+        at.pos = &fin_d_->pos;
+        at.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+        at.out = attn_;
+        at.part = apart_;
+        at.count = acount_;
+        at.status = status_;
+        ck(launch_attention(at, head_dim, attn_splits_, s, cfg_.pdl), "launch attention");
+
+        GemvArgs o = gemv_base(L_[l].wo);
+        o.x = attn_;
+        o.y = xmid_;
+        o.resid = x_in;
+        gemv(o, kProPlain, kEpiResid, s);
+
+        GemvArgs fi = gemv_base(L_[l].ffn_in);
+        fi.x = xmid_;
+        fi.gamma = L_[l].norm2;
+        fi.eps = norm_eps;
+        fi.y = act_;
+        gemv(fi, kProNorm, kEpiSwiGLU, s);
+
+        GemvArgs fo = gemv_base(L_[l].ffn_out);
+        fo.x = act_;
+        fo.y = x_out;
+        fo.resid = xmid_;
+        gemv(fo, kProPlain, kEpiResid, s);
+    }
+}
+
+// One depformer codebook step (bmo_build_depth_graph, bmo_compute.cpp:2741-3340).
+void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok) {
+    GemvArgs w = gemv_base(dep_in_[cb]);
+    w.x = z;
+    w.y = dxa_;
+    w.emb = cb == 0 ? dep_text_emb_ : dep_emb_[cb - 1];
+    w.tok = tok;
+    gemv(w, kProPlain, kEpiEmbAdd, s);
+    for (int i = 0; i < kDepLayers; ++i) {
+        const long long layer_off = static_cast<long long>(i) * dep_heads * dep_n_ctx * dep_hd;
+        GemvArgs a = gemv_base(D_[i].qkv[cb]);
+        a.x = dxa_;
+        a.gamma = D_[i].norm1;
+        a.eps = norm_eps;
+        a.y = dq_;
+        a.q_dim = dep_dim;
+        a.kv_dim = dep_dim;
+        a.head_dim = dep_hd;
+        a.rope_cs = nullptr;
+        a.k_cache = dk_cache_;
+        a.v_cache = dv_cache_;
+        a.kv_type = kKvF16;
+        a.n_ctx = dep_n_ctx;
+        a.pos = dep_pos_ + cb;
+        a.kv_layer_off = layer_off;
+        a.v_out = dvraw_;
+        gemv(a, kProNorm, kEpiQKV, s);
+
+        AttnArgs at{};
+        at.q = dq_;
+        at.v_raw = dvraw_;
+        at.k_cache = dk_cache_;
+        at.v_cache = dv_cache_;
+        at.kv_layer_off = layer_off;
+        at.n_heads = dep_heads;
+        at.n_kv_heads = dep_heads;
+        at.n_ctx = dep_n_ctx;
+        at.kv_type = kKvF16;
+        at.pos = dep_pos_ + cb;
+        at.scale = 1.0f / std::sqrt(static_cast<float>(dep_hd));
+        at.out = dattn_;
+        at.part = apart_;
+        at.count = acount_;
+        at.status = status_;
+        ck(launch_attention(at, dep_hd, 1, s, cfg_.pdl), "launch depth attention");
+
+        GemvArgs o = gemv_base(D_[i].wo[cb]);
+        o.x = dattn_;
+        o.y = dxb_;
+        o.resid = dxa_;
+        gemv(o, kProPlain, kEpiResid, s);
+
+        GemvArgs fi = gemv_base(D_[i].ffn_in[cb]);
+        fi.x = dxb_;
+        fi.gamma = D_[i].norm2;
+        fi.eps = norm_eps;
+        fi.y = dact_;
+        gemv(fi, kProNorm, kEpiSwiGLU, s);
+
+        GemvArgs fo = gemv_base(D_[i].ffn_out[cb]);
+        fo.x = dact_;
+        fo.y = dxa_;
+        fo.resid = dxb_;
+        gemv(fo, kProPlain, kEpiResid, s);
+    }
+    GemvArgs h = gemv_base(dep_head_[cb]);
+    h.x = dxa_;
+    h.y = dlogits_ + static_cast<size_t>(cb) * audio_vocab;
+    h.argmax_pairs = dpairs_ + static_cast<size_t>(cb) * dpairs_stride_;
+    h.argmax_limit = std::min(audio_vocab, 2048);
+    gemv(h, kProPlain, kEpiLogits, s);
+}
+
+void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
+    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
+    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
+    for (int cb = 0; cb < dep_q; ++cb) {
+        TokenSrc t{};
+        if (cb == 0) {
+            t = first;
+            t.tok_out = tok_out_;
+        } else {
+            t.pairs = dpairs_ + static_cast<size_t>(cb - 1) * dpairs_stride_;
+            t.n_pairs = dep_head_[cb - 1].n_tiles;
+            t.tok_out = tok_out_ + cb;
+        }
+        enqueue_depth_step(s, cb, z, t);
+    }
+    enqueue_finalize_tokens(s);
+}
+
+void Engine::enqueue_finalize_tokens(cudaStream_t s) {
+    const int cb = dep_q - 1;
+    ck(launch_finalize_token(dpairs_ + static_cast<size_t>(cb) * dpairs_stride_, dep_head_[cb].n_tiles,
+                             tok_out_ + 1 + cb, s, cfg_.pdl),
+       "launch finalize");
+}
+
+cudaGraphExec_t Engine::capture(const std::function<void(cudaStream_t)> &fn) {
+    cudaGraph_t g = nullptr;
+    ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+        fn(stream);
+    } catch (...) {
+        cudaStreamEndCapture(stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    ck(cudaStreamEndCapture(stream, &g), "end capture");
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+    cudaGraphDestroy(g);
+    ck(err, "graph instantiate");
+    return e;
+}
+
+void Engine::launch(cudaGraphExec_t &g, const std::function<void(cudaStream_t)> &fn) {
+    if (!cfg_.graphs) {
+        fn(stream);
+        return;
+    }
+    if (!g) g = capture(fn);
+    ck(cudaGraphLaunch(g, stream), "graph launch");
+}
+
+// Status word back to the host; a raised device error leaves the split
+// counters undefined, so they are cleared before the error is reported.
+void Engine::finish_call() {
+    ck(cudaMemcpyAsync(status_h_, status_, sizeof(int), cudaMemcpyDeviceToHost, stream), "status copy");
+    ck(cudaStreamSynchronize(stream), "stream sync");
+    if (*status_h_ != 0) {
+        const int st = *status_h_;
+        cudaMemsetAsync(status_, 0, sizeof(int), stream);
+        cudaMemsetAsync(gcount_, 0, gcount_bytes_, stream);
+        cudaMemsetAsync(acount_, 0, acount_bytes_, stream);
+        cudaStreamSynchronize(stream);
+        throw std::runtime_error("device status " + std::to_string(st) + ": a bulk copy wait timed out");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// operations
+// ---------------------------------------------------------------------------
+void Engine::run_temporal(const int32_t *tokens, int K, int pos) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    std::memset(fin_h_->tokens, 0, sizeof(fin_h_->tokens));
+    std::memcpy(fin_h_->tokens, tokens, sizeof(int32_t) * static_cast<size_t>(K));
+    fin_h_->n_tok = K;
+    fin_h_->pos = pos;
+    ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
+    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+    ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
+    if (has_text_head)
+        ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
+    finish_call();
+}
+
+void Engine::copy_resid(int layer, float *out) {
+    ck(cudaMemcpy(out, resid_ + static_cast<size_t>(layer + 1) * n_embd, sizeof(float) * n_embd,
+                  cudaMemcpyDeviceToHost),
+       "capture copy");
+}
+
+void Engine::run_layers(const float *x_in, int pos, int layer_begin, int layer_end, float *x_out) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    fin_h_->pos = pos;
+    fin_h_->n_tok = 0;
+    std::memcpy(zin_h_, x_in, sizeof(float) * n_embd);
+    ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
+    ck(cudaMemcpyAsync(resid_ + static_cast<size_t>(layer_begin) * n_embd, zin_h_, sizeof(float) * n_embd,
+                       cudaMemcpyHostToDevice, stream),
+       "hidden copy");
+    if (g_layers_ && (g_layers_range_[0] != layer_begin || g_layers_range_[1] != layer_end)) {
+        cudaGraphExecDestroy(g_layers_);
+        g_layers_ = nullptr;
+    }
+    g_layers_range_[0] = layer_begin;
+    g_layers_range_[1] = layer_end;
+    launch(g_layers_, [this, layer_begin, layer_end](cudaStream_t s) {
+        // RoPE table only (no embedding output)
+        ck(launch_embed(ttables_d_, 0, fin_d_->tokens, nullptr, n_embd, nullptr, &fin_d_->pos, rope_theta, head_dim,
+                        rope_, s),
+           "launch rope");
+        for (int l = layer_begin; l < layer_end; ++l) enqueue_layer(s, l);
+    });
+    ck(cudaMemcpyAsync(z_h_, resid_ + static_cast<size_t>(layer_end) * n_embd, sizeof(float) * n_embd,
+                       cudaMemcpyDeviceToHost, stream),
+       "hidden out copy");
+    finish_call();
+    std::memcpy(x_out, z_h_, sizeof(float) * n_embd);
+}
+
+void Engine::run_depth(int cb, int32_t prev, const float *z) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    std::memcpy(zin_h_, z, sizeof(float) * n_embd);
+    fin_h_->prev_token = prev;
+    ck(cudaMemcpyAsync(dz_, zin_h_, sizeof(float) * n_embd, cudaMemcpyHostToDevice, stream), "z in copy");
+    ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
+    launch(g_depth_[cb], [this, cb](cudaStream_t s) {
+        if (cb == 0) {
+            ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
+            ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
+        }
+        TokenSrc t{};
+        t.tok = &fin_d_->prev_token;
+        enqueue_depth_step(s, cb, dz_, t);
+    });
+    ck(cudaMemcpyAsync(dlogits_h_, dlogits_ + static_cast<size_t>(cb) * audio_vocab, sizeof(float) * audio_vocab,
+                       cudaMemcpyDeviceToHost, stream),
+       "audio logits copy");
+    finish_call();
+}
+
+void Engine::run_cascade_greedy(int32_t text_tok, const float *z, int32_t *out_tokens) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    std::memcpy(zin_h_, z, sizeof(float) * n_embd);
+    fin_h_->prev_token = text_tok;
+    ck(cudaMemcpyAsync(dz_, zin_h_, sizeof(float) * n_embd, cudaMemcpyHostToDevice, stream), "z in copy");
+    ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
+    launch(g_cascade_, [this](cudaStream_t s) {
+        TokenSrc t{};
+        t.tok = &fin_d_->prev_token;
+        enqueue_cascade(s, dz_, t);
+    });
+    ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
+    finish_call();
+    for (int cb = 0; cb < dep_q; ++cb) out_tokens[cb] = tok_h_[1 + cb];
+}
+
+void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *out_text_tok, int32_t *out_audio) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    std::memset(fin_h_->tokens, 0, sizeof(fin_h_->tokens));
+    std::memcpy(fin_h_->tokens, tokens, sizeof(int32_t) * static_cast<size_t>(K));
+    fin_h_->n_tok = K;
+    fin_h_->pos = pos;
+    ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
+    launch(g_frame_, [this](cudaStream_t s) {
+        enqueue_temporal(s);
+        TokenSrc t{};
+        t.pairs = tpairs_;
+        t.n_pairs = text_head_.n_tiles;
+        enqueue_cascade(s, z_, t);
+    });
+    ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
+    ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
+    ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
+    finish_call();
+    if (out_text_tok) *out_text_tok = tok_h_[0];
+    if (out_audio)
+        for (int cb = 0; cb < dep_q; ++cb) out_audio[cb] = tok_h_[1 + cb];
+}
+
+void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
+    launch(g_frame_, [this](cudaStream_t s) {
+        enqueue_temporal(s);
+        TokenSrc t{};
+        t.pairs = tpairs_;
+        t.n_pairs = text_head_.n_tiles;
+        enqueue_cascade(s, z_, t);
+    });
+    if (out_tokens_dev)
+        ck(cudaMemcpyAsync(out_tokens_dev, tok_out_, sizeof(int) * (1 + dep_q), cudaMemcpyDeviceToDevice, stream),
+           "tokens copy");
+}
+
+int Engine::sync_status() {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    finish_call();
+    return 0;
+}
+
+void Engine::capture_all() {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    if (!cfg_.graphs) {
+        graphs_ready_ = false;
+        return;
+    }
+    auto temporal = [this](cudaStream_t s) { enqueue_temporal(s); };
+    if (!g_temporal_) g_temporal_ = capture(temporal);
+    if (has_dep_tables && dep_dim > 0) {
+        for (int cb = 0; cb < dep_q; ++cb) {
+            if (g_depth_[cb]) continue;
+            g_depth_[cb] = capture([this, cb](cudaStream_t s) {
+                if (cb == 0) {
+                    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
+                    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
+                }
+                TokenSrc t{};
+                t.tok = &fin_d_->prev_token;
+                enqueue_depth_step(s, cb, dz_, t);
+            });
+        }
+        if (!g_cascade_)
+            g_cascade_ = capture([this](cudaStream_t s) {
+                TokenSrc t{};
+                t.tok = &fin_d_->prev_token;
+                enqueue_cascade(s, dz_, t);
+            });
+        if (!g_frame_ && has_text_head)
+            g_frame_ = capture([this](cudaStream_t s) {
+                enqueue_temporal(s);
+                TokenSrc t{};
+                t.pairs = tpairs_;
+                t.n_pairs = text_head_.n_tiles;
+                enqueue_cascade(s, z_, t);
+            });
+    }
+    graphs_ready_ = true;
+}
+
+void Engine::reset_kv() {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(cudaMemsetAsync(k_cache_, 0, kv_plane_bytes_, stream), "reset kv");
+    ck(cudaMemsetAsync(v_cache_, 0, kv_plane_bytes_, stream), "reset kv");
+    if (kv_scale_bytes_) {
+        ck(cudaMemsetAsync(k_scale_, 0, kv_scale_bytes_, stream), "reset kv");
+        ck(cudaMemsetAsync(v_scale_, 0, kv_scale_bytes_, stream), "reset kv");
+    }
+    ck(cudaStreamSynchronize(stream), "reset sync");
+}
+
+void Engine::reset_depth_kv() {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, stream), "reset depth kv");
+    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, stream), "reset depth kv");
+    ck(cudaStreamSynchronize(stream), "reset sync");
+}
+
+// Host-side conversion of fp32 rows into the ring format, one contiguous
+// run of slots per head.
+int Engine::kv_import(int layer, int slot0, int n, const float *k_rows, const float *v_rows) {
+    if (layer < 0 || layer >= n_layers || slot0 < 0 || n <= 0 || slot0 + n > n_ctx) return 2;
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    const int hd = head_dim;
+    std::vector<uint8_t> plane, scales;
+    for (int which = 0; which < 2; ++which) {
+        const float *src = which ? v_rows : k_rows;
+        uint8_t *cache = static_cast<uint8_t *>(which ? v_cache_ : k_cache_);
+        uint8_t *scale = which ? v_scale_ : k_scale_;
+        for (int h = 0; h < n_kv_heads; ++h) {
+            const size_t row0 = (static_cast<size_t>(layer) * n_kv_heads + h) * n_ctx + slot0;
+            std::vector<float> rows(static_cast<size_t>(n) * hd);
+            for (int i = 0; i < n; ++i)
+                std::memcpy(&rows[static_cast<size_t>(i) * hd], src + (static_cast<size_t>(i) * n_kv_heads + h) * hd,
+                            sizeof(float) * hd);
+            if (kv_type == kKvF16) {
+                std::vector<__half> hv(rows.size());
+                for (size_t e = 0; e < rows.size(); ++e) hv[e] = __float2half_rn(rows[e]);
+                ck(cudaMemcpy(cache + row0 * hd * 2, hv.data(), hv.size() * 2, cudaMemcpyHostToDevice), "kv import");
+            } else {
+                std::vector<uint8_t> blocks(rows.size() / 32 * 18);
+                bmo_quantize_q4_0_ref(rows.data(), static_cast<long long>(rows.size()), blocks.data());
+                plane.assign(rows.size() / 2, 0);
+                scales.assign(rows.size() / 32 * 2, 0);
+                for (size_t b = 0; b < rows.size() / 32; ++b) {
+                    std::memcpy(&scales[b * 2], &blocks[b * 18], 2);
+                    std::memcpy(&plane[b * 16], &blocks[b * 18 + 2], 16);
+                }
+                ck(cudaMemcpy(cache + row0 * hd / 2, plane.data(), plane.size(), cudaMemcpyHostToDevice), "kv import");
+                ck(cudaMemcpy(scale + row0 * (hd / 32) * 2, scales.data(), scales.size(), cudaMemcpyHostToDevice),
+                   "kv import");
+            }
+        }
+    }
+    return 0;
+}
+
+int Engine::copy_cache_f32(int which, int layer, int t_start, int n_positions, float *out) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(cudaStreamSynchronize(stream), "sync");
+    const int hd = head_dim;
+    const uint8_t *cache = static_cast<const uint8_t *>(which ? v_cache_ : k_cache_);
+    const uint8_t *scale = which ? v_scale_ : k_scale_;
+    int w = 0;
+    for (int h = 0; h < n_kv_heads; ++h) {
+        const size_t row0 = (static_cast<size_t>(layer) * n_kv_heads + h) * n_ctx + t_start;
+        std::vector<float> rows(static_cast<size_t>(n_positions) * hd);
+        if (kv_type == kKvF16) {
+            std::vector<__half> hv(rows.size());
+            ck(cudaMemcpy(hv.data(), cache + row0 * hd * 2, hv.size() * 2, cudaMemcpyDeviceToHost), "kv copy");
+            for (size_t e = 0; e < rows.size(); ++e) rows[e] = __half2float(hv[e]);
+        } else {
+            std::vector<uint8_t> plane(rows.size() / 2);
+            std::vector<__half> sc(rows.size() / 32);
+            ck(cudaMemcpy(plane.data(), cache + row0 * hd / 2, plane.size(), cudaMemcpyDeviceToHost), "kv copy");
+            ck(cudaMemcpy(sc.data(), scale + row0 * (hd / 32) * 2, sc.size() * 2, cudaMemcpyDeviceToHost), "kv copy");
+            for (size_t b = 0; b < sc.size(); ++b) {
+                const float d = __half2float(sc[b]);
+                for (int j = 0; j < 16; ++j) {
+                    rows[b * 32 + j] = static_cast<float>((plane[b * 16 + j] & 0x0F) - 8) * d;
+                    rows[b * 32 + 16 + j] = static_cast<float>((plane[b * 16 + j] >> 4) - 8) * d;
+                }
+            }
+        }
+        for (int p = 0; p < n_positions; ++p)
+            std::memcpy(out + (static_cast<size_t>(p) * n_kv_heads + h) * hd, &rows[static_cast<size_t>(p) * hd],
+                        sizeof(float) * hd);
+        w += n_positions * hd;
+    }
+    return w;
+}
+
+long long Engine::copy_kv_raw(int which, int part, int layer, void *out, long long max_bytes) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(cudaStreamSynchronize(stream), "sync");
+    const size_t layer_elems = static_cast<size_t>(n_kv_heads) * n_ctx * head_dim;
+    const uint8_t *src;
+    size_t bytes;
+    if (part == 0) {
+        const size_t per = kv_type == kKvF16 ? layer_elems * 2 : layer_elems / 2;
+        src = static_cast<const uint8_t *>(which ? v_cache_ : k_cache_) + per * layer;
+        bytes = per;
+    } else {
+        if (kv_type == kKvF16) return 0;
+        const size_t per = layer_elems / 32 * 2;
+        src = (which ? v_scale_ : k_scale_) + per * layer;
+        bytes = per;
+    }
+    if (static_cast<long long>(bytes) > max_bytes) return -2;
+    ck(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost), "kv raw copy");
+    return static_cast<long long>(bytes);
+}
+
+}  // namespace bmo

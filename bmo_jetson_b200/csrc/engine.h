@@ -1,0 +1,173 @@
+// engine.h -- device-side decode-step engine behind the C ABI.
+//
+// Owns the model in HBM (Q4_0 matrices repacked into row tiles, embedding
+// tables and norms as stored), the temporal KV ring, the depformer KV, the
+// activation buffers, and one CUDA graph per entry point:
+//   temporal      embed -> 32 x {QKV, attention, O, FFN-in, FFN-out} -> head
+//   depth[cb]     one depformer step (reference bmo_forward_depth)
+//   cascade       dep_q depformer steps with greedy argmax chaining on device
+//   frame         temporal + greedy text token + cascade
+// Kernels are chained with programmatic dependent launch inside each graph.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.h"
+#include "layout.h"
+
+namespace bmo {
+
+constexpr int kDepQMax = 8;
+constexpr int kDepLayers = 6;
+constexpr int kMaxTokens = 64;
+
+struct EngineConfig {
+    int device = -1;   // < 0: BMO_DEVICE or current device
+    int n_ctx = 0;     // <= 0: 2048
+    int kv_type = -1;  // < 0: BMO_KV_TYPE or fp16
+    bool graphs = true;
+    bool pdl = true;
+};
+
+// Per-call inputs, copied to the device in one transfer.
+struct FrameIn {
+    int32_t tokens[kMaxTokens];
+    int32_t n_tok;
+    int32_t pos;
+    int32_t prev_token;
+    int32_t pad;
+};
+
+class Engine {
+public:
+    Engine(const std::string &gguf_path, const EngineConfig &cfg);
+    ~Engine();
+    Engine(const Engine &) = delete;
+    Engine &operator=(const Engine &) = delete;
+
+    // ---- geometry (reference names, src/bmo.h:263-291) ----
+    int n_layers = 0, n_embd = 0, n_heads = 0, head_dim = 0, n_kv_heads = 0, ffn = 0;
+    int n_ctx = 0, kv_type = kKvF16, n_q = 0, num_codebooks = 0, dep_q = 0;
+    int text_vocab = 0, audio_vocab = 0;
+    float rope_theta = 10000.0f, norm_eps = 1e-8f;
+    int dep_dim = 0, dep_heads = 16, dep_hd = 0, dep_ffn = 0, dep_n_ctx = 0;
+    bool has_text_head = false;
+    bool has_dep_head[kDepQMax] = {};
+    bool has_dep_tables = false;
+    int device = 0, sm_count = 148;
+    cudaStream_t stream = nullptr;
+    size_t device_bytes = 0;
+
+    // ---- synchronous operations (caller serialises) ----
+    void run_temporal(const int32_t *tokens, int K, int pos);
+    const float *z_host() const { return z_h_; }
+    const float *logits_host() const { return logits_h_; }
+    void copy_resid(int layer, float *out);  // post-layer residual of the last temporal step
+    void run_layers(const float *x_in, int pos, int layer_begin, int layer_end, float *x_out);
+    void run_depth(int cb, int32_t prev, const float *z);
+    const float *depth_logits_host() const { return dlogits_h_; }
+    void run_cascade_greedy(int32_t text_tok, const float *z, int32_t *out_tokens);
+    void run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *out_text_tok, int32_t *out_audio);
+    void enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev);
+    int sync_status();
+    void reset_kv();
+    void reset_depth_kv();
+    int kv_import(int layer, int slot0, int n, const float *k_rows, const float *v_rows);
+    int copy_cache_f32(int which, int layer, int t_start, int n_positions, float *out);
+    long long copy_kv_raw(int which, int part, int layer, void *out, long long max_bytes);
+    void capture_all();
+    bool graphs_captured() const { return graphs_ready_; }
+
+private:
+    struct Layer {
+        QMatDesc qkv, wo, ffn_in, ffn_out;
+        float *norm1 = nullptr, *norm2 = nullptr;
+    };
+    struct DepLayer {
+        QMatDesc qkv[kDepQMax], wo[kDepQMax], ffn_in[kDepQMax], ffn_out[kDepQMax];
+        float *norm1 = nullptr, *norm2 = nullptr;
+    };
+
+    void load(const std::string &path);
+    void alloc_state();
+    void *arena(size_t bytes);
+    QMatDesc upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t row0, int64_t rows);
+    float *upload_f32(const GgufTensor *t, int64_t n);
+    EmbTable upload_table(const GgufTensor *t);
+    int gemv_grid(const QMatDesc &m) const;
+    GemvArgs gemv_base(const QMatDesc &m) const;
+    void gemv(const GemvArgs &a, int pro, int epi, cudaStream_t s);
+
+    void enqueue_temporal(cudaStream_t s);
+    void enqueue_layer(cudaStream_t s, int l);
+    void enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok);
+    void enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first);
+    void enqueue_finalize_tokens(cudaStream_t s);
+    cudaGraphExec_t capture(const std::function<void(cudaStream_t)> &fn);
+    void launch(cudaGraphExec_t &g, const std::function<void(cudaStream_t)> &fn);
+    void finish_call();
+
+    EngineConfig cfg_;
+    GgufFile file_;
+    std::vector<void *> allocs_;
+    uint8_t *arena_ = nullptr;
+    size_t arena_size_ = 0, arena_used_ = 0;
+    uint8_t *staging_d_ = nullptr;
+    size_t staging_bytes_ = 0;
+
+    // weights
+    std::vector<Layer> L_;
+    QMatDesc text_head_{};
+    float *text_bias_ = nullptr, *out_norm_ = nullptr;
+    QMatDesc dep_in_[kDepQMax] = {}, dep_head_[kDepQMax] = {};
+    DepLayer D_[kDepLayers];
+    EmbTable *ttables_d_ = nullptr;
+    int n_ttables_ = 0;
+    EmbTable dep_text_emb_{}, dep_emb_[kDepQMax] = {};
+
+    // temporal state and activations
+    void *k_cache_ = nullptr, *v_cache_ = nullptr;
+    uint8_t *k_scale_ = nullptr, *v_scale_ = nullptr;
+    size_t kv_plane_bytes_ = 0, kv_scale_bytes_ = 0;
+    float *resid_ = nullptr, *xmid_ = nullptr, *q_ = nullptr, *vraw_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
+    float *z_ = nullptr, *logits_ = nullptr;
+    float2 *rope_ = nullptr, *tpairs_ = nullptr;
+    // depformer state and activations
+    __half *dk_cache_ = nullptr, *dv_cache_ = nullptr;
+    size_t dkv_bytes_ = 0;
+    float *dz_ = nullptr, *dxa_ = nullptr, *dxb_ = nullptr, *dq_ = nullptr, *dvraw_ = nullptr, *dattn_ = nullptr;
+    float *dact_ = nullptr, *dlogits_ = nullptr;
+    float2 *dpairs_ = nullptr;
+    int dpairs_stride_ = 0;
+    int *dep_pos_ = nullptr;
+    int *tok_out_ = nullptr;  // [1 + kDepQMax]: text token, audio tokens
+    // scratch
+    float *gpart_ = nullptr;
+    int *gcount_ = nullptr;
+    size_t gpart_bytes_ = 0, gcount_bytes_ = 0;
+    float *apart_ = nullptr;
+    int *acount_ = nullptr;
+    size_t apart_bytes_ = 0, acount_bytes_ = 0;
+    int attn_splits_ = 1;
+    int *status_ = nullptr;
+    FrameIn *fin_d_ = nullptr;
+
+    // pinned host staging
+    FrameIn *fin_h_ = nullptr;
+    float *z_h_ = nullptr, *logits_h_ = nullptr, *zin_h_ = nullptr, *dlogits_h_ = nullptr;
+    int *tok_h_ = nullptr, *status_h_ = nullptr;
+
+    // graphs
+    cudaGraphExec_t g_temporal_ = nullptr, g_depth_[kDepQMax] = {}, g_cascade_ = nullptr, g_frame_ = nullptr;
+    cudaGraphExec_t g_layers_ = nullptr;
+    int g_layers_range_[2] = {-1, -1};
+    bool graphs_ready_ = false;
+};
+
+}  // namespace bmo

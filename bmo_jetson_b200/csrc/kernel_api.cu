@@ -1,0 +1,172 @@
+// kernel_api.cu -- the device-pointer kernel layer (include/bmo_kernels.h).
+#include <climits>
+
+#include "../../include/bmo_kernels.h"
+#include "kernels/common.cuh"
+#include "launch.h"
+
+namespace bmo {
+namespace {
+
+QMatDesc make_desc(const void *tiles, int rows, int cols, int perm, int swiglu_f) {
+    QMatDesc m{};
+    m.tiles = static_cast<const uint8_t *>(tiles);
+    m.rows = perm == kPermSwiGLU ? 2 * swiglu_f : rows;
+    m.cols = cols;
+    m.nbx = ((cols / 32) + kChunkBlocks - 1) / kChunkBlocks * kChunkBlocks;
+    m.cpt = m.nbx / kChunkBlocks;
+    m.perm = perm;
+    m.swiglu_f = swiglu_f;
+    m.n_tiles = perm == kPermSwiGLU ? swiglu_f / 16 : (rows + kTileRows - 1) / kTileRows;
+    return m;
+}
+
+bool shape_ok(int rows, int cols, int perm, int swiglu_f) {
+    if (cols <= 0 || cols % 32) return false;
+    if (perm == kPermSwiGLU) return swiglu_f > 0 && swiglu_f % 16 == 0 && rows == 2 * swiglu_f;
+    return perm == kPermIdentity && rows > 0;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Appends one token's K and V (fp32 [n_kv][hd]) at ring slot pos % n_ctx:
+// one warp per 32-element block, fp16 rows or Q4_0 blocks (the same
+// conversions as the QKV epilogue of the GEMV).
+__global__ void kv_append_kernel(const float *k, const float *v, void *k_cache, void *v_cache, uint8_t *k_scale,
+                                 uint8_t *v_scale, int n_kv, int hd, int n_ctx, const int *pos, long long layer_off,
+                                 int kv_type) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int blocks = n_kv * hd / 32;
+    if (warp >= 2 * blocks) return;
+    const bool is_v = warp >= blocks;
+    const int b = is_v ? warp - blocks : warp;
+    const int kh = (b * 32) / hd, d = (b * 32) % hd + lane;
+    const float x = (is_v ? v : k)[kh * hd + d];
+    const int slot = *pos % n_ctx;
+    const long long e = layer_off + (static_cast<long long>(kh) * n_ctx + slot) * hd + d;
+    void *cache = is_v ? v_cache : k_cache;
+    if (kv_type == kKvF16) {
+        static_cast<__half *>(cache)[e] = __float2half_rn(x);
+    } else {
+        const long long e0 = e - lane;
+        warp_store_q4_0(x, lane, static_cast<uint8_t *>(cache) + e0 / 2,
+                        reinterpret_cast<__half *>(is_v ? v_scale : k_scale) + e0 / 32);
+    }
+}
+
+}  // namespace
+}  // namespace bmo
+
+using namespace bmo;
+
+extern "C" {
+
+int bmo_k_quantize_q8_1(const float *x_dev, void *out_dev, int n, void *stream) {
+    if (!x_dev || !out_dev || n < 0 || n % 32) return static_cast<int>(cudaErrorInvalidValue);
+    return static_cast<int>(launch_quantize_q8_1(x_dev, out_dev, n, static_cast<cudaStream_t>(stream)));
+}
+
+size_t bmo_k_q4_0_tiled_bytes(int rows, int cols, int perm, int swiglu_f) {
+    if (!shape_ok(rows, cols, perm, swiglu_f)) return 0;
+    const QMatDesc m = make_desc(nullptr, rows, cols, perm, swiglu_f);
+    return static_cast<size_t>(m.n_tiles) * m.cpt * kChunkBytes;
+}
+
+int bmo_k_repack_q4_0(const void *ggml_dev, void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                      void *stream) {
+    if (!ggml_dev || !tiled_dev || !shape_ok(rows, cols, perm, swiglu_f)) return static_cast<int>(cudaErrorInvalidValue);
+    const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
+    return static_cast<int>(launch_repack_q4_0(ggml_dev, tiled_dev, rows, cols, m, static_cast<cudaStream_t>(stream)));
+}
+
+size_t bmo_k_gemv_scratch_bytes(int rows, int cols, int perm, int swiglu_f) {
+    if (!shape_ok(rows, cols, perm, swiglu_f)) return 0;
+    const QMatDesc m = make_desc(nullptr, rows, cols, perm, swiglu_f);
+    return align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float)) +
+           align256(static_cast<size_t>(m.n_tiles) * sizeof(int)) + 256;
+}
+
+int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
+                    const float *gamma_dev, float eps, const float *resid_dev, float *y_dev, void *q8_out_dev,
+                    float *xn_out_dev, void *scratch_dev, size_t scratch_bytes, int grid, void *stream) {
+    if (!tiled_dev || !x_dev || !y_dev || !scratch_dev || !shape_ok(rows, cols, perm, swiglu_f))
+        return static_cast<int>(cudaErrorInvalidValue);
+    if (scratch_bytes < bmo_k_gemv_scratch_bytes(rows, cols, perm, swiglu_f)) return static_cast<int>(cudaErrorInvalidValue);
+    if (cols / 32 > gemv_max_nbx() * kChunkBlocks) return static_cast<int>(cudaErrorInvalidValue);
+    const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
+    GemvArgs a{};
+    a.W = m;
+    a.x = x_dev;
+    a.gamma = gamma_dev;
+    a.eps = eps;
+    a.xn_out = xn_out_dev;
+    a.q8_out = static_cast<uint8_t *>(q8_out_dev);
+    a.y = y_dev;
+    a.resid = resid_dev;
+    a.argmax_limit = INT_MAX;
+    uint8_t *s = static_cast<uint8_t *>(scratch_dev);
+    a.gpart = reinterpret_cast<float *>(s);
+    a.gcount = reinterpret_cast<int *>(s + align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float)));
+    a.status = a.gcount + m.n_tiles;  // last word of the scratch block
+    const long long nc = static_cast<long long>(m.n_tiles) * m.cpt;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    long long g = grid > 0 ? grid : (nc < sms ? nc : sms);
+    const long long need = (m.n_tiles + gemv_max_tiles_per_cta() - 3) / (gemv_max_tiles_per_cta() - 2);
+    if (g < need) g = need < nc ? need : nc;
+    if (g > nc) g = nc;
+    const int pro = gamma_dev ? kProNorm : kProPlain;
+    const int epi = perm == kPermSwiGLU ? kEpiSwiGLU : (resid_dev ? kEpiResid : kEpiStore);
+    return static_cast<int>(launch_gemv(a, pro, epi, static_cast<int>(g), static_cast<cudaStream_t>(stream), false));
+}
+
+size_t bmo_k_attention_scratch_bytes(int n_heads, int head_dim, int n_ctx) {
+    const int splits = (n_ctx + attn_max_per_split() - 1) / attn_max_per_split();
+    return align256(static_cast<size_t>(n_heads) * splits * (head_dim + 2) * sizeof(float)) +
+           align256(static_cast<size_t>(n_heads) * sizeof(int)) + 256;
+}
+
+int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
+                           void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev, int head_dim,
+                           int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev, int layer, int kv_type,
+                           void *scratch_dev, size_t scratch_bytes, void *stream) {
+    if (!q_dev || !k_dev || !v_dev || !k_cache_dev || !v_cache_dev || !out_dev || !pos_dev || !scratch_dev)
+        return static_cast<int>(cudaErrorInvalidValue);
+    if ((head_dim != 64 && head_dim != 128) || n_kv_heads <= 0 || n_heads % n_kv_heads || n_ctx <= 0 || layer < 0)
+        return static_cast<int>(cudaErrorInvalidValue);
+    if (kv_type == kKvQ4_0 && (!k_scale_dev || !v_scale_dev)) return static_cast<int>(cudaErrorInvalidValue);
+    if (scratch_bytes < bmo_k_attention_scratch_bytes(n_heads, head_dim, n_ctx)) return static_cast<int>(cudaErrorInvalidValue);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const long long layer_off = static_cast<long long>(layer) * n_kv_heads * n_ctx * head_dim;
+    const int warps = 2 * n_kv_heads * head_dim / 32;
+    kv_append_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(
+        k_dev, v_dev, k_cache_dev, v_cache_dev, static_cast<uint8_t *>(k_scale_dev), static_cast<uint8_t *>(v_scale_dev),
+        n_kv_heads, head_dim, n_ctx, pos_dev, layer_off, kv_type);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int splits = (n_ctx + attn_max_per_split() - 1) / attn_max_per_split();
+    uint8_t *sc = static_cast<uint8_t *>(scratch_dev);
+    AttnArgs a{};
+    a.q = q_dev;
+    a.v_raw = v_dev;
+    a.k_cache = k_cache_dev;
+    a.v_cache = v_cache_dev;
+    a.k_scale = static_cast<const uint8_t *>(k_scale_dev);
+    a.v_scale = static_cast<const uint8_t *>(v_scale_dev);
+    a.kv_layer_off = layer_off;
+    a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.n_ctx = n_ctx;
+    a.kv_type = kv_type;
+    a.pos = pos_dev;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.out = out_dev;
+    a.part = reinterpret_cast<float *>(sc);
+    a.count = reinterpret_cast<int *>(sc + align256(static_cast<size_t>(n_heads) * splits * (head_dim + 2) * sizeof(float)));
+    a.status = a.count + n_heads;
+    return static_cast<int>(launch_attention(a, head_dim, splits, s, false));
+}
+
+}  // extern "C"

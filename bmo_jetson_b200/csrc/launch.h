@@ -1,0 +1,33 @@
+// launch.h -- host-side launchers of the sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "layout.h"
+
+namespace bmo {
+
+// GEMV (kernels/gemv_q4.cu).  `grid` CTAs split the (tile, chunk) units;
+// `pdl` enables programmatic dependent launch on the stream.
+cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl);
+size_t gemv_smem_bytes();
+int gemv_max_tiles_per_cta();
+int gemv_max_nbx();
+
+// Ring decode attention (kernels/attention.cu), grid (heads, splits).
+cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl);
+int attn_max_per_split();
+
+// Frame-start embedding sum + RoPE table (kernels/misc.cu).
+cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,
+                         float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, cudaStream_t s);
+cudaError_t launch_set_frame(int *fin_tokens, int *fin_n_tok, int *fin_pos, const int *tokens, int K, int pos,
+                             cudaStream_t s);
+cudaError_t launch_finalize_token(const float2 *pairs, int n, int *out, cudaStream_t s, bool pdl);
+// Sets the shared-memory opt-in of every kernel variant on the current device.
+cudaError_t configure_kernels();
+cudaError_t launch_repack_q4_0(const void *src, void *dst, int rows, int cols, const QMatDesc &m, cudaStream_t s);
+cudaError_t launch_quantize_q8_1(const float *x, void *out, int n, cudaStream_t s);
+
+}  // namespace bmo

@@ -1,0 +1,124 @@
+// layout.h -- HBM layouts and kernel argument blocks shared by host and device.
+//
+// Q4_0 weights are repacked at load time from ggml's row-major 18-byte blocks
+// (fp16 d + 16 bytes of nibbles) into "row tiles": 32 rows x all blocks,
+// cut into chunks of 8 blocks.  One chunk is 4608 contiguous bytes:
+//   [8 blocks][32 rows][16 B nibbles]  (4096 B, row r's block at blk*512 + r*16)
+//   [8 blocks][32 rows][fp16 d]        (512 B)
+// so a warp reads one block of 32 rows as a single 512-byte coalesced line,
+// the activation block is a shared-memory broadcast, and every chunk is a
+// 16-byte aligned bulk copy.  The bytes per weight are unchanged (18 per 32).
+#pragma once
+
+#include <stdint.h>
+
+namespace bmo {
+
+constexpr int kTileRows = 32;
+constexpr int kChunkBlocks = 8;
+constexpr int kChunkQsBytes = kChunkBlocks * kTileRows * 16;   // 4096
+constexpr int kChunkBytes = kChunkQsBytes + kChunkBlocks * kTileRows * 2;  // 4608
+
+// Row order inside a tile.
+enum RowPerm : int {
+    kPermIdentity = 0,  // lane l of tile t is row 32t + l
+    kPermSwiGLU = 1,    // lanes 0-15 gate rows 16t+l, lanes 16-31 up rows F+16t+l-16
+};
+
+// Prologue: how the GEMV input vector reaches shared memory as Q8_1 blocks.
+enum Prologue : int {
+    kProPlain = 0,  // quantise fp32 x
+    kProNorm = 1,   // RMSNorm(x) * gamma, then quantise
+};
+
+// Epilogue: what happens to the finished dot products of a tile.
+enum Epilogue : int {
+    kEpiStore = 0,   // y = acc (+ bias)
+    kEpiResid = 1,   // y = resid + acc
+    kEpiSwiGLU = 2,  // act = silu(gate) * up
+    kEpiQKV = 3,     // RoPE on q/k, append k/v into the ring cache, q out
+    kEpiLogits = 4,  // logits (+ bias) and per-tile (max, argmax)
+    kEpiEmbAdd = 5,  // y = acc + embedding row of a token
+};
+
+enum KvType : int { kKvF16 = 0, kKvQ4_0 = 1 };
+
+// ggml tensor element types used by embedding tables.
+enum GgmlType : int { kTF32 = 0, kTF16 = 1, kTQ4_0 = 2, kTQ8_0 = 8, kTI32 = 26, kTBF16 = 30 };
+
+struct QMatDesc {
+    const uint8_t *tiles;  // device, n_tiles * cpt * kChunkBytes
+    int rows;              // logical rows
+    int cols;              // logical cols (multiple of 32)
+    int nbx;               // blocks per row incl. padding (multiple of 8)
+    int cpt;               // chunks per tile = nbx / 8
+    int n_tiles;
+    int perm;
+    int swiglu_f;          // F for kPermSwiGLU
+};
+
+// Source of a token id for an embedding lookup: either a device int, or the
+// reduction of per-tile (max, argmax) pairs left by a logits epilogue.
+struct TokenSrc {
+    const int *tok;        // used when pairs == nullptr
+    const float2 *pairs;   // (value, index-as-float bits) per tile
+    int n_pairs;
+    int *tok_out;          // optional: resolved token written here (one thread)
+};
+
+struct EmbTable {
+    const void *data;
+    int type;              // GgmlType
+    int rows;              // vocabulary rows
+    int dim;               // row length
+    long long row_bytes;
+};
+
+struct GemvArgs {
+    QMatDesc W;
+    // prologue
+    const float *x;
+    const float *gamma;
+    float eps;
+    float *xn_out;         // optional: CTA 0 writes the normalised vector
+    uint8_t *q8_out;       // optional: CTA 0 writes the Q8_1 blocks (36 B each)
+    // epilogue
+    float *y;
+    const float *resid;
+    const float *bias;
+    float2 *argmax_pairs;
+    int argmax_limit;      // rows >= limit excluded from the argmax
+    // qkv epilogue
+    int q_dim, kv_dim, head_dim;
+    const float2 *rope_cs; // [head_dim/2] (cos, sin) for this position, or null (no RoPE)
+    void *k_cache, *v_cache;        // fp16 or Q4_0 planes
+    uint8_t *k_scale, *v_scale;     // Q4_0 fp16 scale planes
+    int kv_type, n_ctx;
+    const int *pos;        // device position (slot = pos % n_ctx)
+    long long kv_layer_off;  // element offset of this layer in the cache planes
+    float *v_out;          // raw fp32 v (window-of-one case)
+    // embedding-add epilogue
+    EmbTable emb;
+    TokenSrc tok;
+    // stream-K bookkeeping
+    float *gpart;          // [n_tiles][cpt+1][32]
+    int *gcount;           // [n_tiles], zero between launches
+    int *status;
+};
+
+struct AttnArgs {
+    const float *q;          // [n_heads][hd] rotated queries
+    const float *v_raw;      // [n_kv][hd] fp32 v of this token
+    const void *k_cache, *v_cache;
+    const uint8_t *k_scale, *v_scale;
+    long long kv_layer_off;  // element offset of this layer
+    int n_heads, n_kv_heads, n_ctx, kv_type;
+    const int *pos;
+    float scale;
+    float *out;              // [n_heads][hd]
+    float *part;             // [n_heads][splits][hd + 2]
+    int *count;              // [n_heads]
+    int *status;
+};
+
+}  // namespace bmo

@@ -1,0 +1,91 @@
+/*
+ * bmo_ext.h -- extensions of libbmo.so beyond the reference C ABI.
+ *
+ * None of these has a counterpart in utkarshyadav009/bmo_jetson; the
+ * reference entry points in bmo_api.h are unchanged by them.
+ */
+#ifndef BMO_EXT_H
+#define BMO_EXT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bmo_api.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { BMO_KV_F16 = 0, BMO_KV_Q4_0 = 1 };
+
+/* Flags of bmo_init_ex. */
+enum {
+    BMO_FLAG_NO_GRAPHS = 1, /* launch kernels eagerly instead of replaying CUDA graphs */
+    BMO_FLAG_NO_PDL = 2,    /* no programmatic dependent launch between kernels */
+};
+
+/* bmo_init with an explicit CUDA device, KV ring format and flags.
+ * device < 0 selects BMO_DEVICE or the current device. */
+BMO_API bmo_handle_t *bmo_init_ex(const char *gguf_path, int n_ctx, int device, int kv_type, int flags);
+
+BMO_API int bmo_get_kv_type(bmo_handle_t *h);
+BMO_API int bmo_get_n_ctx(bmo_handle_t *h);
+BMO_API int bmo_get_n_kv_heads(bmo_handle_t *h);
+BMO_API int bmo_get_device(bmo_handle_t *h);
+BMO_API int bmo_get_pos(bmo_handle_t *h);
+/* CUDA stream (cudaStream_t) the handle launches on. */
+BMO_API void *bmo_get_stream(bmo_handle_t *h);
+/* Bytes of device memory the handle holds (weights, KV, buffers). */
+BMO_API size_t bmo_get_device_bytes(bmo_handle_t *h);
+
+/* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
+ * slots [slot0, slot0+n) of temporal layer `layer`; rows are
+ * [n][n_kv_heads * head_dim].  Converts to the ring format (fp16 or Q4_0).
+ * Returns 0, or 2 for a bad range. */
+BMO_API int bmo_kv_import_f32(bmo_handle_t *h, int layer, int slot0, int n, const float *k_rows,
+                              const float *v_rows);
+/* Same contract as bmo_copy_k_cache_f32 for the V ring. */
+BMO_API int bmo_copy_v_cache_f32(bmo_handle_t *h, int layer, int t_start, int n_positions, float *out,
+                                 int max_floats);
+/* Raw ring bytes of one layer: which 0 = K, 1 = V; for Q4_0 rings part 0 is
+ * the nibble plane and part 1 the fp16 scale plane. Returns bytes copied. */
+BMO_API long long bmo_copy_kv_raw(bmo_handle_t *h, int which, int part, int layer, void *out, long long max_bytes);
+
+/* One whole frame in a single graph: temporal step at `pos`, greedy text
+ * token (argmax over the text logits), then the greedy depformer cascade
+ * from that token.  Any output pointer may be NULL. */
+BMO_API int bmo_forward_frame_greedy(bmo_handle_t *h, const int32_t *input_tokens, int num_codebooks, int pos,
+                                     float *out_transformer, float *out_text_logits, int32_t *out_text_token,
+                                     int32_t *out_audio_tokens);
+
+/* Temporal layers [layer_begin, layer_end) on an fp32 hidden vector at
+ * absolute position pos (no embedding, no final norm or head), as the
+ * reference harness's per-layer cascade mode drives them.  Appends K/V of
+ * those layers to the ring like a full step.  Returns 0, 1 null, 2 range. */
+BMO_API int bmo_forward_layers(bmo_handle_t *h, const float *x_in, int pos, int layer_begin, int layer_end,
+                               float *x_out);
+
+/* Asynchronous device-resident frame: tokens_dev (device int32[num_codebooks])
+ * are copied on the device, the frame graph is enqueued on the handle's
+ * stream, and the text token + dep_q audio tokens land in out_tokens_dev
+ * (device int32[1 + dep_q]).  No host synchronisation. */
+BMO_API int bmo_enqueue_frame(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos,
+                              int32_t *out_tokens_dev);
+/* Waits for the handle's stream; returns the device status word (0 = ok). */
+BMO_API int bmo_sync(bmo_handle_t *h);
+
+/* Deterministic synthetic data for benchmark models (counter-based RNG,
+ * Box-Muller normals).  q4_0 quantises rows of N(0, sigma) with ggml's
+ * reference Q4_0 rule; f16/f32 fill N(mean, sigma). */
+BMO_API void bmo_synth_normal_f32(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, float *out);
+BMO_API void bmo_synth_f16(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, uint16_t *out);
+BMO_API void bmo_synth_q4_0(uint64_t seed, uint64_t stream, long long rows, long long cols, float sigma,
+                            uint8_t *out);
+/* ggml Q4_0 reference quantiser (18-byte blocks) over n floats. */
+BMO_API void bmo_quantize_q4_0_ref(const float *x, long long n, uint8_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BMO_EXT_H */

@@ -1,0 +1,68 @@
+/*
+ * bmo_kernels.h -- device-pointer kernel layer of libbmo.so.
+ *
+ * The counterpart of the reference's launch_* functions (utkarshyadav009/
+ * bmo_jetson src/bmo.h:348-445): each call takes device buffers and a
+ * cudaStream_t (as void*), launches the sm_100a kernels that the decode step
+ * uses, and returns 0 or a CUDA error code.  Callers own every buffer,
+ * including the scratch the split kernels need (size from the *_scratch_bytes
+ * queries).  Calls are asynchronous on `stream`.
+ */
+#ifndef BMO_KERNELS_H
+#define BMO_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bmo_api.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { BMO_PERM_IDENTITY = 0, BMO_PERM_SWIGLU = 1 };
+
+/* Q8_1 quantisation of n floats (n % 32 == 0) into 36-byte blocks
+ * (fp16 d, fp16 sum, 32 int8).  Replaces bmo_quantize_row_q8_1_kernel as
+ * launched by launch_gemv_q4_0_q8_1 (bmo_cuda_kernels.cu:685-699). */
+BMO_API int bmo_k_quantize_q8_1(const float *x_dev, void *out_dev, int n, void *stream);
+
+/* Bytes of the tiled layout of a rows x cols Q4_0 matrix. */
+BMO_API size_t bmo_k_q4_0_tiled_bytes(int rows, int cols, int perm, int swiglu_f);
+/* ggml Q4_0 row-major blocks -> tiled layout (done once at model load). */
+BMO_API int bmo_k_repack_q4_0(const void *ggml_dev, void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                              void *stream);
+
+/* Scratch bytes bmo_k_gemv_q4_0 needs for a rows x cols matrix. */
+BMO_API size_t bmo_k_gemv_scratch_bytes(int rows, int cols, int perm, int swiglu_f);
+/* y = W x with the reference's Q4_0 x Q8_1 arithmetic (replaces
+ * launch_gemv_q4_0_q8_1, bmo.h:405-412).  W is the tiled layout.
+ * gamma_dev != NULL: x is RMS-normalised and scaled by gamma first (fused
+ * launch_rmsnorm, bmo.h:358-364).  perm == SWIGLU: y receives
+ * silu(gate) * up of length swiglu_f (fused launch_swiglu_split).
+ * resid_dev != NULL: y = resid + W x (fused launch_residual_add).
+ * q8_out_dev / xn_out_dev (optional) receive the Q8_1 blocks and the
+ * normalised fp32 vector the kernel used.  scratch_dev must be zero on the
+ * first call and is left zero by every call that returns 0. */
+BMO_API int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                            const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
+                            float *y_dev, void *q8_out_dev, float *xn_out_dev, void *scratch_dev,
+                            size_t scratch_bytes, int grid, void *stream);
+
+/* Scratch bytes bmo_k_decode_attention needs. */
+BMO_API size_t bmo_k_attention_scratch_bytes(int n_heads, int head_dim, int n_ctx);
+/* Appends k, v (fp32, [n_kv_heads][head_dim]) at ring slot pos % n_ctx of
+ * `layer`, then attends q over the window (replaces launch_decode_attention,
+ * bmo.h:414-428).  Caches are [n_layers][n_kv_heads][n_ctx][head_dim] in
+ * fp16 (kv_type 0) or Q4_0 nibble planes with fp16 scale planes (kv_type 1;
+ * *_scale_dev). pos_dev is a device int. */
+BMO_API int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
+                                   void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev,
+                                   int head_dim, int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev,
+                                   int layer, int kv_type, void *scratch_dev, size_t scratch_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BMO_KERNELS_H */

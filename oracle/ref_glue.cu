@@ -1,0 +1,130 @@
+// ref_glue.cu -- host-buffer C entry points around the reference's own CUDA
+// launchers (utkarshyadav009/bmo_jetson src/bmo_cuda_kernels.cu, compiled
+// unmodified next to this file). TEST INFRASTRUCTURE: used only to produce
+// golden vectors on a B200 that pin the CPU oracle, and to time the
+// reference kernels as a baseline. Each wrapper copies its inputs to the
+// device, calls one reference launcher on the default stream, and copies the
+// results back.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+
+// Launcher signatures, src/bmo.h:358-428.
+void launch_rmsnorm(const float *x_dev, const float *weight_dev, float eps, int n_embd, float *y_dev, void *stream);
+void launch_residual_add(const float *a_dev, const float *b_dev, int n, float *y_dev, void *stream);
+void launch_rope_interleaved(const float *x_dev, int n_heads, int head_dim, int n_token, int pos_base,
+                             float theta_base, float *y_dev, void *stream, const int *pos_dev);
+void launch_swiglu_split(const float *h_dev, int d_ff, float *y_dev, void *stream);
+void launch_gemv_q4_0_q8_1(const void *W_dev, const float *x_dev, float *y_dev, int rows, int cols,
+                           void *q8_scratch, void *stream);
+void launch_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
+                             void *v_cache_dev, float *out_dev, int head_dim, int n_heads, int n_kv_heads,
+                             int n_ctx, int n_past, int layer, void *stream, const int *pos_dev);
+
+namespace {
+struct dbuf {
+    void *p = nullptr;
+    explicit dbuf(size_t n) { cudaMalloc(&p, n ? n : 16); }
+    ~dbuf() { cudaFree(p); }
+    template <class T> T *as() const { return static_cast<T *>(p); }
+};
+int finish() {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+}  // namespace
+
+extern "C" {
+
+int ref_gemv_q4_0_q8_1(const void *W, const float *x, float *y, void *q8_out, int rows, int cols) {
+    const size_t wb = (size_t)rows * (cols / 32) * 18, qb = (size_t)(cols / 32) * 36;
+    dbuf dW(wb), dx((size_t)cols * 4), dy((size_t)rows * 4), dq(qb);
+    cudaMemcpy(dW.p, W, wb, cudaMemcpyHostToDevice);
+    cudaMemcpy(dx.p, x, (size_t)cols * 4, cudaMemcpyHostToDevice);
+    launch_gemv_q4_0_q8_1(dW.p, dx.as<float>(), dy.as<float>(), rows, cols, dq.p, nullptr);
+    int rc = finish();
+    cudaMemcpy(y, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost);
+    if (q8_out) cudaMemcpy(q8_out, dq.p, qb, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+int ref_rmsnorm(const float *x, const float *w, float eps, int n, float *y) {
+    dbuf dx((size_t)n * 4), dw((size_t)n * 4), dy((size_t)n * 4);
+    cudaMemcpy(dx.p, x, (size_t)n * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dw.p, w, (size_t)n * 4, cudaMemcpyHostToDevice);
+    launch_rmsnorm(dx.as<float>(), dw.as<float>(), eps, n, dy.as<float>(), nullptr);
+    int rc = finish();
+    cudaMemcpy(y, dy.p, (size_t)n * 4, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+int ref_rope(const float *x, int n_heads, int head_dim, int pos, float theta, float *y) {
+    const size_t n = (size_t)n_heads * head_dim * 4;
+    dbuf dx(n), dy(n);
+    cudaMemcpy(dx.p, x, n, cudaMemcpyHostToDevice);
+    launch_rope_interleaved(dx.as<float>(), n_heads, head_dim, 1, pos, theta, dy.as<float>(), nullptr, nullptr);
+    int rc = finish();
+    cudaMemcpy(y, dy.p, n, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+int ref_swiglu(const float *h, int d_ff, float *y) {
+    dbuf dh((size_t)d_ff * 8), dy((size_t)d_ff * 4);
+    cudaMemcpy(dh.p, h, (size_t)d_ff * 8, cudaMemcpyHostToDevice);
+    launch_swiglu_split(dh.as<float>(), d_ff, dy.as<float>(), nullptr);
+    int rc = finish();
+    cudaMemcpy(y, dy.p, (size_t)d_ff * 4, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+// k_cache / v_cache: fp16 [n_layers][n_heads][n_ctx][head_dim], updated in place.
+int ref_attention(const float *q, const float *k, const float *v, uint16_t *k_cache, uint16_t *v_cache,
+                  float *out, int head_dim, int n_heads, int n_kv_heads, int n_ctx, int pos, int layer,
+                  int n_layers) {
+    const size_t qn = (size_t)n_heads * head_dim * 4, kn = (size_t)n_kv_heads * head_dim * 4;
+    const size_t cn = (size_t)n_layers * n_heads * n_ctx * head_dim * 2;
+    dbuf dq(qn), dk(kn), dv(kn), dkc(cn), dvc(cn), dout(qn);
+    cudaMemcpy(dq.p, q, qn, cudaMemcpyHostToDevice);
+    cudaMemcpy(dk.p, k, kn, cudaMemcpyHostToDevice);
+    cudaMemcpy(dv.p, v, kn, cudaMemcpyHostToDevice);
+    cudaMemcpy(dkc.p, k_cache, cn, cudaMemcpyHostToDevice);
+    cudaMemcpy(dvc.p, v_cache, cn, cudaMemcpyHostToDevice);
+    launch_decode_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dkc.p, dvc.p, dout.as<float>(),
+                            head_dim, n_heads, n_kv_heads, n_ctx, pos, layer, nullptr, nullptr);
+    int rc = finish();
+    cudaMemcpy(out, dout.p, qn, cudaMemcpyDeviceToHost);
+    cudaMemcpy(k_cache, dkc.p, cn, cudaMemcpyDeviceToHost);
+    cudaMemcpy(v_cache, dvc.p, cn, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+// Times the reference Q8_1 quantise + GEMV pair on resident buffers: returns
+// the median of `iters` launches in microseconds (CUDA events, after warm-up).
+float ref_time_gemv(const void *W, const float *x, int rows, int cols, int warmup, int iters) {
+    const size_t wb = (size_t)rows * (cols / 32) * 18, qb = (size_t)(cols / 32) * 36;
+    dbuf dW(wb), dx((size_t)cols * 4), dy((size_t)rows * 4), dq(qb);
+    cudaMemcpy(dW.p, W, wb, cudaMemcpyHostToDevice);
+    cudaMemcpy(dx.p, x, (size_t)cols * 4, cudaMemcpyHostToDevice);
+    for (int i = 0; i < warmup; ++i)
+        launch_gemv_q4_0_q8_1(dW.p, dx.as<float>(), dy.as<float>(), rows, cols, dq.p, nullptr);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    float ts[1024];
+    if (iters > 1024) iters = 1024;
+    for (int i = 0; i < iters; ++i) {
+        cudaEventRecord(a);
+        launch_gemv_q4_0_q8_1(dW.p, dx.as<float>(), dy.as<float>(), rows, cols, dq.p, nullptr);
+        cudaEventRecord(b);
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&ts[i], a, b);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    for (int i = 1; i < iters; ++i)
+        for (int j = i; j > 0 && ts[j] < ts[j - 1]; --j) { float t = ts[j]; ts[j] = ts[j - 1]; ts[j - 1] = t; }
+    return finish() == 0 ? ts[iters / 2] * 1000.0f : -1.0f;
+}
+
+}  // extern "C"
