@@ -1,0 +1,438 @@
+"""Benchmark: Moshi decode frames/s at batch 1 on B200 (BASELINE configs 2 + 3).
+
+One step = one decode frame: the 32-layer temporal transformer (d 4096,
+32x128 heads, FFN 11264, Q4_0) at the next position, its 32000-way text head
+and greedy text token, then the 8-step depformer cascade (6 layers, d 1024,
+greedy audio tokens).  The 512-slot KV ring of every layer is pre-filled
+with 512 seeded prior positions and decoding starts at position 700, so the
+ring has wrapped.  Weights (4.1 GB) exceed L2 (126 MB), so every frame
+streams them from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`value`: frames/s with inputs resident in HBM (device token buffers, one
+CUDA graph per frame, CUDA events on the engine's stream, max over ranks).
+`e2e`: the same frames through the reference C ABI (bmo_forward_temporal +
+host argmax + bmo_forward_depth_cascade) with host buffers, wall clock.
+With N GPUs (torchrun), every rank runs its own session on its own GPU
+(data-parallel sessions, no collective): weak scaling.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_CTX = 512
+START_POS = 700
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_id(local: int) -> str:
+    """nvidia-smi id of CUDA device `local` (its UUID; CUDA and nvidia-smi
+    indices differ under CUDA_VISIBLE_DEVICES)."""
+    try:
+        import torch
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(local)
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world, local):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return dist
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def reduce_max(dist, v):
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([float(v)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prepare_model(rank, dist):
+    from bmo_jetson_b200 import synth
+    d = os.environ.get("BMO_MODEL_DIR") or os.path.join(os.environ.get("TMPDIR", "/tmp"), "bmo_models")
+    if rank == 0:
+        t0 = time.time()
+        path = synth.ensure_model("config2", d)
+        sys.stderr.write(f"[bench] model ready in {time.time() - t0:.1f}s: {path}\n")
+    barrier(dist)
+    return synth.ensure_model("config2", d)
+
+
+def frame_tokens(n, K, text_vocab, audio_vocab, seed=1):
+    rng = np.random.default_rng(seed)
+    t = np.empty((n, K), np.int32)
+    t[:, 0] = rng.integers(0, text_vocab, n)
+    t[:, 1:] = rng.integers(0, audio_vocab, (n, K - 1))
+    return t
+
+
+def fill_history(e, seed=7):
+    """512 seeded prior positions of N(0,1) K/V in every layer's ring."""
+    rng = np.random.default_rng(seed)
+    width = e.n_kv_heads * e.head_dim
+    for layer in range(e.n_layers):
+        k = rng.standard_normal((N_CTX, width), dtype=np.float32)
+        v = rng.standard_normal((N_CTX, width), dtype=np.float32)
+        e.kv_import(layer, 0, k, v)
+
+
+def frame_bytes(e):
+    """Algorithmic HBM bytes of one frame: Q4_0 weights streamed once, the KV
+    window read once, activations negligible."""
+    d, F, V = e.n_embd, 11264, e.text_vocab
+    q4 = lambda r, c: r * c // 32 * 18
+    per_layer = q4(3 * d, d) + q4(d, d) + q4(2 * F, d) + q4(d, F)
+    temporal = e.n_layers * per_layer + q4(V, d)
+    D, DF = 1024, 2816
+    dep_step = q4(D, d) + 6 * (q4(3 * D, D) + q4(D, D) + q4(2 * DF, D) + q4(D, DF)) + q4(2048, D)
+    kv_elem = 2 if e.kv_type == 0 else 18 / 32
+    kv = 2 * e.n_layers * e.n_kv_heads * N_CTX * e.head_dim * kv_elem
+    return temporal + 8 * dep_step + kv, temporal, 8 * dep_step, kv
+
+
+def gemv_roofline(local, peak_gbs, iters=40):
+    """Times the dominant kernel (Q4_0 GEMV, FFN-in shape 22528x4096 with the
+    fused RMSNorm + SwiGLU) on resident buffers: 8 distinct weight copies
+    (415 MB > L2) rotated per launch, CUDA events on the launching stream."""
+    import torch
+    from bmo_jetson_b200 import engine
+    L = engine.lib()
+    rows, cols, F = 22528, 4096, 11264
+    dev = torch.device("cuda", local)
+    s = torch.cuda.current_stream(dev)
+    nbytes = L.bmo_k_q4_0_tiled_bytes(rows, cols, 1, F)
+    mats = [torch.randint(0, 255, (nbytes,), dtype=torch.uint8, device=dev) for _ in range(8)]
+    for m in mats:  # sane fp16 scales: 0x2000 ~ 0.0078
+        m.view(-1, 4608)[:, 4096:].fill_(0x20)
+    x = torch.randn(cols, device=dev)
+    g = torch.ones(cols, device=dev)
+    y = torch.empty(F, device=dev)
+    sb = L.bmo_k_gemv_scratch_bytes(rows, cols, 1, F)
+    scratch = torch.zeros(sb, dtype=torch.uint8, device=dev)
+
+    def launch(i):
+        rc = L.bmo_k_gemv_q4_0(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8, None,
+                               y.data_ptr(), None, None, scratch.data_ptr(), sb, 0, s.cuda_stream)
+        assert rc == 0, rc
+
+    for i in range(8):
+        launch(i)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(iters):
+        launch(i)
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / iters
+    alg = rows * cols // 32 * 18 + cols * 4 * 2 + F * 4
+    achieved = alg / (ms * 1e-3) / 1e9
+    return {"kernel": "gemv_q4_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0, fused RMSNorm+Q8_1, SwiGLU)",
+            "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": achieved}
+
+
+def traffic_from_profile():
+    p = os.path.join(ROOT, "profiles", "gemv_ffn_in_traffic.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+def cpu_baseline(model_path, n_frames=2):
+    """The CPU oracle (C restatement of the reference arithmetic, OpenMP on
+    all host threads) on `n_frames` full frames of the same workload."""
+    from oracle import oracle as orc
+    o = orc.OracleModel(model_path, n_ctx=N_CTX)
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    width = o.n_kv_heads * o.head_dim
+    for layer in range(o.n_layers):
+        o.kv_import(layer, 0, rng.standard_normal((N_CTX, width), dtype=np.float32),
+                    rng.standard_normal((N_CTX, width), dtype=np.float32))
+    toks = frame_tokens(n_frames + 1, o.n_codebooks, o.text_vocab, o.audio_vocab)
+    z, lg, _ = o.forward_temporal(toks[0], START_POS)  # page in the weights
+    t0 = time.perf_counter()
+    for i in range(n_frames):
+        z, lg, _ = o.forward_temporal(toks[i + 1], START_POS + 1 + i)
+        o.depth_cascade_greedy(int(np.argmax(lg)), z)
+    dt = time.perf_counter() - t0
+    o.close()
+    return {"value": n_frames / dt, "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"{n_frames} full frames (32-layer temporal + text head + 8-step depformer) of the same "
+                      f"model at pos {START_POS + 1}.., oracle in C with OpenMP"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU arithmetic (oracle port) on the host cores."""
+    if rank != 0:
+        return 0
+    path = prepare_model(0, None)
+    from oracle import oracle as orc
+    o = orc.OracleModel(path, n_ctx=N_CTX)
+    rng = np.random.default_rng(7)
+    width = o.n_kv_heads * o.head_dim
+    for layer in range(o.n_layers):
+        o.kv_import(layer, 0, rng.standard_normal((N_CTX, width), dtype=np.float32),
+                    rng.standard_normal((N_CTX, width), dtype=np.float32))
+    toks = frame_tokens(args.warmup + args.steps, o.n_codebooks, o.text_vocab, o.audio_vocab)
+    pos = START_POS
+    for i in range(args.warmup):
+        z, lg, _ = o.forward_temporal(toks[i], pos)
+        o.depth_cascade_greedy(int(np.argmax(lg)), z)
+        pos += 1
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        z, lg, _ = o.forward_temporal(toks[args.warmup + i], pos)
+        o.depth_cascade_greedy(int(np.argmax(lg)), z)
+        pos += 1
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = os.cpu_count() or 1
+    line = {"metric": "Moshi decode frames/s (B=1)", "value": v, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
+            "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales)",
+            "data": "synthetic: seeded N(0,0.02) Q4_0 weights, N(0,1) f16 embeddings, seeded tokens and KV history",
+            "config": {"workload": "config2+3: 32-layer temporal (d4096) + text head + 8-step depformer frame, B=1",
+                       "n_ctx": N_CTX, "start_pos": START_POS, "kv": "f16"},
+            "cpu_baseline": {"value": v, "unit": "frames/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} full frames after {args.warmup} warm-up frames; the reference's "
+                                       "ggml CPU path cannot be built here (llama.cpp not vendored), so this is the "
+                                       "C restatement of its arithmetic (oracle/) with OpenMP"},
+            "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    o.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kv", default="f16", choices=["f16", "q4_0"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true", help="only the standalone GEMV timing (profiling)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 0)
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    peak, peak_kind = measured_peaks()
+    if args.kernel_only:
+        torch.cuda.set_device(local)
+        r = gemv_roofline(local, peak, iters=max(args.steps, 1))
+        print(json.dumps(r), flush=True)
+        return 0
+
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    path = prepare_model(rank, dist)
+    from bmo_jetson_b200 import engine
+    kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
+    e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type)
+    fill_history(e)
+    assert e.capture_graphs() == 0
+    K = e.n_codebooks
+    n_frames = args.warmup + args.steps
+    toks = frame_tokens(2 * n_frames + 2, K, e.text_vocab, e.audio_vocab, seed=1 + rank)
+    dev = torch.device("cuda", local)
+    toks_d = torch.from_numpy(toks).to(dev)
+    out_d = torch.zeros((n_frames, 1 + e.dep_q), dtype=torch.int32, device=dev)
+    stream = torch.cuda.ExternalStream(e.stream, device=dev)
+
+    # ---- device-resident frames (value) ----
+    pos = START_POS
+    for i in range(args.warmup):
+        e.enqueue_frame(toks_d[i].data_ptr(), K, pos, out_d[i].data_ptr())
+        pos += 1
+    e.sync()
+    barrier(dist)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_id(local)) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            e.enqueue_frame(toks_d[args.warmup + i].data_ptr(), K, pos, out_d[args.warmup + i].data_ptr())
+            pos += 1
+        ev1.record(stream)
+        e.sync()
+        torch.cuda.synchronize(dev)
+    barrier(dist)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = reduce_max(dist, ms_local)
+    value = world * 1000.0 / ms
+    out_tokens = out_d.cpu().numpy()
+    assert (out_tokens[:, 0] >= 0).all() and (out_tokens[:, 0] < e.text_vocab).all()
+
+    # ---- end to end through the reference C ABI (e2e) ----
+    z = np.empty(e.n_embd, np.float32)
+    audio = np.empty(e.dep_q, np.int32)
+    for i in range(min(args.warmup, 3)):
+        e.pos = pos
+        z, lg = e.forward_temporal(toks[n_frames + i])
+        e.forward_depth_cascade(int(np.argmax(lg)), z, 0.0, 0)
+        pos += 1
+    barrier(dist)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e.pos = pos
+        z, lg = e.forward_temporal(toks[n_frames + (i % n_frames)])
+        audio = e.forward_depth_cascade(int(np.argmax(lg)), z, 0.0, 0)
+        pos += 1
+    e2e_s = reduce_max(dist, time.perf_counter() - t0)
+    e2e_value = world * args.steps / e2e_s
+    fin_bytes = 64 * 4 + 16
+    h2d = fin_bytes + (fin_bytes + e.n_embd * 4)
+    d2h = e.n_embd * 4 + e.text_vocab * 4 + 4 + (1 + 8) * 4 + 4
+
+    # ---- roofline of the dominant kernel ----
+    rl = gemv_roofline(local, peak)
+    total_b, temporal_b, dep_b, kv_b = frame_bytes(e)
+    launches_per_frame = 1 + e.n_layers * 5 + 1 + e.dep_q * (1 + 6 * 5 + 1) + 1
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            try:
+                cpu = cpu_baseline(path)
+            except Exception as ex:  # reported, not fatal
+                cpu = {"value": None, "unit": "frames/s", "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"failed: {ex}"}
+        line = {
+            "metric": "Moshi decode frames/s (B=1)", "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales)",
+            "data": "synthetic: seeded N(0,0.02) Q4_0 weights, N(0,1) f16 embeddings, seeded tokens and KV history",
+            "config": {"workload": "config2+3: 32-layer temporal (d4096, 32x128, FFN 11264) + 32000 text head + "
+                                   "greedy 8-step depformer (6x d1024) per frame, B=1, one session per GPU",
+                       "n_ctx": N_CTX, "start_pos": START_POS, "kv": args.kv,
+                       "l2": "weights 4.1 GB per frame > 126 MB L2 (no flush needed)",
+                       "parallelism": f"dp{world} (independent sessions)",
+                       "frame_hbm_bytes": total_b, "temporal_bytes": temporal_b, "depformer_bytes": dep_b,
+                       "kv_bytes": kv_b, "frame_hbm_gbs": total_b / (ms * 1e-3) / 1e9,
+                       "frame_hbm_frac": total_b / (ms * 1e-3) / 1e9 / peak},
+            "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": rl["achieved_gbs"] / peak, "traffic": traffic_from_profile(),
+                         "kernel": rl["kernel"], "bytes_per_launch": rl["bytes_per_launch"],
+                         "us_per_launch": rl["us_per_launch"], "peak_source": peak_kind},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "bmo_forward_temporal + host argmax + bmo_forward_depth_cascade (greedy), wall clock"},
+            "gpu_launches": launches_per_frame * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    e.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

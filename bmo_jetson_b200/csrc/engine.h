@@ -86,11 +86,11 @@ public:
 
 private:
     struct Layer {
-        QMatDesc qkv, wo, ffn_in, ffn_out;
+        QMatDesc qkv{}, wo{}, ffn_in{}, ffn_out{};
         float *norm1 = nullptr, *norm2 = nullptr;
     };
     struct DepLayer {
-        QMatDesc qkv[kDepQMax], wo[kDepQMax], ffn_in[kDepQMax], ffn_out[kDepQMax];
+        QMatDesc qkv[kDepQMax] = {}, wo[kDepQMax] = {}, ffn_in[kDepQMax] = {}, ffn_out[kDepQMax] = {};
         float *norm1 = nullptr, *norm2 = nullptr;
     };
 

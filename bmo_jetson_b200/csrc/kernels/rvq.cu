@@ -89,6 +89,7 @@ extern "C" {
 
 int bmo_rvq_decode(const int32_t *codes_dev, const float *proj_tables_dev, float *out_dev, void *stream) {
     if (!codes_dev || !proj_tables_dev || !out_dev) return 1;
+    cudaGetLastError();  // report only this call's launch errors
     rvq_decode_kernel<<<2, 256, 0, static_cast<cudaStream_t>(stream)>>>(codes_dev, proj_tables_dev, out_dev);
     return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
@@ -100,6 +101,7 @@ int bmo_rvq_encode(const float *in_vec_dev, const float *w_in0_dev, const float 
         !out_codes_dev || !scratch_dev)
         return 1;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGetLastError();  // report only this call's launch errors
     float *r = scratch_dev;
     float *bval = r + kRvqDim;
     int *bidx = reinterpret_cast<int *>(bval + kRvqBlocks);

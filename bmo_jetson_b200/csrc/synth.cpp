@@ -29,11 +29,17 @@ struct Gen {
     Gen(uint64_t seed, uint64_t stream) : key(mix64(seed) ^ mix64(stream + 0x632be59bd9b4e019ull)) {}
     // uniform in (0, 1]
     double uniform(uint64_t i) const { return (static_cast<double>(mix64(key ^ mix64(i)) >> 11) + 1.0) * 0x1.0p-53; }
-    double normal(uint64_t i) const {
-        const uint64_t p = i >> 1;
+    // Box-Muller pair p gives elements 2p (cosine branch) and 2p + 1 (sine branch).
+    void normal_pair(uint64_t p, double &z0, double &z1) const {
         const double r = std::sqrt(-2.0 * std::log(uniform(2 * p)));
         const double t = 6.283185307179586 * uniform(2 * p + 1);
-        return (i & 1) ? r * std::sin(t) : r * std::cos(t);
+        z0 = r * std::cos(t);
+        z1 = r * std::sin(t);
+    }
+    double normal(uint64_t i) const {
+        double z0, z1;
+        normal_pair(i >> 1, z0, z1);
+        return (i & 1) ? z1 : z0;
     }
 };
 
@@ -92,11 +98,14 @@ void bmo_synth_normal_f32(uint64_t seed, uint64_t stream, long long n, float mea
 
 void bmo_synth_f16(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, uint16_t *out) {
     const Gen g(seed, stream);
-    parallel_for(n, 4096, [&](long long i) {
-        const float v =
-            static_cast<float>(static_cast<double>(mean) + static_cast<double>(sigma) * g.normal(static_cast<uint64_t>(i)));
-        const __half h = __float2half_rn(v);
-        std::memcpy(&out[i], &h, 2);
+    parallel_for((n + 1) / 2, 2048, [&](long long p) {
+        double z[2];
+        g.normal_pair(static_cast<uint64_t>(p), z[0], z[1]);
+        for (int k = 0; k < 2 && 2 * p + k < n; ++k) {
+            const float v = static_cast<float>(static_cast<double>(mean) + static_cast<double>(sigma) * z[k]);
+            const __half h = __float2half_rn(v);
+            std::memcpy(&out[2 * p + k], &h, 2);
+        }
     });
 }
 
@@ -106,9 +115,12 @@ void bmo_synth_q4_0(uint64_t seed, uint64_t stream, long long rows, long long co
     parallel_for(rows, 1, [&](long long r) {
         float blk[32];
         for (long long b = 0; b < nb; ++b) {
-            for (int j = 0; j < 32; ++j) {
-                const uint64_t i = static_cast<uint64_t>(r * cols + b * 32 + j);
-                blk[j] = static_cast<float>(static_cast<double>(sigma) * g.normal(i));
+            const uint64_t base = static_cast<uint64_t>(r * cols + b * 32);  // even: cols % 32 == 0
+            for (int j = 0; j < 32; j += 2) {
+                double z0, z1;
+                g.normal_pair((base + j) >> 1, z0, z1);
+                blk[j] = static_cast<float>(static_cast<double>(sigma) * z0);
+                blk[j + 1] = static_cast<float>(static_cast<double>(sigma) * z1);
             }
             q4_0_block(blk, out + (r * nb + b) * 18);
         }

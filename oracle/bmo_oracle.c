@@ -733,7 +733,8 @@ orc_model *orc_model_load(const char *path, int n_ctx, int kv_type) {
      * the head count for the small synthetic test models. */
     m->dep_dim = m->dep_in[0] ? (int)m->dep_in[0]->ne[1] : 0;
     m->dep_heads = scalar_i32(g, "depformer_num_heads", 16);
-    m->dep_hd = m->dep_dim / 16;
+    if (m->dep_heads <= 0) m->dep_heads = 16;
+    m->dep_hd = m->dep_dim / m->dep_heads;
     m->dep_ffn = m->dep_gin[0][0] ? (int)(m->dep_gin[0][0]->ne[1] / 2) : 0;
     m->dep_n_ctx = dq > ORC_DEP_Q ? ORC_DEP_Q : dq;
 
@@ -845,6 +846,18 @@ int orc_forward_temporal(orc_model *m, const int32_t *tokens, int K, int pos,
     free(fin);
     for (int c = 0; c < n_capture; ++c)
         if (capture[c] < 0 || capture[c] >= m->n_layers) return 6;
+    return 0;
+}
+
+/* out_norm + text head on a given final residual (bmo_compute.cpp:2660-2735). */
+int orc_text_head(orc_model *m, const float *x_final, float *out_z, float *out_logits) {
+    const int n = m->n_embd;
+    if (m->out_norm) orc_rmsnorm(x_final, f32(m->out_norm), m->norm_eps, n, out_z);
+    else memcpy(out_z, x_final, sizeof(float) * (size_t)n);
+    if (!m->text_linear) return 3;
+    linear_q4_0(q4(m->text_linear), out_z, out_logits, m->text_vocab, n);
+    if (m->text_bias)
+        for (int i = 0; i < m->text_vocab; ++i) out_logits[i] = out_logits[i] + f32(m->text_bias)[i];
     return 0;
 }
 

@@ -78,6 +78,8 @@ int orc_forward_temporal(orc_model *m, const int32_t *tokens, int K, int pos,
 int orc_forward_layers(orc_model *m, const float *x_in, int pos,
                        int layer_begin, int layer_end, float *x_out);
 int orc_embed(orc_model *m, const int32_t *tokens, int K, float *out);
+/* out_norm and text head applied to a given final residual. */
+int orc_text_head(orc_model *m, const float *x_final, float *out_z, float *out_logits);
 int orc_forward_depth(orc_model *m, int cb, int32_t prev_token,
                       const float *z, float *out_logits);
 int orc_forward_depth_cascade_greedy(orc_model *m, int32_t text_token,

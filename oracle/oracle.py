@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
                                            ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         L.orc_forward_layers.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
         L.orc_embed.argtypes = [ctypes.c_void_p, _i32p, ctypes.c_int, _f32p]
+        L.orc_text_head.argtypes = [ctypes.c_void_p, _f32p, _f32p, _f32p]
         L.orc_forward_depth.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int32, _f32p, _f32p]
         L.orc_forward_depth_cascade_greedy.argtypes = [ctypes.c_void_p, ctypes.c_int32, _f32p, _i32p]
         L.orc_kv_import.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
@@ -195,6 +196,15 @@ class OracleModel:
         if rc:
             raise RuntimeError(f"oracle forward_temporal rc={rc}")
         return z, logits, cap
+
+    def text_head(self, x_final):
+        """(z, logits) of the out_norm + text head applied to a given final residual."""
+        z = np.zeros(self.n_embd, np.float32)
+        logits = np.zeros(max(self.text_vocab, 1), np.float32)
+        rc = self._L.orc_text_head(self._m, np.ascontiguousarray(x_final, np.float32), z, logits)
+        if rc:
+            raise RuntimeError(f"oracle text_head rc={rc}")
+        return z, logits
 
     def forward_layers(self, x, pos, begin, end):
         x = np.ascontiguousarray(x, np.float32)

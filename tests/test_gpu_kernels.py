@@ -187,7 +187,8 @@ def test_attention_matches_oracle(kv_type, hd, nh, n_ctx, n_layers, layer, pos):
         vb = orc.quantize_q4_0(hist_v.reshape(-1, 32)).reshape(-1, 18)
         kd, vd = to_dev(kb[:, 2:].copy().reshape(-1)), to_dev(vb[:, 2:].copy().reshape(-1))
         ksd, vsd = to_dev(kb[:, :2].copy().reshape(-1)), to_dev(vb[:, :2].copy().reshape(-1))
-    rc = L.bmo_k_decode_attention(to_dev(q).data_ptr(), to_dev(k).data_ptr(), to_dev(v).data_ptr(), kd.data_ptr(),
+    qd, kdev, vdev = to_dev(q), to_dev(k), to_dev(v)  # keep alive until the kernels ran
+    rc = L.bmo_k_decode_attention(qd.data_ptr(), kdev.data_ptr(), vdev.data_ptr(), kd.data_ptr(),
                                   vd.data_ptr(), ptr(ksd), ptr(vsd), out.data_ptr(), hd, nh, nh, n_ctx,
                                   pos_d.data_ptr(), layer, kv_type, scratch.data_ptr(), nbytes, stream())
     torch.cuda.synchronize()
