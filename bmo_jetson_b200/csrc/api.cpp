@@ -161,6 +161,17 @@ long long bmo_copy_kv_raw(bmo_handle_t *h, int which, int part, int layer, void 
     }
 }
 
+int bmo_debug_tap(bmo_handle_t *h, int which, float *out, int max_floats) {
+    if (!h || !out) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        return h->eng->debug_tap(which, out, max_floats);
+    } catch (const std::exception &e) {
+        h->last_error = e.what();
+        return -1;
+    }
+}
+
 int bmo_kv_import_f32(bmo_handle_t *h, int layer, int slot0, int n, const float *k_rows, const float *v_rows) {
     if (!h || !k_rows || !v_rows) return 1;
     std::lock_guard<std::mutex> lk(h->mu);

@@ -68,6 +68,7 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     cfg_.graphs = cfg.graphs && env_int("BMO_GRAPHS", 1) != 0;
     cfg_.pdl = cfg.pdl && env_int("BMO_PDL", 1) != 0;
     n_ctx = cfg.n_ctx > 0 ? cfg.n_ctx : 2048;
+    if (n_ctx > attn_max_ctx()) throw std::runtime_error("n_ctx exceeds the ring limit of " + std::to_string(attn_max_ctx()));
     if (cfg.kv_type >= 0) {
         kv_type = cfg.kv_type;
     } else {
@@ -466,7 +467,7 @@ void Engine::alloc_state() {
     size_t gp = 0, gc = 0;
     auto acc = [&](const QMatDesc &m) {
         if (!m.tiles) return;
-        gp = std::max(gp, static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float));
+        gp = std::max(gp, static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(double));
         gc = std::max(gc, static_cast<size_t>(m.n_tiles) * sizeof(int));
     };
     for (auto &l : L_) { acc(l.qkv); acc(l.wo); acc(l.ffn_in); acc(l.ffn_out); }
@@ -476,16 +477,11 @@ void Engine::alloc_state() {
         for (int s = 0; s < kDepQMax; ++s) { acc(d.qkv[s]); acc(d.wo[s]); acc(d.ffn_in[s]); acc(d.ffn_out[s]); }
     gpart_bytes_ = gp;
     gcount_bytes_ = gc;
-    gpart_ = static_cast<float *>(dalloc(gp));
+    gpart_ = static_cast<double *>(dalloc(gp));
     gcount_ = static_cast<int *>(dalloc(gc));
 
-    attn_splits_ = std::max(1, (n_ctx + attn_max_per_split() - 1) / attn_max_per_split());
-    const int maxh = std::max(n_heads, dep_heads);
-    apart_bytes_ = static_cast<size_t>(maxh) * attn_splits_ * (std::max(head_dim, dep_hd) + 2) * sizeof(float);
-    acount_bytes_ = static_cast<size_t>(maxh) * sizeof(int);
-    apart_ = static_cast<float *>(dalloc(apart_bytes_));
-    acount_ = static_cast<int *>(dalloc(acount_bytes_));
-    status_ = static_cast<int *>(dalloc(sizeof(int)));
+    attn_splits_ = attn_splits_for(n_ctx);
+    status_ =static_cast<int *>(dalloc(sizeof(int)));
     fin_d_ = static_cast<FrameIn *>(dalloc(sizeof(FrameIn)));
 
     auto halloc = [&](size_t bytes) -> void * {
@@ -593,8 +589,6 @@ void Engine::enqueue_layer(cudaStream_t s, int l) {
         at.pos = &fin_d_->pos;
         at.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
         at.out = attn_;
-        at.part = apart_;
-        at.count = acount_;
         at.status = status_;
         ck(launch_attention(at, head_dim, attn_splits_, s, cfg_.pdl), "launch attention");
 
@@ -660,8 +654,6 @@ void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const To
         at.pos = dep_pos_ + cb;
         at.scale = 1.0f / std::sqrt(static_cast<float>(dep_hd));
         at.out = dattn_;
-        at.part = apart_;
-        at.count = acount_;
         at.status = status_;
         ck(launch_attention(at, dep_hd, 1, s, cfg_.pdl), "launch depth attention");
 
@@ -753,7 +745,6 @@ void Engine::finish_call() {
         const int st = *status_h_;
         cudaMemsetAsync(status_, 0, sizeof(int), stream);
         cudaMemsetAsync(gcount_, 0, gcount_bytes_, stream);
-        cudaMemsetAsync(acount_, 0, acount_bytes_, stream);
         cudaStreamSynchronize(stream);
         throw std::runtime_error("device status " + std::to_string(st) + ": a bulk copy wait timed out");
     }
@@ -1021,6 +1012,26 @@ int Engine::copy_cache_f32(int which, int layer, int t_start, int n_positions, f
         w += n_positions * hd;
     }
     return w;
+}
+
+int Engine::debug_tap(int which, float *out, int max_floats) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(cudaStreamSynchronize(stream), "sync");
+    const float *src = nullptr;
+    int n = 0;
+    switch (which) {
+    case 0: src = q_; n = n_heads * head_dim; break;
+    case 1: src = vraw_; n = n_kv_heads * head_dim; break;
+    case 2: src = attn_; n = n_heads * head_dim; break;
+    case 3: src = xmid_; n = n_embd; break;
+    case 4: src = act_; n = ffn; break;
+    case 5: src = z_; n = n_embd; break;
+    case 6: src = reinterpret_cast<const float *>(rope_); n = head_dim; break;
+    default: return -1;
+    }
+    if (n > max_floats) return -1;
+    ck(cudaMemcpy(out, src, sizeof(float) * n, cudaMemcpyDeviceToHost), "debug tap");
+    return n;
 }
 
 long long Engine::copy_kv_raw(int which, int part, int layer, void *out, long long max_bytes) {

@@ -81,6 +81,7 @@ public:
     int kv_import(int layer, int slot0, int n, const float *k_rows, const float *v_rows);
     int copy_cache_f32(int which, int layer, int t_start, int n_positions, float *out);
     long long copy_kv_raw(int which, int part, int layer, void *out, long long max_bytes);
+    int debug_tap(int which, float *out, int max_floats);
     void capture_all();
     bool graphs_captured() const { return graphs_ready_; }
 
@@ -148,12 +149,9 @@ private:
     int *dep_pos_ = nullptr;
     int *tok_out_ = nullptr;  // [1 + kDepQMax]: text token, audio tokens
     // scratch
-    float *gpart_ = nullptr;
+    double *gpart_ = nullptr;
     int *gcount_ = nullptr;
     size_t gpart_bytes_ = 0, gcount_bytes_ = 0;
-    float *apart_ = nullptr;
-    int *acount_ = nullptr;
-    size_t apart_bytes_ = 0, acount_bytes_ = 0;
     int attn_splits_ = 1;
     int *status_ = nullptr;
     FrameIn *fin_d_ = nullptr;

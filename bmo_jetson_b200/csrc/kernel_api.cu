@@ -82,7 +82,7 @@ int bmo_k_repack_q4_0(const void *ggml_dev, void *tiled_dev, int rows, int cols,
 size_t bmo_k_gemv_scratch_bytes(int rows, int cols, int perm, int swiglu_f) {
     if (!shape_ok(rows, cols, perm, swiglu_f)) return 0;
     const QMatDesc m = make_desc(nullptr, rows, cols, perm, swiglu_f);
-    return align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float)) +
+    return align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(double)) +
            align256(static_cast<size_t>(m.n_tiles) * sizeof(int)) + 256;
 }
 
@@ -105,8 +105,8 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
     a.resid = resid_dev;
     a.argmax_limit = INT_MAX;
     uint8_t *s = static_cast<uint8_t *>(scratch_dev);
-    a.gpart = reinterpret_cast<float *>(s);
-    a.gcount = reinterpret_cast<int *>(s + align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(float)));
+    a.gpart = reinterpret_cast<double *>(s);
+    a.gcount = reinterpret_cast<int *>(s + align256(static_cast<size_t>(m.n_tiles) * (m.cpt + 1) * 32 * sizeof(double)));
     a.status = a.gcount + m.n_tiles;  // last word of the scratch block
     const long long nc = static_cast<long long>(m.n_tiles) * m.cpt;
     int dev = 0;
@@ -122,22 +122,16 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
     return static_cast<int>(launch_gemv(a, pro, epi, static_cast<int>(g), static_cast<cudaStream_t>(stream), false));
 }
 
-size_t bmo_k_attention_scratch_bytes(int n_heads, int head_dim, int n_ctx) {
-    const int splits = (n_ctx + attn_max_per_split() - 1) / attn_max_per_split();
-    return align256(static_cast<size_t>(n_heads) * splits * (head_dim + 2) * sizeof(float)) +
-           align256(static_cast<size_t>(n_heads) * sizeof(int)) + 256;
-}
-
 int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
                            void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev, int head_dim,
                            int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev, int layer, int kv_type,
-                           void *scratch_dev, size_t scratch_bytes, void *stream) {
-    if (!q_dev || !k_dev || !v_dev || !k_cache_dev || !v_cache_dev || !out_dev || !pos_dev || !scratch_dev)
+                           void *stream) {
+    if (!q_dev || !k_dev || !v_dev || !k_cache_dev || !v_cache_dev || !out_dev || !pos_dev)
         return static_cast<int>(cudaErrorInvalidValue);
-    if ((head_dim != 64 && head_dim != 128) || n_kv_heads <= 0 || n_heads % n_kv_heads || n_ctx <= 0 || layer < 0)
+    if ((head_dim != 64 && head_dim != 128) || n_kv_heads <= 0 || n_heads % n_kv_heads || n_ctx <= 0 ||
+        n_ctx > attn_max_ctx() || layer < 0)
         return static_cast<int>(cudaErrorInvalidValue);
     if (kv_type == kKvQ4_0 && (!k_scale_dev || !v_scale_dev)) return static_cast<int>(cudaErrorInvalidValue);
-    if (scratch_bytes < bmo_k_attention_scratch_bytes(n_heads, head_dim, n_ctx)) return static_cast<int>(cudaErrorInvalidValue);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const long long layer_off = static_cast<long long>(layer) * n_kv_heads * n_ctx * head_dim;
     const int warps = 2 * n_kv_heads * head_dim / 32;
@@ -146,8 +140,6 @@ int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *
         n_kv_heads, head_dim, n_ctx, pos_dev, layer_off, kv_type);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
-    const int splits = (n_ctx + attn_max_per_split() - 1) / attn_max_per_split();
-    uint8_t *sc = static_cast<uint8_t *>(scratch_dev);
     AttnArgs a{};
     a.q = q_dev;
     a.v_raw = v_dev;
@@ -163,10 +155,7 @@ int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *
     a.pos = pos_dev;
     a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
     a.out = out_dev;
-    a.part = reinterpret_cast<float *>(sc);
-    a.count = reinterpret_cast<int *>(sc + align256(static_cast<size_t>(n_heads) * splits * (head_dim + 2) * sizeof(float)));
-    a.status = a.count + n_heads;
-    return static_cast<int>(launch_attention(a, head_dim, splits, s, false));
+    return static_cast<int>(launch_attention(a, head_dim, attn_splits_for(n_ctx), s, false));
 }
 
 }  // extern "C"

@@ -2,11 +2,14 @@
 // and epilogues.
 //
 // Computes, per output row r, the reference dot product
-//   y[r] = sum_b d4[r,b] * (d8[b] * sumi[r,b] - 8 * s8[b])
-// (bmo_gemv_q4_0_q8_1_kernel, src/bmo_cuda_kernels.cu:560-683; the reference
-// splits each block into two half-block lanes, each subtracting 4*s8), with
-// the activation quantised to Q8_1 in shared memory by the same rule as
-// bmo_quantize_row_q8_1_kernel (:529-558).
+// (bmo_gemv_q4_0_q8_1_kernel, src/bmo_cuda_kernels.cu:560-683): each half
+// block h (elements {0..7,16..23} and {8..15,24..31}) contributes the fp32
+// term  d4 * ((float)sumi_h * d8 - 4 * s8),  and the terms are summed.  The
+// activation is quantised to Q8_1 in shared memory by the rule of
+// bmo_quantize_row_q8_1_kernel (:529-558).  Exact-reduction semantics: the
+// terms are formed with separately rounded fp32 operations as the reference
+// writes them and summed in double, rounded once to fp32 -- the same value
+// the CPU oracle computes, whatever the split of the work.
 //
 // Design (B200): one CTA per SM, 8 warps.  The weight stream is the only
 // HBM traffic that matters, so each warp keeps kRing 4.6 KB chunks in flight
@@ -14,10 +17,10 @@
 // first chunks are issued before griddepcontrol.wait, so under programmatic
 // dependent launch the stream starts while the previous kernel finishes.
 // Work is split "stream-K" style: CTA c owns a contiguous range of
-// (row tile, chunk) units, tiles that straddle two CTAs are finished by the
-// last owner to arrive (per-tile counter, fixed summation order, so results
-// are deterministic).  Epilogues fuse RoPE + KV-ring append, SwiGLU,
-// residual adds, logits + argmax and the depformer embedding add.
+// (row tile, chunk) units, tiles that straddle CTAs are finished by the last
+// owner to arrive (per-tile counter, fixed summation order, deterministic).
+// Epilogues fuse RoPE + KV-ring append, SwiGLU, residual adds, logits +
+// argmax and the depformer embedding add.
 #include "common.cuh"
 #include "../launch.h"
 
@@ -27,15 +30,15 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRing = 2;
 constexpr int kMaxNbx = 384;  // activations up to 12288 elements
-constexpr int kMaxTilesPerCta = 12;
+constexpr int kMaxTilesPerCta = 10;
 
 struct GemvSmem {
     uint64_t bar[kWarps][kRing];
     alignas(128) uint8_t ring[kWarps][kRing][kChunkBytes];
     alignas(16) int8_t xq[kMaxNbx * 32];
-    float2 xds[kMaxNbx];  // (d8, -8 * s8) of each Q8_1 block
-    float part[kMaxTilesPerCta][kWarps][32];
-    float red[kWarps];
+    float2 xds[kMaxNbx];  // (d8, 4 * s8) of each Q8_1 block
+    double part[kMaxTilesPerCta][kWarps][32];
+    double red[kWarps];
     float tok_v[kWarps];
     int tok_i[kWarps];
     int err;
@@ -49,9 +52,14 @@ __device__ __forceinline__ int cta_of_chunk(long long k, long long nc, int g) {
     return static_cast<int>(((k + 1) * g - 1) / nc);
 }
 
-// Dot product of one 8-block chunk (32 rows) with the activation blocks.
-__device__ __forceinline__ float chunk_dot(const uint8_t *ch, const int8_t *xq, const float2 *xds, int lane) {
-    float acc = 0.0f;
+// One half-block term of the reference: d4 * ((float)sumi * d8 - 4 * s8).
+__device__ __forceinline__ float half_term(int sumi, float d4, float2 ds) {
+    return __fmul_rn(d4, __fsub_rn(__fmul_rn(static_cast<float>(sumi), ds.x), ds.y));
+}
+
+// Dot product of one 8-block chunk (32 rows, lane = row) with the activation.
+__device__ __forceinline__ double chunk_dot(const uint8_t *ch, const int8_t *xq, const float2 *xds, int lane) {
+    double acc = 0.0;
 #pragma unroll
     for (int blk = 0; blk < kChunkBlocks; ++blk) {
         const uint4 w = *reinterpret_cast<const uint4 *>(ch + blk * 512 + lane * 16);
@@ -59,16 +67,18 @@ __device__ __forceinline__ float chunk_dot(const uint8_t *ch, const int8_t *xq, 
         const int4 xa = *reinterpret_cast<const int4 *>(xq + blk * 32);
         const int4 xb = *reinterpret_cast<const int4 *>(xq + blk * 32 + 16);
         const float2 ds = xds[blk];
-        // byte j holds element j (low nibble) and element j+16 (high nibble)
-        int s = __dp4a(static_cast<int>(w.x & 0x0F0F0F0Fu), xa.x, 0);
-        s = __dp4a(static_cast<int>((w.x >> 4) & 0x0F0F0F0Fu), xb.x, s);
-        s = __dp4a(static_cast<int>(w.y & 0x0F0F0F0Fu), xa.y, s);
-        s = __dp4a(static_cast<int>((w.y >> 4) & 0x0F0F0F0Fu), xb.y, s);
-        s = __dp4a(static_cast<int>(w.z & 0x0F0F0F0Fu), xa.z, s);
-        s = __dp4a(static_cast<int>((w.z >> 4) & 0x0F0F0F0Fu), xb.z, s);
-        s = __dp4a(static_cast<int>(w.w & 0x0F0F0F0Fu), xa.w, s);
-        s = __dp4a(static_cast<int>((w.w >> 4) & 0x0F0F0F0Fu), xb.w, s);
-        acc = fmaf(d4, fmaf(ds.x, static_cast<float>(s), ds.y), acc);
+        // byte j holds element j (low nibble) and element j+16 (high nibble);
+        // bytes 0-7 form the first half block, bytes 8-15 the second
+        int lo = __dp4a(static_cast<int>(w.x & 0x0F0F0F0Fu), xa.x, 0);
+        lo = __dp4a(static_cast<int>((w.x >> 4) & 0x0F0F0F0Fu), xb.x, lo);
+        lo = __dp4a(static_cast<int>(w.y & 0x0F0F0F0Fu), xa.y, lo);
+        lo = __dp4a(static_cast<int>((w.y >> 4) & 0x0F0F0F0Fu), xb.y, lo);
+        int hi = __dp4a(static_cast<int>(w.z & 0x0F0F0F0Fu), xa.z, 0);
+        hi = __dp4a(static_cast<int>((w.z >> 4) & 0x0F0F0F0Fu), xb.z, hi);
+        hi = __dp4a(static_cast<int>(w.w & 0x0F0F0F0Fu), xa.w, hi);
+        hi = __dp4a(static_cast<int>((w.w >> 4) & 0x0F0F0F0Fu), xb.w, hi);
+        acc += static_cast<double>(half_term(lo, d4, ds));
+        acc += static_cast<double>(half_term(hi, d4, ds));
     }
     return acc;
 }
@@ -85,12 +95,12 @@ __device__ __forceinline__ float emb_elem(const EmbTable &e, int tok, int i) {
         const float d = __half2float(*reinterpret_cast<const __half *>(b));
         const int j = i & 31;
         const int nib = j < 16 ? (b[2 + j] & 0x0F) : (b[2 + j - 16] >> 4);
-        return static_cast<float>(nib - 8) * d;
+        return __fmul_rn(static_cast<float>(nib - 8), d);
     }
     case kTQ8_0: {
         const uint8_t *b = row + (i >> 5) * 34;
         const float d = __half2float(*reinterpret_cast<const __half *>(b));
-        return static_cast<float>(static_cast<int8_t>(b[2 + (i & 31)])) * d;
+        return __fmul_rn(static_cast<float>(static_cast<int8_t>(b[2 + (i & 31)])), d);
     }
     default: return 0.0f;
     }
@@ -130,20 +140,23 @@ template <int EPI>
 __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane, float v, int tok) {
     const int r = t * kTileRows + lane;
     if constexpr (EPI == kEpiStore) {
-        if (r < a.W.rows) a.y[r] = a.bias ? v + a.bias[r] : v;
+        if (r < a.W.rows) a.y[r] = a.bias ? __fadd_rn(v, a.bias[r]) : v;
     } else if constexpr (EPI == kEpiResid) {
-        if (r < a.W.rows) a.y[r] = a.resid[r] + v;
+        if (r < a.W.rows) a.y[r] = __fadd_rn(a.resid[r], v);
     } else if constexpr (EPI == kEpiSwiGLU) {
+        // silu(gate) * up (swiglu_split_kernel, bmo_cuda_kernels.cu:370-387),
+        // exp evaluated in double and rounded once
         const float up = __shfl_down_sync(0xffffffffu, v, 16);
         const int h = t * 16 + lane;
         if (lane < 16 && h < a.W.swiglu_f) {
-            const float silu = v / (1.0f + __expf(-v));
-            a.y[h] = silu * up;
+            const float e = __double2float_rn(exp(-static_cast<double>(v)));
+            const float silu = __fdiv_rn(v, __fadd_rn(1.0f, e));
+            a.y[h] = __fmul_rn(silu, up);
         }
     } else if constexpr (EPI == kEpiLogits) {
         float val = -INFINITY;
         if (r < a.W.rows) {
-            val = a.bias ? v + a.bias[r] : v;
+            val = a.bias ? __fadd_rn(v, a.bias[r]) : v;
             a.y[r] = val;
         }
         float bv = (r < a.W.rows && r < a.argmax_limit) ? val : -INFINITY;
@@ -158,7 +171,7 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
     } else if constexpr (EPI == kEpiEmbAdd) {
         if (r < a.W.rows) {
             const bool ok = tok >= 0 && tok < a.emb.rows && a.emb.dim == a.W.rows;
-            a.y[r] = v + (ok ? emb_elem(a.emb, tok, r) : 0.0f);
+            a.y[r] = ok ? __fadd_rn(v, emb_elem(a.emb, tok, r)) : __fadd_rn(v, 0.0f);
         }
     } else if constexpr (EPI == kEpiQKV) {
         // whole tile lies inside one head of q, k or v (head_dim % 32 == 0)
@@ -167,10 +180,12 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
         const bool is_q = r < a.q_dim;
         const bool is_k = !is_q && r < a.q_dim + a.kv_dim;
         if ((is_q || is_k) && a.rope_cs) {
+            // interleaved RoPE (rope_interleaved_kernel, :317-368), separately rounded
             const int d = (is_q ? r : r - a.q_dim) % hd;
             const float2 cs = a.rope_cs[d >> 1];
             const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-            out = (lane & 1) ? partner * cs.y + v * cs.x : v * cs.x - partner * cs.y;
+            out = (lane & 1) ? __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x))
+                             : __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
         }
         if (is_q) {
             a.y[r] = out;
@@ -227,18 +242,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
     const int nb = a.W.cols / 32, nbx = a.W.nbx;
     float scale = 1.0f;
     if constexpr (PRO == kProNorm) {
-        float ss = 0.0f;
+        // rmsnorm_kernel (bmo_cuda_kernels.cu:244-295): scale = 1/sqrt(mean(x^2)+eps),
+        // the sum of squares in double, the root and reciprocal in double
+        double ss = 0.0;
         for (int i = tid; i < a.W.cols; i += kThreads) {
-            const float xv = a.x[i];
-            ss = fmaf(xv, xv, ss);
+            const double xv = static_cast<double>(a.x[i]);
+            ss = fma(xv, xv, ss);
         }
-        ss = warp_sum(ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) S.red[warp] = ss;
         __syncthreads();
-        float tot = 0.0f;
+        double tot = 0.0;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) tot += S.red[w];
-        scale = rsqrtf(tot / static_cast<float>(a.W.cols) + a.eps);
+        const float total = __double2float_rn(tot);
+        const float mean_eps = __fadd_rn(__fdiv_rn(total, static_cast<float>(a.W.cols)), a.eps);
+        scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(static_cast<double>(mean_eps))));
     }
     for (int b = tid; b < nbx; b += kThreads) {
         int4 *qd = reinterpret_cast<int4 *>(S.xq + b * 32);
@@ -266,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
             const int *qi = reinterpret_cast<const int *>(q);
             qd[0] = make_int4(qi[0], qi[1], qi[2], qi[3]);
             qd[1] = make_int4(qi[4], qi[5], qi[6], qi[7]);
-            S.xds[b] = make_float2(__low2float(ds), -8.0f * __high2float(ds));
+            S.xds[b] = make_float2(__low2float(ds), 4.0f * __high2float(ds));
             if (c == 0 && a.q8_out) {
                 int *o = reinterpret_cast<int *>(a.q8_out + static_cast<size_t>(b) * 36);
                 o[0] = *reinterpret_cast<const int *>(&ds);
@@ -284,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
             S.xds[b] = make_float2(0.0f, 0.0f);
         }
     }
-    for (int i = tid; i < kMaxTilesPerCta * kWarps * 32; i += kThreads) (&S.part[0][0][0])[i] = 0.0f;
+    for (int i = tid; i < kMaxTilesPerCta * kWarps * 32; i += kThreads) (&S.part[0][0][0])[i] = 0.0;
     int tok = -1;
     if constexpr (EPI == kEpiEmbAdd) {
         tok = resolve_token(a.tok, S.tok_v, S.tok_i);
@@ -295,13 +315,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
     // ---- main loop: stream chunks through the ring ----
     const int t_first = c0 / cpt;
     int cur = -1;
-    float acc = 0.0f;
+    double acc = 0.0;
     for (int i = 0; i < n_mine; ++i) {
         const int k = c0 + warp + kWarps * i;
         const int tile = k / cpt, kc = k - tile * cpt;
         if (tile != cur) {
             if (cur >= 0) S.part[cur - t_first][warp][lane] = acc;
-            acc = 0.0f;
+            acc = 0.0;
             cur = tile;
         }
         if (!mbar_wait(&S.bar[warp][i % kRing], (i / kRing) & 1)) {
@@ -325,17 +345,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
     }
     if (c1 <= c0) return;
 
-    // ---- per-tile reduction (fixed order) and epilogue ----
+    // ---- per-tile reduction (fixed order, double) and epilogue ----
     const int t_last = (c1 - 1) / cpt;
     for (int tl = warp; tl <= t_last - t_first; tl += kWarps) {
         const int t = t_first + tl;
-        float v = 0.0f;
+        double v = 0.0;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += S.part[tl][w][lane];
         const int f = cta_of_chunk(static_cast<long long>(t) * cpt, NC, G);
         const int l = cta_of_chunk(static_cast<long long>(t) * cpt + cpt - 1, NC, G);
         if (f != l) {
-            float *gp = a.gpart + (static_cast<size_t>(t) * (cpt + 1)) * 32;
+            double *gp = a.gpart + (static_cast<size_t>(t) * (cpt + 1)) * 32;
             gp[(c - f) * 32 + lane] = v;
             __threadfence();
             __syncwarp();
@@ -344,11 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old != l - f) continue;
             __threadfence();
-            v = 0.0f;
+            v = 0.0;
             for (int o = 0; o <= l - f; ++o) v += __ldcg(gp + o * 32 + lane);
             if (lane == 0) a.gcount[t] = 0;
         }
-        tile_epilogue<EPI>(a, t, lane, v, tok);
+        tile_epilogue<EPI>(a, t, lane, __double2float_rn(v), tok);
     }
 }
 
@@ -387,20 +407,23 @@ static cudaError_t configure_one() {
                                 static_cast<int>(sizeof(GemvSmem)));
 }
 
+#define BMO_GEMV_VARIANTS(X)  \
+    X(kProNorm, kEpiQKV)      \
+    X(kProPlain, kEpiResid)   \
+    X(kProNorm, kEpiSwiGLU)   \
+    X(kProNorm, kEpiLogits)   \
+    X(kProPlain, kEpiLogits)  \
+    X(kProPlain, kEpiEmbAdd)  \
+    X(kProPlain, kEpiStore)   \
+    X(kProNorm, kEpiStore)    \
+    X(kProPlain, kEpiSwiGLU)  \
+    X(kProNorm, kEpiResid)
+
 cudaError_t configure_gemv() {
     cudaError_t e = cudaSuccess;
 #define BMO_GEMV_CFG(P, E) \
     if ((e = configure_one<P, E>()) != cudaSuccess) return e;
-    BMO_GEMV_CFG(kProNorm, kEpiQKV)
-    BMO_GEMV_CFG(kProPlain, kEpiResid)
-    BMO_GEMV_CFG(kProNorm, kEpiSwiGLU)
-    BMO_GEMV_CFG(kProNorm, kEpiLogits)
-    BMO_GEMV_CFG(kProPlain, kEpiLogits)
-    BMO_GEMV_CFG(kProPlain, kEpiEmbAdd)
-    BMO_GEMV_CFG(kProPlain, kEpiStore)
-    BMO_GEMV_CFG(kProNorm, kEpiStore)
-    BMO_GEMV_CFG(kProPlain, kEpiSwiGLU)
-    BMO_GEMV_CFG(kProNorm, kEpiResid)
+    BMO_GEMV_VARIANTS(BMO_GEMV_CFG)
 #undef BMO_GEMV_CFG
     return e;
 }
@@ -414,16 +437,7 @@ cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid,
     if ((per_cta + a.W.cpt - 1) / a.W.cpt + 1 > kMaxTilesPerCta) return cudaErrorInvalidValue;
 #define BMO_GEMV_CASE(P, E) \
     if (prologue == P && epilogue == E) return launch_t<P, E>(a, grid, s, pdl);
-    BMO_GEMV_CASE(kProPlain, kEpiSwiGLU)
-    BMO_GEMV_CASE(kProNorm, kEpiResid)
-    BMO_GEMV_CASE(kProNorm, kEpiQKV)
-    BMO_GEMV_CASE(kProPlain, kEpiResid)
-    BMO_GEMV_CASE(kProNorm, kEpiSwiGLU)
-    BMO_GEMV_CASE(kProNorm, kEpiLogits)
-    BMO_GEMV_CASE(kProPlain, kEpiLogits)
-    BMO_GEMV_CASE(kProPlain, kEpiEmbAdd)
-    BMO_GEMV_CASE(kProPlain, kEpiStore)
-    BMO_GEMV_CASE(kProNorm, kEpiStore)
+    BMO_GEMV_VARIANTS(BMO_GEMV_CASE)
 #undef BMO_GEMV_CASE
     return cudaErrorInvalidValue;
 }

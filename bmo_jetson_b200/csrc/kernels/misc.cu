@@ -48,13 +48,15 @@ __global__ void embed_kernel(const EmbTable *tables, int n_tables, const int *to
         out[i] = acc;
     }
     if (blockIdx.x == 0 && rope_cs && threadIdx.x < head_dim / 2) {
+        // exponent and angle in fp32 as the reference; the power and the
+        // trig evaluated in double and rounded once (exact-reduction semantics)
         const int k = threadIdx.x;
         const float exponent = __fdiv_rn(static_cast<float>(2 * k), static_cast<float>(head_dim));
-        const float inv_freq = powf(theta, -exponent);
+        const float inv_freq = __double2float_rn(pow(static_cast<double>(theta), -static_cast<double>(exponent)));
         const float angle = __fmul_rn(static_cast<float>(*pos), inv_freq);
-        float sn, cs;
-        sincosf(angle, &sn, &cs);
-        rope_cs[k] = make_float2(cs, sn);
+        double sn, cs;
+        sincos(static_cast<double>(angle), &sn, &cs);
+        rope_cs[k] = make_float2(__double2float_rn(cs), __double2float_rn(sn));
     }
 }
 

@@ -15,9 +15,10 @@ size_t gemv_smem_bytes();
 int gemv_max_tiles_per_cta();
 int gemv_max_nbx();
 
-// Ring decode attention (kernels/attention.cu), grid (heads, splits).
+// Ring decode attention (kernels/attention.cu): one cluster of `splits` CTAs per head.
 cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl);
-int attn_max_per_split();
+int attn_splits_for(int n_ctx);
+int attn_max_ctx();
 
 // Frame-start embedding sum + RoPE table (kernels/misc.cu).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,

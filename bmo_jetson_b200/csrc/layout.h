@@ -101,7 +101,7 @@ struct GemvArgs {
     EmbTable emb;
     TokenSrc tok;
     // stream-K bookkeeping
-    float *gpart;          // [n_tiles][cpt+1][32]
+    double *gpart;         // [n_tiles][cpt+1][32] per-owner partial sums
     int *gcount;           // [n_tiles], zero between launches
     int *status;
 };
@@ -116,8 +116,6 @@ struct AttnArgs {
     const int *pos;
     float scale;
     float *out;              // [n_heads][hd]
-    float *part;             // [n_heads][splits][hd + 2]
-    int *count;              // [n_heads]
     int *status;
 };
 

@@ -78,6 +78,8 @@ def lib() -> ctypes.CDLL:
     L.bmo_forward_frame_greedy.restype = i
     L.bmo_forward_layers.argtypes = [vp, _c_f32p, i, i, i, _c_f32p]
     L.bmo_forward_layers.restype = i
+    L.bmo_debug_tap.argtypes = [vp, i, _c_f32p, i]
+    L.bmo_debug_tap.restype = i
     L.bmo_enqueue_frame.argtypes = [vp, vp, i, i, vp]
     L.bmo_enqueue_frame.restype = i
     L.bmo_last_error.argtypes = [vp]
@@ -98,9 +100,7 @@ def lib() -> ctypes.CDLL:
     L.bmo_k_gemv_scratch_bytes.restype = sz
     L.bmo_k_gemv_q4_0.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, vp, vp, vp, sz, i, vp]
     L.bmo_k_gemv_q4_0.restype = i
-    L.bmo_k_attention_scratch_bytes.argtypes = [i, i, i]
-    L.bmo_k_attention_scratch_bytes.restype = sz
-    L.bmo_k_decode_attention.argtypes = [vp] * 8 + [i] * 4 + [vp, i, i, vp, sz, vp]
+    L.bmo_k_decode_attention.argtypes = [vp] * 8 + [i] * 4 + [vp, i, i, vp]
     L.bmo_k_decode_attention.restype = i
     _lib = L
     return L
@@ -270,6 +270,16 @@ class BMOEngine:
         if rc != 0:
             raise RuntimeError(f"bmo_forward_layers rc={rc}: {_err(self._h)}")
         return out
+
+    TAPS = {"q": 0, "v": 1, "attn": 2, "xmid": 3, "act": 4, "z": 5, "rope": 6}
+
+    def debug_tap(self, name: str) -> np.ndarray:
+        """An activation buffer as left by the last call (see bmo_debug_tap)."""
+        out = np.empty(1 << 16, np.float32)
+        n = lib().bmo_debug_tap(self._h, self.TAPS[name], out.ctypes.data_as(_c_f32p), out.size)
+        if n < 0:
+            raise RuntimeError(f"bmo_debug_tap({name}) failed")
+        return out[:n].copy()
 
     def enqueue_frame(self, tokens_dev_ptr: int, n_tokens: int, pos: int, out_tokens_dev_ptr: int) -> None:
         rc = lib().bmo_enqueue_frame(self._h, tokens_dev_ptr, n_tokens, pos, out_tokens_dev_ptr)

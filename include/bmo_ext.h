@@ -65,6 +65,13 @@ BMO_API int bmo_forward_frame_greedy(bmo_handle_t *h, const int32_t *input_token
 BMO_API int bmo_forward_layers(bmo_handle_t *h, const float *x_in, int pos, int layer_begin, int layer_end,
                                float *x_out);
 
+/* Debug taps (the role of the reference's BMO_DUMP_* dumps): copies the
+ * engine's activation buffer `which` as left by the last call into out
+ * (max_floats).  which: 0 rotated q, 1 raw v, 2 attention output, 3
+ * post-attention residual, 4 SwiGLU activation, 5 normed hidden z, 6 RoPE
+ * (cos, sin) table.  Returns floats copied or -1. */
+BMO_API int bmo_debug_tap(bmo_handle_t *h, int which, float *out, int max_floats);
+
 /* Asynchronous device-resident frame: tokens_dev (device int32[num_codebooks])
  * are copied on the device, the frame graph is enqueued on the handle's
  * stream, and the text token + dep_q audio tokens land in out_tokens_dev

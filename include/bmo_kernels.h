@@ -49,17 +49,17 @@ BMO_API int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm,
                             float *y_dev, void *q8_out_dev, float *xn_out_dev, void *scratch_dev,
                             size_t scratch_bytes, int grid, void *stream);
 
-/* Scratch bytes bmo_k_decode_attention needs. */
-BMO_API size_t bmo_k_attention_scratch_bytes(int n_heads, int head_dim, int n_ctx);
 /* Appends k, v (fp32, [n_kv_heads][head_dim]) at ring slot pos % n_ctx of
  * `layer`, then attends q over the window (replaces launch_decode_attention,
  * bmo.h:414-428).  Caches are [n_layers][n_kv_heads][n_ctx][head_dim] in
  * fp16 (kv_type 0) or Q4_0 nibble planes with fp16 scale planes (kv_type 1;
- * *_scale_dev). pos_dev is a device int. */
+ * *_scale_dev).  pos_dev is a device int; n_ctx <= 8192.  No scratch: the
+ * window splits of a head exchange partial results through distributed
+ * shared memory. */
 BMO_API int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
                                    void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev,
                                    int head_dim, int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev,
-                                   int layer, int kv_type, void *scratch_dev, size_t scratch_bytes, void *stream);
+                                   int layer, int kv_type, void *stream);
 
 #ifdef __cplusplus
 }

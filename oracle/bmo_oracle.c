@@ -18,9 +18,18 @@
  * restated by gguf-py's quants.Q4_0) for weights and the Q4_0 KV mode.
  *
  * Build with -ffp-contract=off: the quantisers depend on separately rounded
- * multiplies and adds.  The only freedom taken is the order of fp32
- * reductions (dot products accumulate in double), which the reference
- * leaves to its thread layout.
+ * multiplies and adds.
+ *
+ * Exact-reduction semantics.  Where the reference leaves a result to its
+ * thread layout (the order of fp32 reductions) or to a fast approximation
+ * (__expf, __powf, __sincosf, rsqrtf), this restatement fixes one value:
+ * reductions are carried in double and rounded once, transcendentals are
+ * evaluated in double and rounded once to fp32.  Every other operation is
+ * the reference's fp32 operation in the reference's order.  The CUDA kernels
+ * implement the same semantics, so the two agree bit for bit (up to rare
+ * double-rounding ties) instead of drifting apart through the Q8_1
+ * requantisation of every activation, which turns last-bit differences into
+ * whole-code flips.
  */
 #include "bmo_oracle.h"
 
@@ -211,15 +220,16 @@ void orc_rmsnorm(const float *x, const float *w, float eps, int n, float *y) {
 }
 
 /* rope_interleaved_kernel, bmo_cuda_kernels.cu:317-368: pair (2i, 2i+1),
- * inv_freq = theta^(-2i/hd) and angle = pos*inv_freq in fp32 as in the
- * kernel; the trig itself is evaluated accurately. */
+ * exponent 2i/hd and angle = pos*inv_freq in fp32 as in the kernel; the
+ * power and the trig are evaluated in double and rounded once to fp32
+ * (the kernel's __powf/__sincosf are approximations of the same values). */
 void orc_rope_interleaved(const float *x, int n_heads, int head_dim, int pos,
                           float theta, float *y) {
     const int half = head_dim / 2;
     for (int h = 0; h < n_heads; ++h) {
         for (int i = 0; i < half; ++i) {
             const float exponent = (float)(2 * i) / (float)head_dim;
-            const float inv_freq = powf(theta, -exponent);
+            const float inv_freq = (float)pow((double)theta, -(double)exponent);
             const float angle = (float)pos * inv_freq;
             const float cs = (float)cos((double)angle), sn = (float)sin((double)angle);
             const float xr = x[h * head_dim + 2 * i], xi = x[h * head_dim + 2 * i + 1];
@@ -229,11 +239,14 @@ void orc_rope_interleaved(const float *x, int n_heads, int head_dim, int pos,
     }
 }
 
-/* swiglu_split_kernel, bmo_cuda_kernels.cu:370-387. */
+/* swiglu_split_kernel, bmo_cuda_kernels.cu:370-387: silu(gate) * up with
+ * exp(-gate) evaluated in double and rounded once (the kernel's __expf is an
+ * approximation of it); the divide and multiply are fp32. */
 void orc_swiglu(const float *h, int d_ff, float *y) {
     for (int i = 0; i < d_ff; ++i) {
         const float gate = h[i], up = h[i + d_ff];
-        const float silu = gate / (1.0f + expf(-gate));
+        const float e = (float)exp(-(double)gate);
+        const float silu = gate / (1.0f + e);
         y[i] = silu * up;
     }
 }
@@ -312,19 +325,19 @@ static void decode_attention(const float *q, const float *k, const float *v,
             scores[i] = (float)dot * scale;
             if (scores[i] > mx) mx = scores[i];
         }
-        float sum = 0.0f;
+        /* p_i = exp(s_i - max) rounded once to fp32; the normalisation and the
+         * weighted sum are carried in double and rounded once per output. */
+        double sum = 0.0;
         for (int i = 0; i < window; ++i) {
-            scores[i] = expf(scores[i] - mx);
-            sum += scores[i];
+            scores[i] = (float)exp((double)(scores[i] - mx));
+            sum += (double)scores[i];
         }
-        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
         for (int i = 0; i < window; ++i) {
             const int slot = (start + i) % n_ctx;
             kv_load(kv, 1, base + (size_t)slot * hd, row, hd);
-            const float w = scores[i] * inv;
-            for (int d = 0; d < hd; ++d) acc[d] += (double)w * (double)row[d];
+            for (int d = 0; d < hd; ++d) acc[d] += (double)scores[i] * (double)row[d];
         }
-        for (int d = 0; d < hd; ++d) out[(size_t)h * hd + d] = (float)acc[d];
+        for (int d = 0; d < hd; ++d) out[(size_t)h * hd + d] = (float)(acc[d] / sum);
         free(scores);
         free(row);
         free(acc);

@@ -14,13 +14,13 @@ from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-3          # hidden states
-TOL_LOGITS = 1e-2   # end-to-end logits of the 256-wide test models, see below
-# One Q8_1 code that rounds the other way (a 1-ulp upstream difference at a
-# .5 boundary) moves the logits of a 256-wide activation by ~1.5e-3 relative;
-# the reference's own CPU and GPU paths differ the same way.  Kernel error is
-# isolated separately: the head applied to the GPU's own hidden state must
-# match to 1e-5, and greedy tokens must be identical.
+TOL = 1e-5          # hidden states (1e-3)
+TOL_LOGITS = 1e-5   # logits (1e-3)
+# The CUDA path and the oracle share exact-reduction semantics, so they agree
+# to the last bit except for rare double-rounding ties; without them a single
+# Q8_1 code rounding the other way (a last-bit difference at a .5 boundary)
+# moves a 256-wide activation's logits by ~1.5e-3 and the drift compounds
+# through every requantisation.  Greedy tokens must be identical.
 
 
 def head_weights(path):
@@ -223,7 +223,7 @@ def test_wrapped_ring_from_imported_history(tiny_model, kv_type):
         vg = e.get_v_cache_f32(layer, 0, n_ctx).reshape(n_ctx, -1)
         vo = o.kv_export(1, layer, 0, n_ctx)
         np.testing.assert_array_equal(vg[kept], vo[kept])
-        assert rel_l2(vg[sorted(appended)], vo[sorted(appended)]) < (TOL if kv_type == 0 else 0.05)
+        assert rel_l2(vg[sorted(appended)], vo[sorted(appended)]) < TOL
     e.close()
     o.close()
 
@@ -271,8 +271,7 @@ def test_full_width_block_at_wrapped_position(model_dir):
         yo = o.forward_layers(x, 700, 0, 1)
         assert rel_l2(y, yo) < TOL
         # slot 700 % 512 = 188 now holds this token's K
-        tol = TOL if kv_type == 0 else 0.05  # one Q4 step can differ when the fp32 inputs differ in the last bit
-        assert rel_l2(e.get_k_cache_f32(0, 188, 1).reshape(-1), o.kv_export(0, 0, 188, 1).reshape(-1)) < tol
+        assert rel_l2(e.get_k_cache_f32(0, 188, 1).reshape(-1), o.kv_export(0, 0, 188, 1).reshape(-1)) < TOL
         e.close()
         o.close()
 
