@@ -49,6 +49,30 @@ BMO_API int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm,
                             float *y_dev, void *q8_out_dev, float *xn_out_dev, void *scratch_dev,
                             size_t scratch_bytes, int grid, void *stream);
 
+/* Size of the fixed scratch buffer behind bmo_k_gemv_q4_0_static (4 MiB: every
+ * temporal and depformer layer matrix of the 7B Moshi shapes fits; the
+ * 32000-row text head does not). */
+#define BMO_K_GEMV_STATIC_SCRATCH_BYTES (4u << 20)
+/* Returned by bmo_k_gemv_q4_0_static when the matrix needs more scratch than
+ * BMO_K_GEMV_STATIC_SCRATCH_BYTES (see bmo_k_gemv_scratch_bytes). */
+#define BMO_K_ERR_SCRATCH_TOO_SMALL (-2)
+
+/* bmo_k_gemv_q4_0 for callers that cannot allocate device memory when they
+ * run it (a real-time callback that must not block in cudaMalloc, a host
+ * framework that owns all allocations, a process under a device-memory cap).
+ * No counterpart in the reference.  The split-K scratch is a fixed 4 MiB
+ * buffer inside libbmo (held by every GPU that loads the library until
+ * exit) instead of scratch_dev; nothing is allocated or freed.  Arguments
+ * and results are those of bmo_k_gemv_q4_0.  The buffer is shared by every
+ * call on a device and keeps the last call's contents (its counters are
+ * cleared on `stream` before each launch), so calls that can overlap on the
+ * GPU race: keep them on one stream or order them.  The first call on a
+ * device looks up the buffer's address; make it before any stream capture.
+ * Returns BMO_K_ERR_SCRATCH_TOO_SMALL for matrices beyond the buffer. */
+BMO_API int bmo_k_gemv_q4_0_static(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                                   const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
+                                   float *y_dev, void *q8_out_dev, float *xn_out_dev, int grid, void *stream);
+
 /* Appends k, v (fp32, [n_kv_heads][head_dim]) at ring slot pos % n_ctx of
  * `layer`, then attends q over the window (replaces launch_decode_attention,
  * bmo.h:414-428).  Caches are [n_layers][n_kv_heads][n_ctx][head_dim] in
