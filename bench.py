@@ -389,6 +389,21 @@ def main():
     h2d = fin_bytes + (fin_bytes + e.n_embd * 4)
     d2h = e.n_embd * 4 + e.text_vocab * 4 + 4 + (1 + 8) * 4 + 4
 
+    # ---- per-part device time: temporal step alone, depformer cascade alone ----
+    def timed(fn, n):
+        e.sync()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(n):
+            fn(i)
+        b.record(stream)
+        e.sync()
+        return a.elapsed_time(b) / n
+    n_part = max(5, min(args.steps, 20))
+    temporal_ms = timed(lambda i: e.enqueue_temporal(toks_d[i % n_frames].data_ptr(), K, pos + i), n_part)
+    pos += n_part
+    depth_ms = timed(lambda i: e.enqueue_cascade(int(out_tokens[i % n_frames, 0])), n_part)
+
     # ---- roofline of the dominant kernel ----
     rl = gemv_roofline(local, peak)
     total_b, temporal_b, dep_b, kv_b = frame_bytes(e)
@@ -416,7 +431,9 @@ def main():
                        "parallelism": f"dp{world} (independent sessions)",
                        "frame_hbm_bytes": total_b, "temporal_bytes": temporal_b, "depformer_bytes": dep_b,
                        "kv_bytes": kv_b, "frame_hbm_gbs": total_b / (ms * 1e-3) / 1e9,
-                       "frame_hbm_frac": total_b / (ms * 1e-3) / 1e9 / peak},
+                       "frame_hbm_frac": total_b / (ms * 1e-3) / 1e9 / peak,
+                       "temporal_ms": temporal_ms, "depformer_ms": depth_ms,
+                       "temporal_hbm_gbs": (temporal_b + kv_b) / (temporal_ms * 1e-3) / 1e9},
             "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
                          "frac": rl["achieved_gbs"] / peak, "traffic": traffic_from_profile(),
                          "kernel": rl["kernel"], "bytes_per_launch": rl["bytes_per_launch"],

@@ -415,6 +415,35 @@ int bmo_enqueue_frame(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebo
     }
 }
 
+int bmo_enqueue_temporal(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos) {
+    if (!h || !tokens_dev) return 1;
+    bmo::Engine *e = h->eng.get();
+    if (num_codebooks <= 0 || num_codebooks > e->num_codebooks || pos < 0) return 2;
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        e->enqueue_temporal_device(tokens_dev, num_codebooks, pos);
+        h->pos = pos + 1;
+        return 0;
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
+int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token) {
+    if (!h) return 1;
+    bmo::Engine *e = h->eng.get();
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        if (e->dep_dim <= 0 || !e->has_dep_tables) return 3;
+        e->enqueue_cascade_device(text_token);
+        return 0;
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
 int bmo_sync(bmo_handle_t *h) {
     if (!h) return 1;
     std::lock_guard<std::mutex> lk(h->mu);

@@ -88,6 +88,7 @@ Engine::~Engine() {
     };
     drop(g_temporal_);
     drop(g_layers_);
+    drop(g_cascade_z_);
     drop(g_cascade_);
     drop(g_frame_);
     for (auto &g : g_depth_) drop(g);
@@ -875,6 +876,22 @@ void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int
     if (out_tokens_dev)
         ck(cudaMemcpyAsync(out_tokens_dev, tok_out_, sizeof(int) * (1 + dep_q), cudaMemcpyDeviceToDevice, stream),
            "tokens copy");
+}
+
+void Engine::enqueue_temporal_device(const int32_t *tokens_dev, int K, int pos) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
+    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+}
+
+void Engine::enqueue_cascade_device(int32_t text_token) {
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    ck(launch_set_int(&fin_d_->prev_token, text_token, stream), "set token");
+    launch(g_cascade_z_, [this](cudaStream_t s) {
+        TokenSrc t{};
+        t.tok = &fin_d_->prev_token;
+        enqueue_cascade(s, z_, t);
+    });
 }
 
 int Engine::sync_status() {

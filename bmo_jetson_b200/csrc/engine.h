@@ -75,6 +75,8 @@ public:
     void run_cascade_greedy(int32_t text_tok, const float *z, int32_t *out_tokens);
     void run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *out_text_tok, int32_t *out_audio);
     void enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev);
+    void enqueue_temporal_device(const int32_t *tokens_dev, int K, int pos);
+    void enqueue_cascade_device(int32_t text_token);
     int sync_status();
     void reset_kv();
     void reset_depth_kv();
@@ -163,7 +165,7 @@ private:
 
     // graphs
     cudaGraphExec_t g_temporal_ = nullptr, g_depth_[kDepQMax] = {}, g_cascade_ = nullptr, g_frame_ = nullptr;
-    cudaGraphExec_t g_layers_ = nullptr;
+    cudaGraphExec_t g_layers_ = nullptr, g_cascade_z_ = nullptr;
     int g_layers_range_[2] = {-1, -1};
     bool graphs_ready_ = false;
 };

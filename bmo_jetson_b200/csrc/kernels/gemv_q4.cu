@@ -26,9 +26,12 @@
 
 namespace bmo {
 
+#ifndef BMO_GEMV_RING
+#define BMO_GEMV_RING 2
+#endif
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRing = 2;
+constexpr int kRing = BMO_GEMV_RING;  // chunks in flight per warp
 constexpr int kMaxNbx = 384;  // activations up to 12288 elements
 constexpr int kMaxTilesPerCta = 10;
 

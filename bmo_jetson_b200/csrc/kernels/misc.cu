@@ -85,6 +85,13 @@ cudaError_t launch_set_frame(int *fin_tokens, int *fin_n_tok, int *fin_pos, cons
     return cudaGetLastError();
 }
 
+__global__ void set_int_kernel(int *dst, int v) { *dst = v; }
+
+cudaError_t launch_set_int(int *dst, int v, cudaStream_t s) {
+    set_int_kernel<<<1, 1, 0, s>>>(dst, v);
+    return cudaGetLastError();
+}
+
 // Greedy token from per-tile (max, argmax) pairs: highest value, lowest
 // index among equals (std::max_element's first maximum).
 __global__ void finalize_token_kernel(const float2 *pairs, int n, int *out) {

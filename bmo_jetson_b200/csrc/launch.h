@@ -25,6 +25,7 @@ cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens
                          float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, cudaStream_t s);
 cudaError_t launch_set_frame(int *fin_tokens, int *fin_n_tok, int *fin_pos, const int *tokens, int K, int pos,
                              cudaStream_t s);
+cudaError_t launch_set_int(int *dst, int v, cudaStream_t s);
 cudaError_t launch_finalize_token(const float2 *pairs, int n, int *out, cudaStream_t s, bool pdl);
 // Sets the shared-memory opt-in of every kernel variant on the current device.
 cudaError_t configure_kernels();

@@ -80,6 +80,10 @@ def lib() -> ctypes.CDLL:
     L.bmo_forward_layers.restype = i
     L.bmo_debug_tap.argtypes = [vp, i, _c_f32p, i]
     L.bmo_debug_tap.restype = i
+    L.bmo_enqueue_temporal.argtypes = [vp, vp, i, i]
+    L.bmo_enqueue_temporal.restype = i
+    L.bmo_enqueue_cascade.argtypes = [vp, ctypes.c_int32]
+    L.bmo_enqueue_cascade.restype = i
     L.bmo_enqueue_frame.argtypes = [vp, vp, i, i, vp]
     L.bmo_enqueue_frame.restype = i
     L.bmo_last_error.argtypes = [vp]
@@ -287,6 +291,16 @@ class BMOEngine:
         rc = lib().bmo_enqueue_frame(self._h, tokens_dev_ptr, n_tokens, pos, out_tokens_dev_ptr)
         if rc != 0:
             raise RuntimeError(f"bmo_enqueue_frame rc={rc}: {_err(self._h)}")
+
+    def enqueue_temporal(self, tokens_dev_ptr: int, n_tokens: int, pos: int) -> None:
+        rc = lib().bmo_enqueue_temporal(self._h, tokens_dev_ptr, n_tokens, pos)
+        if rc != 0:
+            raise RuntimeError(f"bmo_enqueue_temporal rc={rc}: {_err(self._h)}")
+
+    def enqueue_cascade(self, text_token: int) -> None:
+        rc = lib().bmo_enqueue_cascade(self._h, int(text_token))
+        if rc != 0:
+            raise RuntimeError(f"bmo_enqueue_cascade rc={rc}: {_err(self._h)}")
 
     def sync(self) -> None:
         rc = lib().bmo_sync(self._h)

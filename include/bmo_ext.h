@@ -78,6 +78,12 @@ BMO_API int bmo_debug_tap(bmo_handle_t *h, int which, float *out, int max_floats
  * (device int32[1 + dep_q]).  No host synchronisation. */
 BMO_API int bmo_enqueue_frame(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos,
                               int32_t *out_tokens_dev);
+/* Asynchronous parts of a frame, for timing: the temporal step alone
+ * (tokens_dev as in bmo_enqueue_frame) and the greedy depformer cascade
+ * alone (on the last temporal output, starting from text_token). */
+BMO_API int bmo_enqueue_temporal(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos);
+BMO_API int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token);
+
 /* Waits for the handle's stream; returns the device status word (0 = ok). */
 BMO_API int bmo_sync(bmo_handle_t *h);
 
