@@ -67,6 +67,7 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
     cfg_.graphs = cfg.graphs && env_int("BMO_GRAPHS", 1) != 0;
     cfg_.pdl = cfg.pdl && env_int("BMO_PDL", 1) != 0;
+    cfg_.persistent = (cfg.persistent || env_int("BMO_PERSISTENT", 0) != 0) && env_int("BMO_PERSISTENT", 1) != 0;
     n_ctx = cfg.n_ctx > 0 ? cfg.n_ctx : 2048;
     if (n_ctx > attn_max_ctx()) throw std::runtime_error("n_ctx exceeds the ring limit of " + std::to_string(attn_max_ctx()));
     if (cfg.kv_type >= 0) {
@@ -77,6 +78,7 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     }
     load(gguf_path);
     alloc_state();
+    build_programs();
 }
 
 Engine::~Engine() {
@@ -504,16 +506,6 @@ void Engine::alloc_state() {
 // ---------------------------------------------------------------------------
 // enqueue sequences
 // ---------------------------------------------------------------------------
-int Engine::gemv_grid(const QMatDesc &m) const {
-    const long long nc = static_cast<long long>(m.n_tiles) * m.cpt;
-    long long g = std::min<long long>(sm_count, nc);
-    // keep the tiles one CTA touches within the shared-memory partial table
-    const long long need = (static_cast<long long>(m.n_tiles) + gemv_max_tiles_per_cta() - 3) /
-                           (gemv_max_tiles_per_cta() - 2);
-    g = std::max(g, std::min(need, nc));
-    return static_cast<int>(std::max<long long>(g, 1));
-}
-
 GemvArgs Engine::gemv_base(const QMatDesc &m) const {
     GemvArgs a{};
     a.W = m;
@@ -524,104 +516,114 @@ GemvArgs Engine::gemv_base(const QMatDesc &m) const {
     return a;
 }
 
-void Engine::gemv(const GemvArgs &a, int pro, int epi, cudaStream_t s) {
-    ck(launch_gemv(a, pro, epi, gemv_grid(a.W), s, cfg_.pdl), "launch gemv");
-}
-
-void Engine::enqueue_temporal(cudaStream_t s) {
-    ck(launch_embed(ttables_d_, n_ttables_, fin_d_->tokens, &fin_d_->n_tok, n_embd, resid_, &fin_d_->pos, rope_theta,
-                    head_dim, rope_, s),
-       "launch embed");
-    for (int l = 0; l < n_layers; ++l) enqueue_layer(s, l);
-    if (has_text_head) {
-        GemvArgs h = gemv_base(text_head_);
-        h.x = resid_ + static_cast<size_t>(n_layers) * n_embd;
-        h.gamma = out_norm_;
-        h.eps = norm_eps;
-        h.xn_out = z_;
-        h.y = logits_;
-        h.bias = text_bias_;
-        h.argmax_pairs = tpairs_;
-        h.argmax_limit = text_vocab;
-        gemv(h, out_norm_ ? kProNorm : kProPlain, kEpiLogits, s);
-    }
+static FramePhase gemv_op(const GemvArgs &g, int pro, int epi) {
+    FramePhase p{};
+    p.kind = kPhGemv;
+    p.pro = pro;
+    p.epi = epi;
+    p.g = g;
+    return p;
 }
 
 // One temporal layer (bmo_compute.cpp:2188-2640): reads resid[l], writes resid[l+1].
-void Engine::enqueue_layer(cudaStream_t s, int l) {
+void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     const int q_dim = n_heads * head_dim, kv_dim = n_kv_heads * head_dim;
-    {
-        float *x_in = resid_ + static_cast<size_t>(l) * n_embd;
-        float *x_out = x_in + n_embd;
-        const long long layer_off = static_cast<long long>(l) * n_kv_heads * n_ctx * head_dim;
+    float *x_in = resid_ + static_cast<size_t>(l) * n_embd;
+    float *x_out = x_in + n_embd;
+    const long long layer_off = static_cast<long long>(l) * n_kv_heads * n_ctx * head_dim;
 
-        GemvArgs a = gemv_base(L_[l].qkv);
-        a.x = x_in;
-        a.gamma = L_[l].norm1;
-        a.eps = norm_eps;
-        a.y = q_;
-        a.q_dim = q_dim;
-        a.kv_dim = kv_dim;
-        a.head_dim = head_dim;
-        a.rope_cs = rope_;
-        a.k_cache = k_cache_;
-        a.v_cache = v_cache_;
-        a.k_scale = k_scale_;
-        a.v_scale = v_scale_;
-        a.kv_type = kv_type;
-        a.n_ctx = n_ctx;
-        a.pos = &fin_d_->pos;
-        a.kv_layer_off = layer_off;
-        a.v_out = vraw_;
-        gemv(a, kProNorm, kEpiQKV, s);
+    GemvArgs a = gemv_base(L_[l].qkv);
+    a.x = x_in;
+    a.gamma = L_[l].norm1;
+    a.eps = norm_eps;
+    a.y = q_;
+    a.q_dim = q_dim;
+    a.kv_dim = kv_dim;
+    a.head_dim = head_dim;
+    a.rope_cs = rope_;
+    a.k_cache = k_cache_;
+    a.v_cache = v_cache_;
+    a.k_scale = k_scale_;
+    a.v_scale = v_scale_;
+    a.kv_type = kv_type;
+    a.n_ctx = n_ctx;
+    a.pos = &fin_d_->pos;
+    a.kv_layer_off = layer_off;
+    a.v_out = vraw_;
+    v.push_back(gemv_op(a, kProNorm, kEpiQKV));
 
-        AttnArgs at{};
-        at.q = q_;
-        at.v_raw = vraw_;
-        at.k_cache = k_cache_;
-        at.v_cache = v_cache_;
-        at.k_scale = k_scale_;
-        at.v_scale = v_scale_;
-        at.kv_layer_off = layer_off;
-        at.n_heads = n_heads;
-        at.n_kv_heads = n_kv_heads;
-        at.n_ctx = n_ctx;
-        at.kv_type = kv_type;
-        at.pos = &fin_d_->pos;
-        at.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
-        at.out = attn_;
-        at.status = status_;
-        ck(launch_attention(at, head_dim, attn_splits_, s, cfg_.pdl), "launch attention");
+    FramePhase at{};
+    at.kind = kPhAttn;
+    at.head_dim = head_dim;
+    at.splits = attn_splits_;
+    at.at.q = q_;
+    at.at.v_raw = vraw_;
+    at.at.k_cache = k_cache_;
+    at.at.v_cache = v_cache_;
+    at.at.k_scale = k_scale_;
+    at.at.v_scale = v_scale_;
+    at.at.kv_layer_off = layer_off;
+    at.at.n_heads = n_heads;
+    at.at.n_kv_heads = n_kv_heads;
+    at.at.n_ctx = n_ctx;
+    at.at.kv_type = kv_type;
+    at.at.pos = &fin_d_->pos;
+    at.at.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+    at.at.out = attn_;
+    at.at.status = status_;
+    v.push_back(at);
 
-        GemvArgs o = gemv_base(L_[l].wo);
-        o.x = attn_;
-        o.y = xmid_;
-        o.resid = x_in;
-        gemv(o, kProPlain, kEpiResid, s);
+    GemvArgs o = gemv_base(L_[l].wo);
+    o.x = attn_;
+    o.y = xmid_;
+    o.resid = x_in;
+    v.push_back(gemv_op(o, kProPlain, kEpiResid));
 
-        GemvArgs fi = gemv_base(L_[l].ffn_in);
-        fi.x = xmid_;
-        fi.gamma = L_[l].norm2;
-        fi.eps = norm_eps;
-        fi.y = act_;
-        gemv(fi, kProNorm, kEpiSwiGLU, s);
+    GemvArgs fi = gemv_base(L_[l].ffn_in);
+    fi.x = xmid_;
+    fi.gamma = L_[l].norm2;
+    fi.eps = norm_eps;
+    fi.y = act_;
+    v.push_back(gemv_op(fi, kProNorm, kEpiSwiGLU));
 
-        GemvArgs fo = gemv_base(L_[l].ffn_out);
-        fo.x = act_;
-        fo.y = x_out;
-        fo.resid = xmid_;
-        gemv(fo, kProPlain, kEpiResid, s);
-    }
+    GemvArgs fo = gemv_base(L_[l].ffn_out);
+    fo.x = act_;
+    fo.y = x_out;
+    fo.resid = xmid_;
+    v.push_back(gemv_op(fo, kProPlain, kEpiResid));
+}
+
+// Output norm, text logits and per-tile argmax (the greedy text token).
+void Engine::ops_text_head(std::vector<FramePhase> &v) const {
+    GemvArgs h = gemv_base(text_head_);
+    h.x = resid_ + static_cast<size_t>(n_layers) * n_embd;
+    h.gamma = out_norm_;
+    h.eps = norm_eps;
+    h.xn_out = z_;
+    h.y = logits_;
+    h.bias = text_bias_;
+    h.argmax_pairs = tpairs_;
+    h.argmax_limit = text_vocab;
+    v.push_back(gemv_op(h, out_norm_ ? kProNorm : kProPlain, kEpiLogits));
+}
+
+std::vector<FramePhase> Engine::ops_temporal() const {
+    std::vector<FramePhase> v;
+    for (int l = 0; l < n_layers; ++l) ops_layer(v, l);
+    if (has_text_head) ops_text_head(v);
+    return v;
 }
 
 // One depformer codebook step (bmo_build_depth_graph, bmo_compute.cpp:2741-3340).
-void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok) {
+// fold: the attention of all heads becomes the O-projection's prologue
+// (persistent kernel only).
+void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok, bool fold) const {
     GemvArgs w = gemv_base(dep_in_[cb]);
     w.x = z;
     w.y = dxa_;
     w.emb = cb == 0 ? dep_text_emb_ : dep_emb_[cb - 1];
     w.tok = tok;
-    gemv(w, kProPlain, kEpiEmbAdd, s);
+    v.push_back(gemv_op(w, kProPlain, kEpiEmbAdd));
     for (int i = 0; i < kDepLayers; ++i) {
         const long long layer_off = static_cast<long long>(i) * dep_heads * dep_n_ctx * dep_hd;
         GemvArgs a = gemv_base(D_[i].qkv[cb]);
@@ -640,7 +642,7 @@ void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const To
         a.pos = dep_pos_ + cb;
         a.kv_layer_off = layer_off;
         a.v_out = dvraw_;
-        gemv(a, kProNorm, kEpiQKV, s);
+        v.push_back(gemv_op(a, kProNorm, kEpiQKV));
 
         AttnArgs at{};
         at.q = dq_;
@@ -656,38 +658,50 @@ void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const To
         at.scale = 1.0f / std::sqrt(static_cast<float>(dep_hd));
         at.out = dattn_;
         at.status = status_;
-        ck(launch_attention(at, dep_hd, 1, s, cfg_.pdl), "launch depth attention");
 
         GemvArgs o = gemv_base(D_[i].wo[cb]);
         o.x = dattn_;
         o.y = dxb_;
         o.resid = dxa_;
-        gemv(o, kProPlain, kEpiResid, s);
+        if (fold) {
+            FramePhase op = gemv_op(o, kProDepAttn, kEpiResid);
+            op.at = at;
+            op.head_dim = dep_hd;
+            v.push_back(op);
+        } else {
+            FramePhase ap{};
+            ap.kind = kPhAttn;
+            ap.at = at;
+            ap.head_dim = dep_hd;
+            ap.splits = 1;
+            v.push_back(ap);
+            v.push_back(gemv_op(o, kProPlain, kEpiResid));
+        }
 
         GemvArgs fi = gemv_base(D_[i].ffn_in[cb]);
         fi.x = dxb_;
         fi.gamma = D_[i].norm2;
         fi.eps = norm_eps;
         fi.y = dact_;
-        gemv(fi, kProNorm, kEpiSwiGLU, s);
+        v.push_back(gemv_op(fi, kProNorm, kEpiSwiGLU));
 
         GemvArgs fo = gemv_base(D_[i].ffn_out[cb]);
         fo.x = dact_;
         fo.y = dxa_;
         fo.resid = dxb_;
-        gemv(fo, kProPlain, kEpiResid, s);
+        v.push_back(gemv_op(fo, kProPlain, kEpiResid));
     }
     GemvArgs h = gemv_base(dep_head_[cb]);
     h.x = dxa_;
     h.y = dlogits_ + static_cast<size_t>(cb) * audio_vocab;
     h.argmax_pairs = dpairs_ + static_cast<size_t>(cb) * dpairs_stride_;
     h.argmax_limit = std::min(audio_vocab, 2048);
-    gemv(h, kProPlain, kEpiLogits, s);
+    v.push_back(gemv_op(h, kProPlain, kEpiLogits));
 }
 
-void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
-    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
-    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
+// dep_q greedy steps, each step's token the argmax of the previous head,
+// then the last step's token.
+void Engine::ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first, bool fold) const {
     for (int cb = 0; cb < dep_q; ++cb) {
         TokenSrc t{};
         if (cb == 0) {
@@ -698,16 +712,144 @@ void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &fir
             t.n_pairs = dep_head_[cb - 1].n_tiles;
             t.tok_out = tok_out_ + cb;
         }
-        enqueue_depth_step(s, cb, z, t);
+        ops_depth_step(v, cb, z, t, fold);
     }
-    enqueue_finalize_tokens(s);
+    FramePhase f{};
+    f.kind = kPhTokenOut;
+    f.tok.pairs = dpairs_ + static_cast<size_t>(dep_q - 1) * dpairs_stride_;
+    f.tok.n_pairs = dep_head_[dep_q - 1].n_tiles;
+    f.tok.tok_out = tok_out_ + dep_q;
+    v.push_back(f);
 }
 
-void Engine::enqueue_finalize_tokens(cudaStream_t s) {
-    const int cb = dep_q - 1;
-    ck(launch_finalize_token(dpairs_ + static_cast<size_t>(cb) * dpairs_stride_, dep_head_[cb].n_tiles,
-                             tok_out_ + 1 + cb, s, cfg_.pdl),
-       "launch finalize");
+// Per-op path: one kernel per entry, chained by programmatic dependent launch.
+void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
+    for (const FramePhase &op : ops) {
+        switch (op.kind) {
+        case kPhGemv: {
+            if (op.pro != kProPlain && op.pro != kProNorm) throw std::runtime_error("internal: op needs the frame kernel");
+            const GemvPlan p = plan_gemv(op.g.W, sm_count);
+            GemvArgs b = op.g;
+            b.tile_aligned = p.tile_aligned;
+            ck(launch_gemv(b, op.pro, op.epi, p.grid, s, cfg_.pdl), "launch gemv");
+            break;
+        }
+        case kPhAttn: ck(launch_attention(op.at, op.head_dim, op.splits, s, cfg_.pdl), "launch attention"); break;
+        case kPhTokenOut:
+            ck(launch_finalize_token(op.tok.pairs, op.tok.n_pairs, op.tok.tok_out, s, cfg_.pdl), "launch finalize");
+            break;
+        default: throw std::runtime_error("internal: unknown op");
+        }
+    }
+}
+
+void Engine::enqueue_embed(cudaStream_t s) {
+    ck(launch_embed(ttables_d_, n_ttables_, fin_d_->tokens, &fin_d_->n_tok, n_embd, resid_, &fin_d_->pos, rope_theta,
+                    head_dim, rope_, s),
+       "launch embed");
+}
+
+void Engine::enqueue_temporal(cudaStream_t s) {
+    enqueue_embed(s);
+    enqueue_ops(s, ops_temporal());
+}
+
+void Engine::enqueue_layer(cudaStream_t s, int l) {
+    std::vector<FramePhase> v;
+    ops_layer(v, l);
+    enqueue_ops(s, v);
+}
+
+void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok) {
+    std::vector<FramePhase> v;
+    ops_depth_step(v, cb, z, tok, false);
+    enqueue_ops(s, v);
+}
+
+void Engine::reset_depth_kv_async(cudaStream_t s) {
+    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
+    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
+}
+
+void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
+    reset_depth_kv_async(s);
+    std::vector<FramePhase> v;
+    ops_cascade(v, z, first, false);
+    enqueue_ops(s, v);
+}
+
+// ---------------------------------------------------------------------------
+// persistent frame kernel programs
+// ---------------------------------------------------------------------------
+// Decides whether this model runs under the frame kernel and uploads its
+// programs.  Anything the kernel does not cover keeps the per-op path.
+void Engine::build_programs() {
+    persistent_ = false;
+    if (!cfg_.persistent || kv_type != kKvF16) return;
+    frame_grid_ = frame_max_grid();
+    if (frame_grid_ <= 0) return;
+    if (n_ctx > frame_max_window() || (head_dim != 64 && head_dim != 128) || n_heads > frame_grid_) return;
+    const bool dep = has_dep_tables && dep_dim > 0 && dep_q > 0;
+    if (dep && (dep_n_ctx > frame_dep_max_window() || dep_hd != frame_dep_head_dim() ||
+                dep_heads * dep_hd > frame_max_window()))
+        return;
+    auto fits = [&](const std::vector<FramePhase> &ops) {
+        for (const FramePhase &op : ops) {
+            if (op.kind != kPhGemv) continue;
+            const int tiles_per_cta = (op.g.W.n_tiles + frame_grid_ - 1) / frame_grid_;
+            if (tiles_per_cta > frame_max_tiles_per_cta() || op.g.W.nbx > gemv_max_nbx()) return false;
+            if (op.pro == kProNorm && op.g.W.cols > 8192) return false;
+            if ((reinterpret_cast<uintptr_t>(op.g.x) & 15) != 0) return false;
+        }
+        return true;
+    };
+    auto upload = [&](const std::vector<FramePhase> &ops, DevProgram &p) {
+        const size_t bytes = sizeof(FramePhase) * ops.size();
+        FramePhase *d = nullptr;
+        ck(cudaMalloc(&d, bytes), "program alloc");
+        allocs_.push_back(d);
+        ck(cudaMemcpy(d, ops.data(), bytes, cudaMemcpyHostToDevice), "program upload");
+        p.d = d;
+        p.n = static_cast<int>(ops.size());
+    };
+    const std::vector<FramePhase> temporal = ops_temporal();
+    std::vector<FramePhase> casc_z, casc_dz, frame = temporal;
+    if (dep) {
+        TokenSrc prev{};
+        prev.tok = &fin_d_->prev_token;
+        ops_cascade(casc_z, z_, prev, true);
+        ops_cascade(casc_dz, dz_, prev, true);
+        if (has_text_head) {
+            TokenSrc tp{};
+            tp.pairs = tpairs_;
+            tp.n_pairs = text_head_.n_tiles;
+            ops_cascade(frame, z_, tp, true);
+        }
+    }
+    if (!fits(temporal) || !fits(casc_z) || !fits(casc_dz) || !fits(frame)) return;
+    ck(cudaMalloc(&fbar_, 2 * sizeof(unsigned)), "barrier alloc");
+    allocs_.push_back(fbar_);
+    upload(temporal, prog_temporal_);
+    if (dep) {
+        upload(casc_z, prog_cascade_z_);
+        upload(casc_dz, prog_cascade_dz_);
+        if (has_text_head) upload(frame, prog_frame_);
+    }
+    persistent_ = true;
+}
+
+void Engine::enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal) {
+    if (!p.d) throw std::runtime_error("internal: missing frame program");
+    ck(cudaMemsetAsync(fbar_, 0, 2 * sizeof(unsigned), s), "barrier reset");
+    FrameArgs fa{};
+    fa.prog = p.d;
+    fa.n_phases = p.n;
+    fa.bar = fbar_;
+    fa.abort = reinterpret_cast<int *>(fbar_ + 1);
+    fa.status = status_;
+    fa.rope = temporal ? rope_ : nullptr;
+    fa.rope_pairs = temporal ? head_dim / 2 : 0;
+    ck(launch_frame(fa, frame_grid_, s), "launch frame kernel");
 }
 
 cudaGraphExec_t Engine::capture(const std::function<void(cudaStream_t)> &fn) {
@@ -747,7 +889,11 @@ void Engine::finish_call() {
         cudaMemsetAsync(status_, 0, sizeof(int), stream);
         cudaMemsetAsync(gcount_, 0, gcount_bytes_, stream);
         cudaStreamSynchronize(stream);
-        throw std::runtime_error("device status " + std::to_string(st) + ": a bulk copy wait timed out");
+        std::string what;
+        if (st & (1 << 1)) what += " a bulk copy wait timed out;";
+        if (st & (1 << 2)) what += " launch arguments inconsistent with the weight layout;";
+        if (st & (1 << 3)) what += " a grid barrier timed out;";
+        throw std::runtime_error("device status " + std::to_string(st) + ":" + what);
     }
 }
 
@@ -761,7 +907,12 @@ void Engine::run_temporal(const int32_t *tokens, int K, int pos) {
     fin_h_->n_tok = K;
     fin_h_->pos = pos;
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+    if (persistent_) {
+        enqueue_embed(stream);
+        enqueue_program(stream, prog_temporal_, true);
+    } else {
+        launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+    }
     ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
     if (has_text_head)
         ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
@@ -810,10 +961,7 @@ void Engine::run_depth(int cb, int32_t prev, const float *z) {
     ck(cudaMemcpyAsync(dz_, zin_h_, sizeof(float) * n_embd, cudaMemcpyHostToDevice, stream), "z in copy");
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
     launch(g_depth_[cb], [this, cb](cudaStream_t s) {
-        if (cb == 0) {
-            ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
-            ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
-        }
+        if (cb == 0) reset_depth_kv_async(s);
         TokenSrc t{};
         t.tok = &fin_d_->prev_token;
         enqueue_depth_step(s, cb, dz_, t);
@@ -830,11 +978,16 @@ void Engine::run_cascade_greedy(int32_t text_tok, const float *z, int32_t *out_t
     fin_h_->prev_token = text_tok;
     ck(cudaMemcpyAsync(dz_, zin_h_, sizeof(float) * n_embd, cudaMemcpyHostToDevice, stream), "z in copy");
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    launch(g_cascade_, [this](cudaStream_t s) {
-        TokenSrc t{};
-        t.tok = &fin_d_->prev_token;
-        enqueue_cascade(s, dz_, t);
-    });
+    if (persistent_) {
+        reset_depth_kv_async(stream);
+        enqueue_program(stream, prog_cascade_dz_, false);
+    } else {
+        launch(g_cascade_, [this](cudaStream_t s) {
+            TokenSrc t{};
+            t.tok = &fin_d_->prev_token;
+            enqueue_cascade(s, dz_, t);
+        });
+    }
     ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
     finish_call();
     for (int cb = 0; cb < dep_q; ++cb) out_tokens[cb] = tok_h_[1 + cb];
@@ -847,13 +1000,19 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
     fin_h_->n_tok = K;
     fin_h_->pos = pos;
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    launch(g_frame_, [this](cudaStream_t s) {
-        enqueue_temporal(s);
-        TokenSrc t{};
-        t.pairs = tpairs_;
-        t.n_pairs = text_head_.n_tiles;
-        enqueue_cascade(s, z_, t);
-    });
+    if (persistent_ && prog_frame_.d) {
+        enqueue_embed(stream);
+        reset_depth_kv_async(stream);
+        enqueue_program(stream, prog_frame_, true);
+    } else {
+        launch(g_frame_, [this](cudaStream_t s) {
+            enqueue_temporal(s);
+            TokenSrc t{};
+            t.pairs = tpairs_;
+            t.n_pairs = text_head_.n_tiles;
+            enqueue_cascade(s, z_, t);
+        });
+    }
     ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
     ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
     ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
@@ -866,13 +1025,19 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
 void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
-    launch(g_frame_, [this](cudaStream_t s) {
-        enqueue_temporal(s);
-        TokenSrc t{};
-        t.pairs = tpairs_;
-        t.n_pairs = text_head_.n_tiles;
-        enqueue_cascade(s, z_, t);
-    });
+    if (persistent_ && prog_frame_.d) {
+        enqueue_embed(stream);
+        reset_depth_kv_async(stream);
+        enqueue_program(stream, prog_frame_, true);
+    } else {
+        launch(g_frame_, [this](cudaStream_t s) {
+            enqueue_temporal(s);
+            TokenSrc t{};
+            t.pairs = tpairs_;
+            t.n_pairs = text_head_.n_tiles;
+            enqueue_cascade(s, z_, t);
+        });
+    }
     if (out_tokens_dev)
         ck(cudaMemcpyAsync(out_tokens_dev, tok_out_, sizeof(int) * (1 + dep_q), cudaMemcpyDeviceToDevice, stream),
            "tokens copy");
@@ -881,17 +1046,27 @@ void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int
 void Engine::enqueue_temporal_device(const int32_t *tokens_dev, int K, int pos) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
-    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+    if (persistent_) {
+        enqueue_embed(stream);
+        enqueue_program(stream, prog_temporal_, true);
+    } else {
+        launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
+    }
 }
 
 void Engine::enqueue_cascade_device(int32_t text_token) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_int(&fin_d_->prev_token, text_token, stream), "set token");
-    launch(g_cascade_z_, [this](cudaStream_t s) {
-        TokenSrc t{};
-        t.tok = &fin_d_->prev_token;
-        enqueue_cascade(s, z_, t);
-    });
+    if (persistent_) {
+        reset_depth_kv_async(stream);
+        enqueue_program(stream, prog_cascade_z_, false);
+    } else {
+        launch(g_cascade_z_, [this](cudaStream_t s) {
+            TokenSrc t{};
+            t.tok = &fin_d_->prev_token;
+            enqueue_cascade(s, z_, t);
+        });
+    }
 }
 
 int Engine::sync_status() {
@@ -907,27 +1082,24 @@ void Engine::capture_all() {
         return;
     }
     auto temporal = [this](cudaStream_t s) { enqueue_temporal(s); };
-    if (!g_temporal_) g_temporal_ = capture(temporal);
+    if (!g_temporal_ && !persistent_) g_temporal_ = capture(temporal);
     if (has_dep_tables && dep_dim > 0) {
         for (int cb = 0; cb < dep_q; ++cb) {
             if (g_depth_[cb]) continue;
             g_depth_[cb] = capture([this, cb](cudaStream_t s) {
-                if (cb == 0) {
-                    ck(cudaMemsetAsync(dk_cache_, 0, dkv_bytes_, s), "reset depth kv");
-                    ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
-                }
+                if (cb == 0) reset_depth_kv_async(s);
                 TokenSrc t{};
                 t.tok = &fin_d_->prev_token;
                 enqueue_depth_step(s, cb, dz_, t);
             });
         }
-        if (!g_cascade_)
+        if (!g_cascade_ && !persistent_)
             g_cascade_ = capture([this](cudaStream_t s) {
                 TokenSrc t{};
                 t.tok = &fin_d_->prev_token;
                 enqueue_cascade(s, dz_, t);
             });
-        if (!g_frame_ && has_text_head)
+        if (!g_frame_ && has_text_head && !persistent_)
             g_frame_ = capture([this](cudaStream_t s) {
                 enqueue_temporal(s);
                 TokenSrc t{};

@@ -7,7 +7,9 @@
 //   depth[cb]     one depformer step (reference bmo_forward_depth)
 //   cascade       dep_q depformer steps with greedy argmax chaining on device
 //   frame         temporal + greedy text token + cascade
-// Kernels are chained with programmatic dependent launch inside each graph.
+// Two execution paths run the same op lists: one kernel per op chained with
+// programmatic dependent launch inside CUDA graphs, or (default where the
+// model fits) the persistent frame kernel running the list as a program.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -33,6 +35,7 @@ struct EngineConfig {
     int kv_type = -1;  // < 0: BMO_KV_TYPE or fp16
     bool graphs = true;
     bool pdl = true;
+    bool persistent = false;  // run frames as one persistent kernel where the model allows
 };
 
 // Per-call inputs, copied to the device in one transfer.
@@ -86,6 +89,7 @@ public:
     int debug_tap(int which, float *out, int max_floats);
     void capture_all();
     bool graphs_captured() const { return graphs_ready_; }
+    bool persistent() const { return persistent_; }
 
 private:
     struct Layer {
@@ -103,15 +107,29 @@ private:
     QMatDesc upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t row0, int64_t rows);
     float *upload_f32(const GgufTensor *t, int64_t n);
     EmbTable upload_table(const GgufTensor *t);
-    int gemv_grid(const QMatDesc &m) const;
     GemvArgs gemv_base(const QMatDesc &m) const;
-    void gemv(const GemvArgs &a, int pro, int epi, cudaStream_t s);
 
+    // a frame's steps as op lists (layout.h FramePhase)
+    void ops_layer(std::vector<FramePhase> &v, int l) const;
+    void ops_text_head(std::vector<FramePhase> &v) const;
+    std::vector<FramePhase> ops_temporal() const;
+    void ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok, bool fold) const;
+    void ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first, bool fold) const;
+    // per-op path
+    void enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops);
+    void enqueue_embed(cudaStream_t s);
     void enqueue_temporal(cudaStream_t s);
     void enqueue_layer(cudaStream_t s, int l);
     void enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok);
     void enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first);
-    void enqueue_finalize_tokens(cudaStream_t s);
+    void reset_depth_kv_async(cudaStream_t s);
+    // persistent path
+    struct DevProgram {
+        FramePhase *d = nullptr;
+        int n = 0;
+    };
+    void build_programs();
+    void enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal);
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)> &fn);
     void launch(cudaGraphExec_t &g, const std::function<void(cudaStream_t)> &fn);
     void finish_call();
@@ -168,6 +186,12 @@ private:
     cudaGraphExec_t g_layers_ = nullptr, g_cascade_z_ = nullptr;
     int g_layers_range_[2] = {-1, -1};
     bool graphs_ready_ = false;
+
+    // persistent frame kernel
+    bool persistent_ = false;
+    int frame_grid_ = 0;
+    unsigned *fbar_ = nullptr;  // [grid barrier counter, abort flag]
+    DevProgram prog_temporal_, prog_cascade_z_, prog_cascade_dz_, prog_frame_;
 };
 
 }  // namespace bmo

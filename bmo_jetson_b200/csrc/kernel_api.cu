@@ -93,6 +93,8 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
         return static_cast<int>(cudaErrorInvalidValue);
     if (scratch_bytes < bmo_k_gemv_scratch_bytes(rows, cols, perm, swiglu_f)) return static_cast<int>(cudaErrorInvalidValue);
     if (cols / 32 > gemv_max_nbx() * kChunkBlocks) return static_cast<int>(cudaErrorInvalidValue);
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (reinterpret_cast<uintptr_t>(xn_out_dev) & 15))
+        return static_cast<int>(cudaErrorInvalidValue);
     const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
     GemvArgs a{};
     a.W = m;
@@ -113,10 +115,18 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
     cudaGetDevice(&dev);
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    long long g = grid > 0 ? grid : (nc < sms ? nc : sms);
-    const long long need = (m.n_tiles + gemv_max_tiles_per_cta() - 3) / (gemv_max_tiles_per_cta() - 2);
-    if (g < need) g = need < nc ? need : nc;
-    if (g > nc) g = nc;
+    long long g;
+    if (grid > 0) {  // caller-chosen grid: even (stream-K) split
+        g = grid;
+        const long long need = (m.n_tiles + gemv_max_tiles_per_cta() - 3) / (gemv_max_tiles_per_cta() - 2);
+        if (g < need) g = need < nc ? need : nc;
+        if (g > nc) g = nc;
+        a.tile_aligned = 0;
+    } else {
+        const GemvPlan p = plan_gemv(m, sms);
+        g = p.grid;
+        a.tile_aligned = p.tile_aligned;
+    }
     const int pro = gamma_dev ? kProNorm : kProPlain;
     const int epi = perm == kPermSwiGLU ? kEpiSwiGLU : (resid_dev ? kEpiResid : kEpiStore);
     return static_cast<int>(launch_gemv(a, pro, epi, static_cast<int>(g), static_cast<cudaStream_t>(stream), false));

@@ -34,20 +34,27 @@ constexpr int kAttnMaxSplits = 8;     // portable cluster size
 constexpr int kAttnMaxPos = 1024;     // window positions per split
 constexpr int kAttnMaxCtx = kAttnMaxSplits * kAttnMaxPos;
 
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kAttnPosPerWarp = 4;  // positions one warp scores at a time (independent accumulators)
+
 template <int HD, bool Q4>
 struct AttnSmem {
     static constexpr int kRowBytes = Q4 ? HD / 2 : HD * 2;
     static constexpr int kScales = Q4 ? HD / 32 : 1;
+    static constexpr int kGroups = kAttnThreads / HD;  // position groups of the weighted sum
     uint64_t kbar, vbar;
     alignas(128) uint8_t k[kAttnSub][kRowBytes];
     alignas(128) uint8_t v[kAttnSub][kRowBytes];
     __half kd[kAttnSub][kScales];
     __half vd[kAttnSub][kScales];
     float q[HD];
-    float s[kAttnMaxPos];  // scores, then p
-    double o_part[HD];
-    double l_part;
-    float m_local;
+    float s[kAttnMaxPos];                // scores, then p
+    float wmax[kAttnWarps];
+    float m_rank[kAttnMaxSplits];        // every split's local maximum (pushed by the owner)
+    double o_grp[kGroups][HD];
+    double l_warp;
+    double o_rank[kAttnMaxSplits][HD];   // rank 0: every split's partial output (pushed)
+    double l_rank[kAttnMaxSplits];
 };
 
 template <int HD, bool Q4>
@@ -129,6 +136,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
         fence_barrier_init();
     }
     __syncthreads();
+    // Every CTA of the cluster must be running before any writes into its
+    // shared memory: arrive now, wait just before the first remote store.
+    cluster_arrive_relaxed();
     pdl_launch_dependents();
     uint32_t kphase = 0, vphase = 0;
     const bool prefetched = (nsub == 1);
@@ -146,72 +156,129 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
             mbar_wait(&S.kbar, 0);
             mbar_wait(&S.vbar, 0);
         }
+        cluster_wait();
         return;
     }
     bool ok = true;
-    for (int d = tid; d < HD; d += kAttnThreads) S.q[d] = a.q[h * HD + d];
+    // q and (single-sub splits) the newest K/V rows: one memory round trip
+    for (int d = tid; d < HD; d += kAttnThreads) S.q[d] = __ldcg(a.q + h * HD + d);
+    const bool newest_here = n > 0 && i0 + n == window;
+    if (prefetched && newest_here) {
+        load_newest(S.k, S.kd, kc, kdc, n - 1);
+        load_newest(S.v, S.vd, vc, vdc, n - 1);
+    }
+    __syncthreads();
+    float qr[HD / 32];
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) qr[i] = S.q[lane + 32 * i];
 
-    // ---- pass 1: scores of this split ----
+    // ---- pass 1: scores of this split, kAttnPosPerWarp positions per warp at a time ----
     for (int sub = 0; sub < nsub; ++sub) {
         const int j0 = sub * kAttnSub, nj = min(kAttnSub, n - j0);
-        if (!prefetched) stage(S.k, S.kd, kc, kdc, &S.kbar, j0, nj);
-        if (i0 + j0 + nj == window) load_newest(S.k, S.kd, kc, kdc, nj - 1);
+        if (!prefetched) {
+            stage(S.k, S.kd, kc, kdc, &S.kbar, j0, nj);
+            if (i0 + j0 + nj == window) load_newest(S.k, S.kd, kc, kdc, nj - 1);
+        }
         ok &= mbar_wait(&S.kbar, kphase);
         kphase ^= 1u;
         __syncthreads();
-        for (int j = warp; j < nj; j += kAttnThreads / 32) {
-            double dot = 0.0;
+        for (int jb = warp * kAttnPosPerWarp; jb < nj; jb += kAttnThreads / 32 * kAttnPosPerWarp) {
+            double dot[kAttnPosPerWarp];
 #pragma unroll
-            for (int d = lane; d < HD; d += 32)
-                dot = fma(static_cast<double>(S.q[d]), static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], d)), dot);
+            for (int u = 0; u < kAttnPosPerWarp; ++u) {
+                const int j = min(jb + u, nj - 1);
+                dot[u] = 0.0;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            if (lane == 0) S.s[j0 + j] = __fmul_rn(__double2float_rn(dot), a.scale);
-        }
-        __syncthreads();
-    }
-    float m = -INFINITY;
-    for (int j = 0; j < n; ++j) m = fmaxf(m, S.s[j]);
-    if (tid == 0) S.m_local = m;
-    cluster.sync();
-    float M = -INFINITY;
-    for (int r = 0; r < nsp; ++r) M = fmaxf(M, *cluster.map_shared_rank(&S.m_local, r));
-
-    // ---- pass 2: p = exp(s - M), partial sums in double ----
-    for (int j = tid; j < n; j += kAttnThreads)
-        S.s[j] = __double2float_rn(exp(static_cast<double>(__fsub_rn(S.s[j], M))));
-    __syncthreads();
-    static_assert(HD <= kAttnThreads, "one thread per output dimension");
-    double o = 0.0, l = 0.0;
-    for (int sub = 0; sub < nsub; ++sub) {
-        const int j0 = sub * kAttnSub, nj = min(kAttnSub, n - j0);
-        if (!prefetched) stage(S.v, S.vd, vc, vdc, &S.vbar, j0, nj);
-        if (i0 + j0 + nj == window) load_newest(S.v, S.vd, vc, vdc, nj - 1);
-        ok &= mbar_wait(&S.vbar, vphase);
-        vphase ^= 1u;
-        __syncthreads();
-        if (tid < HD) {
-            for (int j = 0; j < nj; ++j) {
-                const double p = static_cast<double>(S.s[j0 + j]);
-                o = fma(p, static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], tid)), o);
-                if (tid == 0) l += p;
+                for (int i = 0; i < HD / 32; ++i)
+                    dot[u] = fma(static_cast<double>(qr[i]),
+                                 static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], lane + 32 * i)), dot[u]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < kAttnPosPerWarp; ++u) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], o);
+            if (lane < kAttnPosPerWarp && jb + lane < nj) {
+                double mine = dot[0];
+#pragma unroll
+                for (int u = 1; u < kAttnPosPerWarp; ++u) mine = lane == u ? dot[u] : mine;
+                S.s[j0 + jb + lane] = __fmul_rn(__double2float_rn(mine), a.scale);
             }
         }
         __syncthreads();
     }
-    if (tid < HD) S.o_part[tid] = o;
-    if (tid == 0) S.l_part = l;
+    // local maximum, pushed into every split's shared memory
+    float m = -INFINITY;
+    for (int j = tid; j < n; j += kAttnThreads) m = fmaxf(m, S.s[j]);
+    m = warp_max(m);
+    if (lane == 0) S.wmax[warp] = m;
+    __syncthreads();
+    cluster_wait();
+    if (tid < nsp) {
+        float mm = S.wmax[0];
+#pragma unroll
+        for (int w = 1; w < kAttnWarps; ++w) mm = fmaxf(mm, S.wmax[w]);
+        cluster.map_shared_rank(S.m_rank, tid)[sp] = mm;
+    }
+    cluster.sync();
+    float M = S.m_rank[0];
+    for (int r = 1; r < nsp; ++r) M = fmaxf(M, S.m_rank[r]);
+
+    // ---- pass 2: p = exp(s - M), weighted sums in double ----
+    for (int j = tid; j < n; j += kAttnThreads)
+        S.s[j] = __double2float_rn(exp(static_cast<double>(__fsub_rn(S.s[j], M))));
+    __syncthreads();
+    static_assert(kAttnThreads % HD == 0, "threads cover the output dimensions");
+    constexpr int kG = Smem::kGroups;
+    const int dim = tid % HD, grp = tid / HD;
+    double o4[4] = {0.0, 0.0, 0.0, 0.0};
+    double l = 0.0;
+    for (int sub = 0; sub < nsub; ++sub) {
+        const int j0 = sub * kAttnSub, nj = min(kAttnSub, n - j0);
+        if (!prefetched) {
+            stage(S.v, S.vd, vc, vdc, &S.vbar, j0, nj);
+            if (i0 + j0 + nj == window) load_newest(S.v, S.vd, vc, vdc, nj - 1);
+        }
+        ok &= mbar_wait(&S.vbar, vphase);
+        vphase ^= 1u;
+        __syncthreads();
+        auto pv = [&](int j) {
+            return static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], dim));
+        };
+        int j = grp;
+        for (; j + 3 * kG < nj; j += 4 * kG) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) o4[u] = fma(static_cast<double>(S.s[j0 + j + u * kG]), pv(j + u * kG), o4[u]);
+        }
+        for (; j < nj; j += kG) o4[0] = fma(static_cast<double>(S.s[j0 + j]), pv(j), o4[0]);
+        if (warp == kAttnWarps - 1)
+            for (int j = lane; j < nj; j += 32) l += static_cast<double>(S.s[j0 + j]);
+        __syncthreads();
+    }
+    S.o_grp[grp][dim] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    if (warp == kAttnWarps - 1) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) S.l_warp = l;
+    }
     if (!ok && tid == 0) raise_error(a.status, kErrTmaTimeout);
+    __syncthreads();
+    // push this split's partials into rank 0's shared memory
+    if (tid < HD) {
+        double ot = S.o_grp[0][tid];
+#pragma unroll
+        for (int g = 1; g < kG; ++g) ot += S.o_grp[g][tid];
+        cluster.map_shared_rank(&S.o_rank[0][0], 0)[sp * HD + tid] = ot;
+    }
+    if (tid == 0) cluster.map_shared_rank(S.l_rank, 0)[sp] = S.l_warp;
     cluster.sync();
     if (sp == 0 && tid < HD) {
         double ot = 0.0, lt = 0.0;
         for (int r = 0; r < nsp; ++r) {
-            ot += cluster.map_shared_rank(S.o_part, r)[tid];
-            lt += *cluster.map_shared_rank(&S.l_part, r);
+            ot += S.o_rank[r][tid];
+            lt += S.l_rank[r];
         }
         a.out[h * HD + tid] = __double2float_rn(__ddiv_rn(ot, lt));
     }
-    cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
 template <int HD, bool Q4>

@@ -11,17 +11,23 @@
 // writes them and summed in double, rounded once to fp32 -- the same value
 // the CPU oracle computes, whatever the split of the work.
 //
-// Design (B200): one CTA per SM, 8 warps.  The weight stream is the only
-// HBM traffic that matters, so each warp keeps kRing 4.6 KB chunks in flight
-// through the TMA bulk-copy engine into a private shared-memory ring.  The
-// first chunks are issued before griddepcontrol.wait, so under programmatic
-// dependent launch the stream starts while the previous kernel finishes.
-// Work is split "stream-K" style: CTA c owns a contiguous range of
-// (row tile, chunk) units, tiles that straddle CTAs are finished by the last
+// Design (B200): one CTA of 8 warps per SM, sized (registers <= 128, shared
+// memory < half an SM) so that the NEXT kernel's CTA is resident beside it.
+// The weight stream is the only HBM traffic that matters, so each warp keeps
+// kRing 4.6 KB chunks in flight through the TMA bulk-copy engine into a
+// private shared-memory ring.  The first chunks (and the RMSNorm weight) are
+// issued before griddepcontrol.wait, so under programmatic dependent launch
+// they stream while the previous kernel finishes; after the wait the
+// activation costs a single memory round trip.
+// Work split: normally each CTA owns whole row tiles (no cross-CTA traffic);
+// where that balances badly, CTA c owns an even range of (row tile, chunk)
+// units ("stream-K") and tiles that straddle CTAs are finished by the last
 // owner to arrive (per-tile counter, fixed summation order, deterministic).
 // Epilogues fuse RoPE + KV-ring append, SwiGLU, residual adds, logits +
 // argmax and the depformer embedding add.
-#include "common.cuh"
+#include <algorithm>
+
+#include "gemv_dev.cuh"
 #include "../launch.h"
 
 namespace bmo {
@@ -32,15 +38,25 @@ namespace bmo {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRing = BMO_GEMV_RING;  // chunks in flight per warp
-constexpr int kMaxNbx = 384;  // activations up to 12288 elements
+constexpr int kMaxNbx = 384;  // activations up to 12288 elements (at most two blocks per thread)
 constexpr int kMaxTilesPerCta = 10;
+constexpr int kMaxNormCols = kMaxTilesPerCta * kWarps * 32 * 2;  // RMSNorm weight staged in `part`'s space
+// A cross-CTA combine (partial store, release, acquire, reload) costs about as
+// long as one SM streaming this many chunks.
+constexpr int kCombineChunks = 12;
 
+// Kept under half of an SM's shared memory so that the next kernel's CTA fits
+// beside this one under programmatic dependent launch and prefetches its weights.
 struct GemvSmem {
     uint64_t bar[kWarps][kRing];
+    uint64_t gbar;  // RMSNorm weight bulk copy
     alignas(128) uint8_t ring[kWarps][kRing][kChunkBytes];
     alignas(16) int8_t xq[kMaxNbx * 32];
     float2 xds[kMaxNbx];  // (d8, 4 * s8) of each Q8_1 block
-    double part[kMaxTilesPerCta][kWarps][32];
+    union {
+        alignas(16) double part[kMaxTilesPerCta][kWarps][32];  // main loop and epilogue
+        float gamma[kMaxNormCols];                               // prologue only
+    };
     double red[kWarps];
     float tok_v[kWarps];
     int tok_i[kWarps];
@@ -50,179 +66,35 @@ struct GemvSmem {
 size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
 int gemv_max_tiles_per_cta() { return kMaxTilesPerCta; }
 int gemv_max_nbx() { return kMaxNbx; }
+int gemv_max_norm_cols() { return kMaxNormCols; }
 
 __device__ __forceinline__ int cta_of_chunk(long long k, long long nc, int g) {
     return static_cast<int>(((k + 1) * g - 1) / nc);
 }
 
-// One half-block term of the reference: d4 * ((float)sumi * d8 - 4 * s8).
-__device__ __forceinline__ float half_term(int sumi, float d4, float2 ds) {
-    return __fmul_rn(d4, __fsub_rn(__fmul_rn(static_cast<float>(sumi), ds.x), ds.y));
-}
-
-// Dot product of one 8-block chunk (32 rows, lane = row) with the activation.
-__device__ __forceinline__ double chunk_dot(const uint8_t *ch, const int8_t *xq, const float2 *xds, int lane) {
-    double acc = 0.0;
-#pragma unroll
-    for (int blk = 0; blk < kChunkBlocks; ++blk) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(ch + blk * 512 + lane * 16);
-        const float d4 = __half2float(*reinterpret_cast<const __half *>(ch + kChunkQsBytes + blk * 64 + lane * 2));
-        const int4 xa = *reinterpret_cast<const int4 *>(xq + blk * 32);
-        const int4 xb = *reinterpret_cast<const int4 *>(xq + blk * 32 + 16);
-        const float2 ds = xds[blk];
-        // byte j holds element j (low nibble) and element j+16 (high nibble);
-        // bytes 0-7 form the first half block, bytes 8-15 the second
-        int lo = __dp4a(static_cast<int>(w.x & 0x0F0F0F0Fu), xa.x, 0);
-        lo = __dp4a(static_cast<int>((w.x >> 4) & 0x0F0F0F0Fu), xb.x, lo);
-        lo = __dp4a(static_cast<int>(w.y & 0x0F0F0F0Fu), xa.y, lo);
-        lo = __dp4a(static_cast<int>((w.y >> 4) & 0x0F0F0F0Fu), xb.y, lo);
-        int hi = __dp4a(static_cast<int>(w.z & 0x0F0F0F0Fu), xa.z, 0);
-        hi = __dp4a(static_cast<int>((w.z >> 4) & 0x0F0F0F0Fu), xb.z, hi);
-        hi = __dp4a(static_cast<int>(w.w & 0x0F0F0F0Fu), xa.w, hi);
-        hi = __dp4a(static_cast<int>((w.w >> 4) & 0x0F0F0F0Fu), xb.w, hi);
-        acc += static_cast<double>(half_term(lo, d4, ds));
-        acc += static_cast<double>(half_term(hi, d4, ds));
-    }
-    return acc;
-}
-
-// ---- embedding element fetch (ggml to_float for the supported types) ----
-__device__ __forceinline__ float emb_elem(const EmbTable &e, int tok, int i) {
-    const uint8_t *row = static_cast<const uint8_t *>(e.data) + static_cast<size_t>(tok) * e.row_bytes;
-    switch (e.type) {
-    case kTF32: return reinterpret_cast<const float *>(row)[i];
-    case kTF16: return __half2float(reinterpret_cast<const __half *>(row)[i]);
-    case kTBF16: return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t *>(row)[i]) << 16);
-    case kTQ4_0: {
-        const uint8_t *b = row + (i >> 5) * 18;
-        const float d = __half2float(*reinterpret_cast<const __half *>(b));
-        const int j = i & 31;
-        const int nib = j < 16 ? (b[2 + j] & 0x0F) : (b[2 + j - 16] >> 4);
-        return __fmul_rn(static_cast<float>(nib - 8), d);
-    }
-    case kTQ8_0: {
-        const uint8_t *b = row + (i >> 5) * 34;
-        const float d = __half2float(*reinterpret_cast<const __half *>(b));
-        return __fmul_rn(static_cast<float>(static_cast<int8_t>(b[2 + (i & 31)])), d);
-    }
-    default: return 0.0f;
-    }
-}
-
-// (value, index) max with the lowest index winning ties (first maximum).
-__device__ __forceinline__ void argmax_merge(float &v, int &i, float ov, int oi) {
-    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
-}
-
-// Resolves the token of an embedding lookup (whole CTA participates).
-__device__ int resolve_token(const TokenSrc &src, float *red_v, int *red_i) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (!src.pairs) return src.tok ? *src.tok : -1;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int p = tid; p < src.n_pairs; p += blockDim.x) {
-        const float2 pr = __ldcg(&src.pairs[p]);
-        argmax_merge(bv, bi, pr.x, __float_as_int(pr.y));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        argmax_merge(bv, bi, ov, oi);
-    }
-    if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
-    __syncthreads();
-    float fv = red_v[0];
-    int fi = red_i[0];
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) argmax_merge(fv, fi, red_v[w], red_i[w]);
-    __syncthreads();
-    return fi;
-}
-
-template <int EPI>
-__device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane, float v, int tok) {
-    const int r = t * kTileRows + lane;
-    if constexpr (EPI == kEpiStore) {
-        if (r < a.W.rows) a.y[r] = a.bias ? __fadd_rn(v, a.bias[r]) : v;
-    } else if constexpr (EPI == kEpiResid) {
-        if (r < a.W.rows) a.y[r] = __fadd_rn(a.resid[r], v);
-    } else if constexpr (EPI == kEpiSwiGLU) {
-        // silu(gate) * up (swiglu_split_kernel, bmo_cuda_kernels.cu:370-387),
-        // exp evaluated in double and rounded once
-        const float up = __shfl_down_sync(0xffffffffu, v, 16);
-        const int h = t * 16 + lane;
-        if (lane < 16 && h < a.W.swiglu_f) {
-            const float e = __double2float_rn(exp(-static_cast<double>(v)));
-            const float silu = __fdiv_rn(v, __fadd_rn(1.0f, e));
-            a.y[h] = __fmul_rn(silu, up);
-        }
-    } else if constexpr (EPI == kEpiLogits) {
-        float val = -INFINITY;
-        if (r < a.W.rows) {
-            val = a.bias ? __fadd_rn(v, a.bias[r]) : v;
-            a.y[r] = val;
-        }
-        float bv = (r < a.W.rows && r < a.argmax_limit) ? val : -INFINITY;
-        int bi = r;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            argmax_merge(bv, bi, ov, oi);
-        }
-        if (lane == 0 && a.argmax_pairs) a.argmax_pairs[t] = make_float2(bv, __int_as_float(bi));
-    } else if constexpr (EPI == kEpiEmbAdd) {
-        if (r < a.W.rows) {
-            const bool ok = tok >= 0 && tok < a.emb.rows && a.emb.dim == a.W.rows;
-            a.y[r] = ok ? __fadd_rn(v, emb_elem(a.emb, tok, r)) : __fadd_rn(v, 0.0f);
-        }
-    } else if constexpr (EPI == kEpiQKV) {
-        // whole tile lies inside one head of q, k or v (head_dim % 32 == 0)
-        const int hd = a.head_dim;
-        float out = v;
-        const bool is_q = r < a.q_dim;
-        const bool is_k = !is_q && r < a.q_dim + a.kv_dim;
-        if ((is_q || is_k) && a.rope_cs) {
-            // interleaved RoPE (rope_interleaved_kernel, :317-368), separately rounded
-            const int d = (is_q ? r : r - a.q_dim) % hd;
-            const float2 cs = a.rope_cs[d >> 1];
-            const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-            out = (lane & 1) ? __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x))
-                             : __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
-        }
-        if (is_q) {
-            a.y[r] = out;
-            return;
-        }
-        const int rr = is_k ? r - a.q_dim : r - a.q_dim - a.kv_dim;
-        if (!is_k && a.v_out) a.v_out[rr] = v;
-        const int kh = rr / hd, d = rr % hd;
-        const int slot = *a.pos % a.n_ctx;
-        const long long e = a.kv_layer_off + (static_cast<long long>(kh) * a.n_ctx + slot) * hd + d;
-        void *cache = is_k ? a.k_cache : a.v_cache;
-        if (a.kv_type == kKvF16) {
-            static_cast<__half *>(cache)[e] = __float2half_rn(out);
-        } else {
-            const long long e0 = e - lane;  // first element of this 32-block
-            uint8_t *qs = static_cast<uint8_t *>(cache) + e0 / 2;
-            __half *dp = reinterpret_cast<__half *>(is_k ? a.k_scale : a.v_scale) + e0 / 32;
-            warp_store_q4_0(out, lane, qs, dp);
-        }
-    }
-}
-
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     GemvSmem &S = *reinterpret_cast<GemvSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
     const int cpt = a.W.cpt;
     const long long NC = static_cast<long long>(a.W.n_tiles) * cpt;
-    const int c0 = static_cast<int>(NC * c / G), c1 = static_cast<int>(NC * (c + 1) / G);
+    int c0, c1;
+    if (a.tile_aligned) {
+        c0 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * c / G) * cpt;
+        c1 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * (c + 1) / G) * cpt;
+    } else {
+        c0 = static_cast<int>(NC * c / G);
+        c1 = static_cast<int>(NC * (c + 1) / G);
+    }
     const int n_mine = (c1 - c0 > warp) ? (c1 - c0 - warp + kWarps - 1) / kWarps : 0;
+    const int nb = a.W.cols / 32, nbx = a.W.nbx;
+    // the RMSNorm weight comes through the bulk-copy engine when it is 16-byte aligned
+    const bool gbulk = PRO == kProNorm && (reinterpret_cast<uintptr_t>(a.gamma) & 15) == 0;
 
     if (tid < kWarps * kRing) mbar_init(&S.bar[tid / kRing][tid % kRing], 1);
+    if (tid == kWarps * kRing) mbar_init(&S.gbar, 1);
     if (tid == 0) S.err = 0;
     fence_barrier_init();
     __syncthreads();
@@ -238,20 +110,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
     };
     if (lane == 0)
         for (int i = 0; i < kRing && i < n_mine; ++i) issue(i);
+    if (gbulk && tid == 0) {
+        const uint32_t gb = static_cast<uint32_t>(a.W.cols) * 4u;
+        mbar_arrive_expect_tx(&S.gbar, gb);
+        bulk_load(S.gamma, a.gamma, gb, &S.gbar, l2_evict_last_policy());
+    }
 
     pdl_wait();
 
     // ---- prologue: activation -> Q8_1 blocks in shared memory ----
-    const int nb = a.W.cols / 32, nbx = a.W.nbx;
+    // Thread t converts blocks t and t + kThreads.  Both are loaded before any
+    // other memory access so that the activation costs one round trip.
+    float v0[32], v1[32];
+    const bool h0 = tid < nb, h1 = tid + kThreads < nb;
+    if (h0) load_block32(a.x + tid * 32, v0);
+    if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
+    int tok = -1;
+    if constexpr (EPI == kEpiEmbAdd) {
+        tok = resolve_token<kThreads>(a.tok, S.tok_v, S.tok_i, [] { __syncthreads(); });
+        if (c == 0 && tid == 0 && a.tok.tok_out) *a.tok.tok_out = tok;
+    }
     float scale = 1.0f;
+    const float *gam = a.gamma;
     if constexpr (PRO == kProNorm) {
         // rmsnorm_kernel (bmo_cuda_kernels.cu:244-295): scale = 1/sqrt(mean(x^2)+eps),
         // the sum of squares in double, the root and reciprocal in double
-        double ss = 0.0;
-        for (int i = tid; i < a.W.cols; i += kThreads) {
-            const double xv = static_cast<double>(a.x[i]);
-            ss = fma(xv, xv, ss);
-        }
+        double ss = (h0 ? sum_sq_double(v0) : 0.0) + (h1 ? sum_sq_double(v1) : 0.0);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) S.red[warp] = ss;
@@ -262,75 +146,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
         const float total = __double2float_rn(tot);
         const float mean_eps = __fadd_rn(__fdiv_rn(total, static_cast<float>(a.W.cols)), a.eps);
         scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(static_cast<double>(mean_eps))));
-    }
-    for (int b = tid; b < nbx; b += kThreads) {
-        int4 *qd = reinterpret_cast<int4 *>(S.xq + b * 32);
-        if (b < nb) {
-            float v[32];
-            int8_t q[32];
-            const float4 *xp = reinterpret_cast<const float4 *>(a.x + b * 32);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 t4 = xp[j];
-                v[4 * j] = t4.x; v[4 * j + 1] = t4.y; v[4 * j + 2] = t4.z; v[4 * j + 3] = t4.w;
-            }
-            if constexpr (PRO == kProNorm) {
-                const float4 *gp = reinterpret_cast<const float4 *>(a.gamma + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 g4 = gp[j];
-                    v[4 * j] = __fmul_rn(__fmul_rn(v[4 * j], scale), g4.x);
-                    v[4 * j + 1] = __fmul_rn(__fmul_rn(v[4 * j + 1], scale), g4.y);
-                    v[4 * j + 2] = __fmul_rn(__fmul_rn(v[4 * j + 2], scale), g4.z);
-                    v[4 * j + 3] = __fmul_rn(__fmul_rn(v[4 * j + 3], scale), g4.w);
-                }
-            }
-            const __half2 ds = quant_block_q8_1(v, q);
-            const int *qi = reinterpret_cast<const int *>(q);
-            qd[0] = make_int4(qi[0], qi[1], qi[2], qi[3]);
-            qd[1] = make_int4(qi[4], qi[5], qi[6], qi[7]);
-            S.xds[b] = make_float2(__low2float(ds), 4.0f * __high2float(ds));
-            if (c == 0 && a.q8_out) {
-                int *o = reinterpret_cast<int *>(a.q8_out + static_cast<size_t>(b) * 36);
-                o[0] = *reinterpret_cast<const int *>(&ds);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) o[1 + j] = qi[j];
-            }
-            if (c == 0 && a.xn_out) {
-                float4 *xo = reinterpret_cast<float4 *>(a.xn_out + b * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) xo[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            }
-        } else {
-            qd[0] = make_int4(0, 0, 0, 0);
-            qd[1] = make_int4(0, 0, 0, 0);
-            S.xds[b] = make_float2(0.0f, 0.0f);
+        if (gbulk) {
+            if (!mbar_wait(&S.gbar, 0)) atomicOr(&S.err, 1);
+            gam = S.gamma;
         }
     }
-    for (int i = tid; i < kMaxTilesPerCta * kWarps * 32; i += kThreads) (&S.part[0][0][0])[i] = 0.0;
-    int tok = -1;
-    if constexpr (EPI == kEpiEmbAdd) {
-        tok = resolve_token(a.tok, S.tok_v, S.tok_i);
-        if (c == 0 && tid == 0 && a.tok.tok_out) *a.tok.tok_out = tok;
-    }
+    if (tid < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid, h0, v0, scale, gam, c == 0);
+    if (tid + kThreads < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid + kThreads, h1, v1, scale, gam, c == 0);
     __syncthreads();
 
     // ---- main loop: stream chunks through the ring ----
+    // part[t][w] receives warp w's sum over tile t; every warp writes each
+    // tile of the CTA's range once (0 for tiles it had no chunk of).
     const int t_first = c0 / cpt;
-    int cur = -1;
+    const int t_last = c1 > c0 ? (c1 - 1) / cpt : t_first - 1;
+    int next_unwritten = t_first, cur = -1;
     double acc = 0.0;
+    auto flush = [&](int upto) {  // write tiles [next_unwritten, upto], cur's sum at cur
+        for (int t = next_unwritten; t <= upto; ++t) S.part[t - t_first][warp][lane] = t == cur ? acc : 0.0;
+        next_unwritten = upto + 1;
+    };
     for (int i = 0; i < n_mine; ++i) {
         const int k = c0 + warp + kWarps * i;
         const int tile = k / cpt, kc = k - tile * cpt;
         if (tile != cur) {
-            if (cur >= 0) S.part[cur - t_first][warp][lane] = acc;
+            if (cur >= 0) flush(cur);
             acc = 0.0;
             cur = tile;
         }
         if (!mbar_wait(&S.bar[warp][i % kRing], (i / kRing) & 1)) {
             if (lane == 0) atomicOr(&S.err, 1);
             for (int j = i + 1; j < n_mine && j < i + kRing; ++j) mbar_wait(&S.bar[warp][j % kRing], (j / kRing) & 1);
-            cur = -1;
             break;
         }
         acc += chunk_dot(S.ring[warp][i % kRing], S.xq + kc * kChunkBlocks * 32, S.xds + kc * kChunkBlocks, lane);
@@ -340,7 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
             issue(i + kRing);
         }
     }
-    if (cur >= 0) S.part[cur - t_first][warp][lane] = acc;
+    if (cur >= 0) flush(cur);
+    flush(t_last);
     __syncthreads();
     if (S.err) {
         if (tid == 0) raise_error(a.status, kErrTmaTimeout);
@@ -349,14 +196,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
     if (c1 <= c0) return;
 
     // ---- per-tile reduction (fixed order, double) and epilogue ----
-    const int t_last = (c1 - 1) / cpt;
     for (int tl = warp; tl <= t_last - t_first; tl += kWarps) {
         const int t = t_first + tl;
         double v = 0.0;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += S.part[tl][w][lane];
-        const int f = cta_of_chunk(static_cast<long long>(t) * cpt, NC, G);
-        const int l = cta_of_chunk(static_cast<long long>(t) * cpt + cpt - 1, NC, G);
+        const int f = a.tile_aligned ? 0 : cta_of_chunk(static_cast<long long>(t) * cpt, NC, G);
+        const int l = a.tile_aligned ? 0 : cta_of_chunk(static_cast<long long>(t) * cpt + cpt - 1, NC, G);
         if (f != l) {
             double *gp = a.gpart + (static_cast<size_t>(t) * (cpt + 1)) * 32;
             gp[(c - f) * 32 + lane] = v;
@@ -371,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const __grid_const
             for (int o = 0; o <= l - f; ++o) v += __ldcg(gp + o * 32 + lane);
             if (lane == 0) a.gcount[t] = 0;
         }
-        tile_epilogue<EPI>(a, t, lane, __double2float_rn(v), tok);
+        tile_epilogue<EPI>(a, t, lane, __double2float_rn(v), tok, a.rope_cs);
     }
 }
 
@@ -431,13 +277,38 @@ cudaError_t configure_gemv() {
     return e;
 }
 
+static long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+// Smallest stream-K grid whose CTAs stay within the partial table.
+static long long streamk_min_grid(const QMatDesc &m) {
+    return ceil_div(m.n_tiles, kMaxTilesPerCta - 2);
+}
+
+GemvPlan plan_gemv(const QMatDesc &m, int sms) {
+    const long long nc = static_cast<long long>(m.n_tiles) * m.cpt;
+    long long gs = std::min<long long>(sms, nc);
+    gs = std::max(gs, std::min(streamk_min_grid(m), nc));
+    long long ga = std::min<long long>(sms, m.n_tiles);
+    ga = std::max(ga, ceil_div(m.n_tiles, kMaxTilesPerCta));
+    const long long busiest_aligned = ceil_div(m.n_tiles, ga) * m.cpt;
+    const long long busiest_streamk = ceil_div(nc, gs);
+    if (busiest_aligned <= busiest_streamk + kCombineChunks) return GemvPlan{static_cast<int>(ga), 1};
+    return GemvPlan{static_cast<int>(std::max<long long>(gs, 1)), 0};
+}
+
 cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl) {
     if (a.W.nbx > kMaxNbx || grid <= 0 || a.W.cpt <= 0 || a.W.n_tiles <= 0) return cudaErrorInvalidValue;
+    if (prologue == kProNorm && a.W.cols > kMaxNormCols) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(a.x) & 15) return cudaErrorInvalidValue;
     // every CTA's tile range must fit the shared partial table
     const long long nc = static_cast<long long>(a.W.n_tiles) * a.W.cpt;
-    if (grid > nc) return cudaErrorInvalidValue;
-    const long long per_cta = (nc + grid - 1) / grid;
-    if ((per_cta + a.W.cpt - 1) / a.W.cpt + 1 > kMaxTilesPerCta) return cudaErrorInvalidValue;
+    if (a.tile_aligned) {
+        if (grid > a.W.n_tiles || ceil_div(a.W.n_tiles, grid) > kMaxTilesPerCta) return cudaErrorInvalidValue;
+    } else {
+        if (grid > nc) return cudaErrorInvalidValue;
+        const long long per_cta = ceil_div(nc, grid);
+        if (ceil_div(per_cta, a.W.cpt) + 1 > kMaxTilesPerCta) return cudaErrorInvalidValue;
+    }
 #define BMO_GEMV_CASE(P, E) \
     if (prologue == P && epilogue == E) return launch_t<P, E>(a, grid, s, pdl);
     BMO_GEMV_VARIANTS(BMO_GEMV_CASE)

@@ -14,11 +14,40 @@ cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid,
 size_t gemv_smem_bytes();
 int gemv_max_tiles_per_cta();
 int gemv_max_nbx();
+int gemv_max_norm_cols();
+// Grid and split for a matrix on a device with `sms` SMs: whole row tiles per
+// CTA unless that leaves the busiest CTA much more work than an even split.
+struct GemvPlan {
+    int grid;
+    int tile_aligned;
+};
+GemvPlan plan_gemv(const QMatDesc &m, int sms);
 
 // Ring decode attention (kernels/attention.cu): one cluster of `splits` CTAs per head.
 cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl);
 int attn_splits_for(int n_ctx);
 int attn_max_ctx();
+
+// Persistent frame kernel (kernels/frame.cu): runs `n_phases` FramePhase
+// steps with one CTA per SM (cooperative launch) and a grid barrier between
+// steps.  `bar` and `abort` are zero at launch.
+struct FrameArgs {
+    const FramePhase *prog;  // device
+    int n_phases;
+    unsigned *bar;
+    int *abort;
+    int *status;
+    const float2 *rope;      // this frame's RoPE table (device), copied into shared memory
+    int rope_pairs;
+};
+cudaError_t launch_frame(const FrameArgs &fa, int grid, cudaStream_t s);
+// SMs the frame kernel can cover (0: it cannot be resident on this device).
+int frame_max_grid();
+size_t frame_smem_bytes();
+int frame_max_window();
+int frame_max_tiles_per_cta();
+int frame_dep_max_window();
+int frame_dep_head_dim();
 
 // Frame-start embedding sum + RoPE table (kernels/misc.cu).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,

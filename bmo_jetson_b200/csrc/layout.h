@@ -27,8 +27,10 @@ enum RowPerm : int {
 
 // Prologue: how the GEMV input vector reaches shared memory as Q8_1 blocks.
 enum Prologue : int {
-    kProPlain = 0,  // quantise fp32 x
-    kProNorm = 1,   // RMSNorm(x) * gamma, then quantise
+    kProPlain = 0,    // quantise fp32 x
+    kProNorm = 1,     // RMSNorm(x) * gamma, then quantise
+    kProDepAttn = 2,  // persistent frame kernel only: x = decode attention of every head
+                      // over a short ring (the depformer), computed in each CTA
 };
 
 // Epilogue: what happens to the finished dot products of a tile.
@@ -100,6 +102,9 @@ struct GemvArgs {
     // embedding-add epilogue
     EmbTable emb;
     TokenSrc tok;
+    // work split: tile_aligned = 1 gives every CTA whole row tiles (no
+    // cross-CTA combine); 0 splits the (tile, chunk) units evenly (stream-K)
+    int tile_aligned;
     // stream-K bookkeeping
     double *gpart;         // [n_tiles][cpt+1][32] per-owner partial sums
     int *gcount;           // [n_tiles], zero between launches
@@ -117,6 +122,25 @@ struct AttnArgs {
     float scale;
     float *out;              // [n_heads][hd]
     int *status;
+};
+
+// One step of a decode frame.  The engine builds a frame as a list of these;
+// the per-op path launches one kernel per entry, the persistent frame kernel
+// runs the list as its program with a grid barrier between entries.
+enum PhaseKind : int {
+    kPhGemv = 0,      // g with prologue `pro`, epilogue `epi`
+    kPhAttn = 1,      // decode attention `at` (head_dim, `splits` CTAs per head in the per-op path)
+    kPhTokenOut = 2,  // CTA 0 writes the first maximum over tok.pairs into tok.tok_out
+};
+
+struct FramePhase {
+    int kind;
+    int pro, epi;
+    int head_dim;
+    int splits;
+    GemvArgs g;
+    AttnArgs at;   // kPhAttn, and the attention of a kProDepAttn prologue
+    TokenSrc tok;  // kPhTokenOut
 };
 
 }  // namespace bmo

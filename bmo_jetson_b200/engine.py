@@ -26,7 +26,7 @@ _c_i32p = ctypes.POINTER(ctypes.c_int32)
 _c_f32p = ctypes.POINTER(ctypes.c_float)
 
 KV_F16, KV_Q4_0 = 0, 1
-FLAG_NO_GRAPHS, FLAG_NO_PDL = 1, 2
+FLAG_NO_GRAPHS, FLAG_NO_PDL, FLAG_PERSISTENT = 1, 2, 4
 
 
 def lib() -> ctypes.CDLL:
@@ -50,7 +50,7 @@ def lib() -> ctypes.CDLL:
     for name in ("bmo_get_n_layers", "bmo_get_n_embd", "bmo_get_n_codebooks", "bmo_get_dep_q", "bmo_get_text_vocab",
                  "bmo_get_audio_vocab", "bmo_get_n_attn_heads", "bmo_get_head_dim", "bmo_capture_graphs",
                  "bmo_has_cuda_graphs", "bmo_get_kv_type", "bmo_get_n_ctx", "bmo_get_n_kv_heads", "bmo_get_device",
-                 "bmo_get_pos", "bmo_sync"):
+                 "bmo_get_pos", "bmo_sync", "bmo_get_persistent"):
         fn = getattr(L, name)
         fn.argtypes = [vp]
         fn.restype = i
@@ -163,6 +163,11 @@ class BMOEngine:
 
     def has_cuda_graphs(self) -> bool:
         return bool(lib().bmo_has_cuda_graphs(self._h))
+
+    @property
+    def persistent(self) -> bool:
+        """True when frames run as the persistent frame kernel."""
+        return bool(lib().bmo_get_persistent(self._h))
 
     def forward_temporal(self, tokens: np.ndarray, copy: bool = False) -> Tuple[np.ndarray, np.ndarray]:
         assert tokens.dtype == np.int32 and tokens.shape == (self.n_codebooks,), (
@@ -329,4 +334,8 @@ class BMOEngine:
             self._h = None
 
     def __del__(self):
-        self.close()
+        # at interpreter shutdown the module globals may already be gone
+        try:
+            self.close()
+        except TypeError:
+            pass

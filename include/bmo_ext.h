@@ -22,6 +22,7 @@ enum { BMO_KV_F16 = 0, BMO_KV_Q4_0 = 1 };
 enum {
     BMO_FLAG_NO_GRAPHS = 1, /* launch kernels eagerly instead of replaying CUDA graphs */
     BMO_FLAG_NO_PDL = 2,    /* no programmatic dependent launch between kernels */
+    BMO_FLAG_PERSISTENT = 4, /* run frames as the persistent frame kernel (default: one kernel per op) */
 };
 
 /* bmo_init with an explicit CUDA device, KV ring format and flags.
@@ -37,6 +38,8 @@ BMO_API int bmo_get_pos(bmo_handle_t *h);
 BMO_API void *bmo_get_stream(bmo_handle_t *h);
 /* Bytes of device memory the handle holds (weights, KV, buffers). */
 BMO_API size_t bmo_get_device_bytes(bmo_handle_t *h);
+/* 1 when frames run as the persistent frame kernel, 0 for one kernel per op. */
+BMO_API int bmo_get_persistent(bmo_handle_t *h);
 
 /* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
  * slots [slot0, slot0+n) of temporal layer `layer`; rows are

@@ -43,7 +43,11 @@ BMO_API size_t bmo_k_gemv_scratch_bytes(int rows, int cols, int perm, int swiglu
  * resid_dev != NULL: y = resid + W x (fused launch_residual_add).
  * q8_out_dev / xn_out_dev (optional) receive the Q8_1 blocks and the
  * normalised fp32 vector the kernel used.  scratch_dev must be zero on the
- * first call and is left zero by every call that returns 0. */
+ * first call and is left zero by every call that returns 0.  x_dev and
+ * xn_out_dev are 16-byte aligned; with gamma_dev, cols <= 5120.  grid 0
+ * picks the launch (whole row tiles per CTA where that balances); grid > 0
+ * runs that many CTAs over an even split of the (row tile, 8-block chunk)
+ * units, combining straddled tiles through scratch_dev. */
 BMO_API int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
                             const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
                             float *y_dev, void *q8_out_dev, float *xn_out_dev, void *scratch_dev,

@@ -116,6 +116,50 @@ def test_gemv_rmsnorm_prologue(rows, cols):
     assert_near_exact(y, orc.gemv_q4_0(W, xn, rows, cols), what="gemv after norm")
 
 
+def test_gemv_rmsnorm_unaligned_gamma_and_limits():
+    """A norm weight off a 16-byte boundary is read with plain loads (the bulk
+    copy needs alignment) and gives the same bits; norm widths beyond the
+    kernel's staging buffer and unaligned activations are rejected."""
+    L = engine.lib()
+    rows, cols = 3072, 1024
+    W = weights(rows, cols, 17)
+    rng = np.random.default_rng(18)
+    x = rng.normal(0, 2, cols).astype(np.float32)
+    g = (1 + 0.1 * rng.normal(0, 1, cols)).astype(np.float32)
+    T = tiled(W, rows, cols)
+    y_al, _, xn_al = run_gemv(T, rows, cols, x, gamma=g)
+    xd = to_dev(x)
+    gbuf = torch.zeros(cols + 1, device=DEV)
+    gbuf[1:] = torch.from_numpy(g).to(DEV)
+    y = torch.empty(rows, device=DEV)
+    xn = torch.zeros(cols, device=DEV)
+    nbytes = L.bmo_k_gemv_scratch_bytes(rows, cols, PERM_ID, 0)
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    assert gbuf[1:].data_ptr() % 16 != 0
+    rc = L.bmo_k_gemv_q4_0(T.data_ptr(), rows, cols, PERM_ID, 0, xd.data_ptr(), gbuf[1:].data_ptr(), 1e-8, None,
+                           y.data_ptr(), None, xn.data_ptr(), scratch.data_ptr(), nbytes, 0, stream())
+    torch.cuda.synchronize()
+    assert rc == 0
+    np.testing.assert_array_equal(xn.cpu().numpy(), xn_al)
+    np.testing.assert_array_equal(y.cpu().numpy(), y_al)
+    # unaligned activation
+    xb = torch.zeros(cols + 1, device=DEV)
+    rc = L.bmo_k_gemv_q4_0(T.data_ptr(), rows, cols, PERM_ID, 0, xb[1:].data_ptr(), None, 1e-8, None,
+                           y.data_ptr(), None, None, scratch.data_ptr(), nbytes, 0, stream())
+    assert rc != 0
+    # RMSNorm prologue wider than the staging buffer
+    wide = 8192
+    Tw = torch.zeros(L.bmo_k_q4_0_tiled_bytes(64, wide, PERM_ID, 0), dtype=torch.uint8, device=DEV)
+    xw = torch.zeros(wide, device=DEV)
+    gw = torch.ones(wide, device=DEV)
+    nb2 = L.bmo_k_gemv_scratch_bytes(64, wide, PERM_ID, 0)
+    s2 = torch.zeros(nb2, dtype=torch.uint8, device=DEV)
+    rc = L.bmo_k_gemv_q4_0(Tw.data_ptr(), 64, wide, PERM_ID, 0, xw.data_ptr(), gw.data_ptr(), 1e-8, None,
+                           y.data_ptr(), None, None, s2.data_ptr(), nb2, 0, stream())
+    assert rc != 0
+    torch.cuda.synchronize()
+
+
 def test_gemv_residual_epilogue():
     rows, cols = 4096, 4096
     W = weights(rows, cols, 9)
