@@ -314,6 +314,8 @@ def main():
     ap.add_argument("--kv", default="f16", choices=["f16", "q4_0"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="only the standalone GEMV timing (profiling)")
+    ap.add_argument("--profile-frames", type=int, default=0,
+                    help="profiling: run --warmup frames then this many device-resident frames, print nothing else")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 0)
     rank, world, local = dist_env()
@@ -337,6 +339,17 @@ def main():
     fill_history(e)
     assert e.capture_graphs() == 0
     K = e.n_codebooks
+    if args.profile_frames > 0:
+        n = args.warmup + args.profile_frames
+        toks = torch.from_numpy(frame_tokens(n, K, e.text_vocab, e.audio_vocab)).to(torch.device("cuda", local))
+        out = torch.zeros((n, 1 + e.dep_q), dtype=torch.int32, device=toks.device)
+        for i in range(n):
+            e.enqueue_frame(toks[i].data_ptr(), K, START_POS + i, out[i].data_ptr())
+        e.sync()
+        print(json.dumps({"profile_frames": args.profile_frames, "warmup": args.warmup,
+                          "text_tokens": out[:, 0].cpu().tolist()}), flush=True)
+        e.close()
+        return 0
     n_frames = args.warmup + args.steps
     toks = frame_tokens(2 * n_frames + 2, K, e.text_vocab, e.audio_vocab, seed=1 + rank)
     dev = torch.device("cuda", local)

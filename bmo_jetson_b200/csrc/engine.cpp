@@ -78,6 +78,10 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     }
     load(gguf_path);
     alloc_state();
+    // BMO_DEP_FOLD=1: the depformer attention runs inside its O-projection GEMV
+    // (measured slower than a separate attention kernel on B200, so off by default)
+    dep_fold_ = dep_hd == gemv_dep_attn_head_dim() && dep_n_ctx <= gemv_dep_attn_max_window() &&
+                dep_heads * dep_hd <= gemv_max_norm_cols() && env_int("BMO_DEP_FOLD", 0) != 0;
     build_programs();
 }
 
@@ -664,6 +668,7 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
         o.y = dxb_;
         o.resid = dxa_;
         if (fold) {
+            o.att = at;
             FramePhase op = gemv_op(o, kProDepAttn, kEpiResid);
             op.at = at;
             op.head_dim = dep_hd;
@@ -727,7 +732,6 @@ void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
     for (const FramePhase &op : ops) {
         switch (op.kind) {
         case kPhGemv: {
-            if (op.pro != kProPlain && op.pro != kProNorm) throw std::runtime_error("internal: op needs the frame kernel");
             const GemvPlan p = plan_gemv(op.g.W, sm_count);
             GemvArgs b = op.g;
             b.tile_aligned = p.tile_aligned;
@@ -762,7 +766,7 @@ void Engine::enqueue_layer(cudaStream_t s, int l) {
 
 void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok) {
     std::vector<FramePhase> v;
-    ops_depth_step(v, cb, z, tok, false);
+    ops_depth_step(v, cb, z, tok, dep_fold_);
     enqueue_ops(s, v);
 }
 
@@ -774,7 +778,7 @@ void Engine::reset_depth_kv_async(cudaStream_t s) {
 void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
     reset_depth_kv_async(s);
     std::vector<FramePhase> v;
-    ops_cascade(v, z, first, false);
+    ops_cascade(v, z, first, dep_fold_);
     enqueue_ops(s, v);
 }
 

@@ -189,6 +189,7 @@ private:
 
     // persistent frame kernel
     bool persistent_ = false;
+    bool dep_fold_ = false;  // depformer attention fused into the O-projection GEMV
     int frame_grid_ = 0;
     unsigned *fbar_ = nullptr;  // [grid barrier counter, abort flag]
     DevProgram prog_temporal_, prog_cascade_z_, prog_cascade_dz_, prog_frame_;

@@ -139,7 +139,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     // Every CTA of the cluster must be running before any writes into its
     // shared memory: arrive now, wait just before the first remote store.
     cluster_arrive_relaxed();
-    pdl_launch_dependents();
     uint32_t kphase = 0, vphase = 0;
     const bool prefetched = (nsub == 1);
     if (prefetched) {  // common case: the whole split fits one sub-chunk
@@ -206,6 +205,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
         }
         __syncthreads();
     }
+    pdl_launch_dependents();  // the next kernel prefetches during the softmax and weighted sum
     // local maximum, pushed into every split's shared memory
     float m = -INFINITY;
     for (int j = tid; j < n; j += kAttnThreads) m = fmaxf(m, S.s[j]);

@@ -17,8 +17,9 @@
 // kRing 4.6 KB chunks in flight through the TMA bulk-copy engine into a
 // private shared-memory ring.  The first chunks (and the RMSNorm weight) are
 // issued before griddepcontrol.wait, so under programmatic dependent launch
-// they stream while the previous kernel finishes; after the wait the
-// activation costs a single memory round trip.
+// they stream while the previous kernel finishes its epilogue (the dependent
+// launch is triggered after the weight loop); after the wait the activation
+// costs a single memory round trip.
 // Work split: normally each CTA owns whole row tiles (no cross-CTA traffic);
 // where that balances badly, CTA c owns an even range of (row tile, chunk)
 // units ("stream-K") and tiles that straddle CTAs are finished by the last
@@ -44,6 +45,9 @@ constexpr int kMaxNormCols = kMaxTilesPerCta * kWarps * 32 * 2;  // RMSNorm weig
 // A cross-CTA combine (partial store, release, acquire, reload) costs about as
 // long as one SM streaming this many chunks.
 constexpr int kCombineChunks = 12;
+// kProDepAttn: head size and longest window (the window is held in registers)
+constexpr int kDepAttnHd = 64;
+constexpr int kDepAttnMaxWin = 8;
 
 // Kept under half of an SM's shared memory so that the next kernel's CTA fits
 // beside this one under programmatic dependent launch and prefetches its weights.
@@ -67,6 +71,8 @@ size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
 int gemv_max_tiles_per_cta() { return kMaxTilesPerCta; }
 int gemv_max_nbx() { return kMaxNbx; }
 int gemv_max_norm_cols() { return kMaxNormCols; }
+int gemv_dep_attn_max_window() { return kDepAttnMaxWin; }
+int gemv_dep_attn_head_dim() { return kDepAttnHd; }
 
 __device__ __forceinline__ int cta_of_chunk(long long k, long long nc, int g) {
     return static_cast<int>(((k + 1) * g - 1) / nc);
@@ -98,7 +104,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_const
     if (tid == 0) S.err = 0;
     fence_barrier_init();
     __syncthreads();
-    pdl_launch_dependents();
 
     // Weights never depend on earlier kernels: start streaming them now.
     const uint64_t pol = l2_evict_first_policy();
@@ -123,8 +128,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_const
     // other memory access so that the activation costs one round trip.
     float v0[32], v1[32];
     const bool h0 = tid < nb, h1 = tid + kThreads < nb;
-    if (h0) load_block32(a.x + tid * 32, v0);
-    if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
+    if constexpr (PRO == kProDepAttn) {
+        // the depformer attention of every head is the activation (n_heads * 64 <= kMaxNormCols)
+        dep_attention_block<kWarps, kDepAttnHd, kDepAttnMaxWin>(a.att, S.gamma);
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v0[j] = h0 ? S.gamma[tid * 32 + j] : 0.0f;
+    } else {
+        if (h0) load_block32(a.x + tid * 32, v0);
+        if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
+    }
     int tok = -1;
     if constexpr (EPI == kEpiEmbAdd) {
         tok = resolve_token<kThreads>(a.tok, S.tok_v, S.tok_i, [] { __syncthreads(); });
@@ -188,6 +201,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_const
     }
     if (cur >= 0) flush(cur);
     flush(t_last);
+    // The next kernel may start now: its weight prefetch then overlaps this
+    // kernel's epilogue instead of competing with its weight stream (measured:
+    // triggering at kernel start costs ~10% of the frame rate).
+    pdl_launch_dependents();
     __syncthreads();
     if (S.err) {
         if (tid == 0) raise_error(a.status, kErrTmaTimeout);
@@ -258,6 +275,7 @@ static cudaError_t configure_one() {
 
 #define BMO_GEMV_VARIANTS(X)  \
     X(kProNorm, kEpiQKV)      \
+    X(kProDepAttn, kEpiResid) \
     X(kProPlain, kEpiResid)   \
     X(kProNorm, kEpiSwiGLU)   \
     X(kProNorm, kEpiLogits)   \
@@ -299,7 +317,12 @@ GemvPlan plan_gemv(const QMatDesc &m, int sms) {
 cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl) {
     if (a.W.nbx > kMaxNbx || grid <= 0 || a.W.cpt <= 0 || a.W.n_tiles <= 0) return cudaErrorInvalidValue;
     if (prologue == kProNorm && a.W.cols > kMaxNormCols) return cudaErrorInvalidValue;
-    if (reinterpret_cast<uintptr_t>(a.x) & 15) return cudaErrorInvalidValue;
+    if (prologue == kProDepAttn &&
+        (a.att.n_ctx > kDepAttnMaxWin || a.att.n_ctx <= 0 || a.att.n_heads <= 0 || a.att.n_kv_heads <= 0 ||
+         a.att.n_heads % a.att.n_kv_heads || a.att.n_heads * kDepAttnHd != a.W.cols || a.W.cols > kMaxNormCols ||
+         a.att.kv_type != kKvF16))
+        return cudaErrorInvalidValue;
+    if (prologue != kProDepAttn && (reinterpret_cast<uintptr_t>(a.x) & 15)) return cudaErrorInvalidValue;
     // every CTA's tile range must fit the shared partial table
     const long long nc = static_cast<long long>(a.W.n_tiles) * a.W.cpt;
     if (a.tile_aligned) {

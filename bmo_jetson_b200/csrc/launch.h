@@ -15,6 +15,9 @@ size_t gemv_smem_bytes();
 int gemv_max_tiles_per_cta();
 int gemv_max_nbx();
 int gemv_max_norm_cols();
+// kProDepAttn limits: longest ring window and head size
+int gemv_dep_attn_max_window();
+int gemv_dep_attn_head_dim();
 // Grid and split for a matrix on a device with `sms` SMs: whole row tiles per
 // CTA unless that leaves the busiest CTA much more work than an even split.
 struct GemvPlan {

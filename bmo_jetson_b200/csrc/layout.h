@@ -76,6 +76,19 @@ struct EmbTable {
     long long row_bytes;
 };
 
+struct AttnArgs {
+    const float *q;          // [n_heads][hd] rotated queries
+    const float *v_raw;      // [n_kv][hd] fp32 v of this token
+    const void *k_cache, *v_cache;
+    const uint8_t *k_scale, *v_scale;
+    long long kv_layer_off;  // element offset of this layer
+    int n_heads, n_kv_heads, n_ctx, kv_type;
+    const int *pos;
+    float scale;
+    float *out;              // [n_heads][hd]
+    int *status;
+};
+
 struct GemvArgs {
     QMatDesc W;
     // prologue
@@ -102,6 +115,8 @@ struct GemvArgs {
     // embedding-add epilogue
     EmbTable emb;
     TokenSrc tok;
+    // kProDepAttn prologue: the decode attention whose output is the activation
+    AttnArgs att;
     // work split: tile_aligned = 1 gives every CTA whole row tiles (no
     // cross-CTA combine); 0 splits the (tile, chunk) units evenly (stream-K)
     int tile_aligned;
@@ -111,18 +126,6 @@ struct GemvArgs {
     int *status;
 };
 
-struct AttnArgs {
-    const float *q;          // [n_heads][hd] rotated queries
-    const float *v_raw;      // [n_kv][hd] fp32 v of this token
-    const void *k_cache, *v_cache;
-    const uint8_t *k_scale, *v_scale;
-    long long kv_layer_off;  // element offset of this layer
-    int n_heads, n_kv_heads, n_ctx, kv_type;
-    const int *pos;
-    float scale;
-    float *out;              // [n_heads][hd]
-    int *status;
-};
 
 // One step of a decode frame.  The engine builds a frame as a list of these;
 // the per-op path launches one kernel per entry, the persistent frame kernel

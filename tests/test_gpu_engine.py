@@ -178,6 +178,33 @@ def test_frame_greedy_equals_steps(pair):
         np.testing.assert_array_equal(audio, o.depth_cascade_greedy(text_tok, zo))
 
 
+@pytest.mark.parametrize("mode", ["dep_fold", "persistent"])
+def test_alternative_paths_match_oracle(tiny_model, mode, monkeypatch):
+    """The depformer attention fused into its O-projection GEMV (BMO_DEP_FOLD=1),
+    and whole frames as the persistent frame kernel: same tokens as the oracle."""
+    flags = 0
+    if mode == "dep_fold":
+        monkeypatch.setenv("BMO_DEP_FOLD", "1")
+    else:
+        flags = engine.FLAG_PERSISTENT
+    e = engine.BMOEngine(tiny_model, n_ctx=32, flags=flags)
+    o = orc.OracleModel(tiny_model, n_ctx=32)
+    assert e.persistent == (mode == "persistent")
+    rng = np.random.default_rng(21)
+    for step in range(4):
+        t = tokens_for(step + 3, e.n_codebooks, e.text_vocab, e.audio_vocab)
+        e.pos = step
+        z, lg = e.forward_temporal(t, copy=True)
+        zo, lo, _ = o.forward_temporal(t, step)
+        assert rel_l2(z, zo) < TOL and rel_l2(lg, lo) < TOL_LOGITS
+        text = int(np.argmax(lo))
+        np.testing.assert_array_equal(e.forward_depth_cascade(text, z, 0.0, 0), o.depth_cascade_greedy(text, zo))
+    zr = rng.normal(0, 1, e.n_embd).astype(np.float32)
+    np.testing.assert_array_equal(e.forward_depth_cascade(9, zr, 0.0, 0), o.depth_cascade_greedy(9, zr))
+    e.close()
+    o.close()
+
+
 def test_graphs_and_eager_agree_bitwise(tiny_model):
     eg = engine.BMOEngine(tiny_model, n_ctx=32)
     ee = engine.BMOEngine(tiny_model, n_ctx=32, flags=engine.FLAG_NO_GRAPHS | engine.FLAG_NO_PDL)
