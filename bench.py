@@ -229,6 +229,76 @@ def gemv_roofline(local, peak_gbs, iters=40):
             "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": achieved}
 
 
+def bench_batch(path, local, dist, sessions, steps, warmup, rank):
+    """Config 4: `sessions` independent sessions on this GPU, each with its own
+    512-slot Q4_0 ring, at seeded positions uniform in [0, 3000), stepped
+    together (one weight stream per frame for all of them).  Device-resident
+    inputs for `value`; host arrays through bmo_forward_frame_batch for e2e."""
+    import torch
+    from bmo_jetson_b200 import engine
+    e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=engine.KV_Q4_0)
+    e.batch_init(sessions)
+    K = e.n_codebooks
+    dev = torch.device("cuda", local)
+    rng = np.random.default_rng(1000 + rank)
+    n = warmup + steps
+    pos0 = rng.integers(0, 3000, sessions).astype(np.int32)
+    pos = np.stack([pos0 + i for i in range(2 * n + 1)]).astype(np.int32)       # [frame][row]
+    toks = np.stack([frame_tokens(sessions, K, e.text_vocab, e.audio_vocab, seed=2000 + 97 * rank + i)
+                     for i in range(2 * n + 1)])                                # [frame][row][K]
+    pos_d = torch.from_numpy(pos).to(dev)
+    toks_d = torch.from_numpy(toks).to(dev)
+    out_d = torch.zeros((n, sessions, 1 + e.dep_q), dtype=torch.int32, device=dev)
+    stream = torch.cuda.ExternalStream(e.stream, device=dev)
+    for i in range(warmup):
+        e.enqueue_frame_batch(sessions, 0, toks_d[i].data_ptr(), K, pos_d[i].data_ptr(), out_d[i].data_ptr())
+    e.sync()
+    barrier(dist)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        f = warmup + i
+        e.enqueue_frame_batch(sessions, 0, toks_d[f].data_ptr(), K, pos_d[f].data_ptr(), out_d[f].data_ptr())
+    b.record(stream)
+    e.sync()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    ms = reduce_max(dist, a.elapsed_time(b) / steps)
+    out = out_d.cpu().numpy()
+    assert (out[:, :, 0] >= 0).all() and (out[:, :, 0] < e.text_vocab).all()
+    # end to end: host tokens and positions in, host tokens out, every frame
+    for i in range(min(warmup, 3)):
+        e.forward_frame_batch(toks[n + i], pos[n + i])
+    barrier(dist)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        e.forward_frame_batch(toks[n + i], pos[n + i])
+    e2e_s = reduce_max(dist, time.perf_counter() - t0)
+    world = 1 if dist is None else dist.get_world_size()
+    # algorithmic bytes: weights once + every session's Q4 KV window (positions advance during the run)
+    d, F, V = e.n_embd, 11264, e.text_vocab
+    q4 = lambda r, c: r * c // 32 * 18
+    w = e.n_layers * (q4(3 * d, d) + q4(d, d) + q4(2 * F, d) + q4(d, F)) + q4(V, d)
+    D, DF = 1024, 2816
+    w += 8 * (q4(D, d) + 6 * (q4(3 * D, D) + q4(D, D) + q4(2 * DF, D) + q4(D, DF)) + q4(2048, D))
+    win = np.minimum(pos[warmup:warmup + steps] + 1, N_CTX).mean(axis=0).sum()
+    kv = 2 * e.n_layers * e.n_kv_heads * e.head_dim * 18 / 32 * win
+    frame_b = w + kv
+    launches = 1 + e.n_layers * 9 + 2 + e.dep_q * (2 + 6 * 9 + 2) + 1
+    h2d = 4 * (64 + 64 + 64 * 64 + 4)
+    d2h = sessions * (1 + e.dep_q) * 4 + 4
+    e.close()
+    return {"sessions_per_gpu": sessions, "value": world * sessions * 1000.0 / ms, "unit": "frames/s",
+            "ms_per_step": ms, "frame_hbm_bytes": frame_b, "weight_bytes": w, "kv_bytes": kv,
+            "frame_hbm_gbs": frame_b / (ms * 1e-3) / 1e9,
+            "e2e": {"value": world * sessions * steps / e2e_s, "unit": "frames/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "bmo_forward_frame_batch (host arrays), wall clock"},
+            "gpu_launches": launches * steps,
+            "config": "config4: independent sessions, each a 512-slot Q4_0 ring, positions uniform in [0,3000), "
+                      "greedy frame (temporal + text head + 8-step depformer) per session per step"}
+
+
 def traffic_from_profile():
     p = os.path.join(ROOT, "profiles", "gemv_ffn_in_traffic.json")
     try:
@@ -314,6 +384,9 @@ def main():
     ap.add_argument("--kv", default="f16", choices=["f16", "q4_0"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="only the standalone GEMV timing (profiling)")
+    ap.add_argument("--sessions", type=int, default=64,
+                    help="config 4: sessions per GPU of the batched measurement (0: skip it)")
+    ap.add_argument("--batch-only", action="store_true", help="only the batched-sessions measurement")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="profiling: run --warmup frames then this many device-resident frames, print nothing else")
     args = ap.parse_args()
@@ -333,6 +406,13 @@ def main():
     dist = init_dist(world, local)
     torch.cuda.set_device(local)
     path = prepare_model(rank, dist)
+    if args.batch_only:
+        r = bench_batch(path, local, dist, args.sessions, args.steps, args.warmup, rank)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     from bmo_jetson_b200 import engine
     kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
     e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type)
@@ -422,6 +502,12 @@ def main():
     total_b, temporal_b, dep_b, kv_b = frame_bytes(e)
     launches_per_frame = 1 + e.n_layers * 5 + 1 + e.dep_q * (1 + 6 * 5 + 1) + 1
 
+    e.close()
+    batch = None
+    if args.sessions > 0:
+        batch = bench_batch(path, local, dist, args.sessions, max(5, min(args.steps, 20)), max(3, min(args.warmup, 3)),
+                            rank)
+
     line = None
     if rank == 0:
         cpu = None
@@ -456,9 +542,9 @@ def main():
                     "path": "bmo_forward_temporal + host argmax + bmo_forward_depth_cascade (greedy), wall clock"},
             "gpu_launches": launches_per_frame * args.steps,
             "clocks": clocks.summary(),
+            "batch": batch,
         }
         print(json.dumps(line), flush=True)
-    e.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0

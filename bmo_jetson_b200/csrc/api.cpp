@@ -447,6 +447,90 @@ int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token) {
     }
 }
 
+int bmo_batch_init(bmo_handle_t *h, int n_sessions) {
+    if (!h) return 1;
+    bmo::Engine *e = h->eng.get();
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        const int rc = e->batch_init(n_sessions);
+        if (rc == 1) set_err(h, "bmo_batch_init: session count outside [1, 64]");
+        if (rc == 3) set_err(h, "bmo_batch_init: sessions already allocated with another count");
+        return rc == 1 ? 2 : rc;
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
+int bmo_batch_sessions(bmo_handle_t *h) { return (h && h->eng) ? h->eng->batch_sessions() : 0; }
+
+int bmo_forward_frame_batch(bmo_handle_t *h, int n_rows, const int32_t *sess_ids, const int32_t *input_tokens,
+                            int num_codebooks, const int32_t *pos, float *out_transformer, float *out_text_logits,
+                            int32_t *out_tokens) {
+    if (!h || !input_tokens || !pos || !out_tokens) {
+        set_err(h, "bmo_forward_frame_batch: null pointer argument");
+        return 1;
+    }
+    bmo::Engine *e = h->eng.get();
+    if (num_codebooks <= 0 || num_codebooks > e->num_codebooks) {
+        set_err(h, "bmo_forward_frame_batch: invalid num_codebooks");
+        return 2;
+    }
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (n_rows < 1 || n_rows > e->batch_sessions()) {
+        set_err(h, "bmo_forward_frame_batch: row count outside [1, sessions] (bmo_batch_init first)");
+        return 2;
+    }
+    try {
+        e->run_frame_batch(n_rows, sess_ids, input_tokens, num_codebooks, pos, out_transformer, out_text_logits,
+                           out_tokens);
+        h->last_error.clear();
+        return 0;
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
+int bmo_enqueue_frame_batch(bmo_handle_t *h, int n_rows, const int32_t *sess_ids_dev, const int32_t *tokens_dev,
+                            int num_codebooks, const int32_t *pos_dev, int32_t *out_tokens_dev) {
+    if (!h || !tokens_dev || !pos_dev) return 1;
+    bmo::Engine *e = h->eng.get();
+    if (num_codebooks <= 0 || num_codebooks > e->num_codebooks) return 2;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (n_rows < 1 || n_rows > e->batch_sessions()) return 2;
+    try {
+        e->enqueue_frame_batch_device(n_rows, sess_ids_dev, tokens_dev, num_codebooks, pos_dev, out_tokens_dev);
+        return 0;
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
+int bmo_batch_kv_import_f32(bmo_handle_t *h, int session, int layer, int slot0, int n, const float *k_rows,
+                            const float *v_rows) {
+    if (!h || !k_rows || !v_rows) return 1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        return h->eng->batch_kv_import(session, layer, slot0, n, k_rows, v_rows);
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
+int bmo_batch_reset(bmo_handle_t *h, int session) {
+    if (!h) return 1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        return h->eng->batch_reset(session);
+    } catch (const std::exception &ex) {
+        set_err(h, ex.what());
+        return 9;
+    }
+}
+
 int bmo_sync(bmo_handle_t *h) {
     if (!h) return 1;
     std::lock_guard<std::mutex> lk(h->mu);

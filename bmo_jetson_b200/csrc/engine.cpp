@@ -88,6 +88,7 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
 Engine::~Engine() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    batch_.reset();
     auto drop = [](cudaGraphExec_t &g) {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
@@ -1136,14 +1137,19 @@ void Engine::reset_depth_kv() {
 // Host-side conversion of fp32 rows into the ring format, one contiguous
 // run of slots per head.
 int Engine::kv_import(int layer, int slot0, int n, const float *k_rows, const float *v_rows) {
+    return kv_import_into(k_cache_, v_cache_, k_scale_, v_scale_, layer, slot0, n, k_rows, v_rows);
+}
+
+int Engine::kv_import_into(void *kc, void *vc, uint8_t *ks, uint8_t *vs, int layer, int slot0, int n,
+                           const float *k_rows, const float *v_rows) {
     if (layer < 0 || layer >= n_layers || slot0 < 0 || n <= 0 || slot0 + n > n_ctx) return 2;
     ck(cudaSetDevice(device), "cudaSetDevice");
     const int hd = head_dim;
     std::vector<uint8_t> plane, scales;
     for (int which = 0; which < 2; ++which) {
         const float *src = which ? v_rows : k_rows;
-        uint8_t *cache = static_cast<uint8_t *>(which ? v_cache_ : k_cache_);
-        uint8_t *scale = which ? v_scale_ : k_scale_;
+        uint8_t *cache = static_cast<uint8_t *>(which ? vc : kc);
+        uint8_t *scale = which ? vs : ks;
         for (int h = 0; h < n_kv_heads; ++h) {
             const size_t row0 = (static_cast<size_t>(layer) * n_kv_heads + h) * n_ctx + slot0;
             std::vector<float> rows(static_cast<size_t>(n) * hd);

@@ -91,6 +91,22 @@ public:
     bool graphs_captured() const { return graphs_ready_; }
     bool persistent() const { return persistent_; }
 
+    // ---- batched sessions: up to kBatchMax independent sessions stepped
+    // together, each with its own temporal ring, sharing one weight stream ----
+    int batch_init(int n_sessions);  // allocates the rings once (0 ok, 1 bad count, 3 already other size)
+    int batch_sessions() const;
+    // One greedy frame for rows s < n: session sess_ids[s] at pos[s] on
+    // tokens[s * K + 0..K).  out_tokens[s * (1 + dep_q)] = text token, then
+    // the dep_q audio tokens; out_z [n][n_embd] and out_logits
+    // [n][text_vocab] are optional.
+    void run_frame_batch(int n, const int32_t *sess_ids, const int32_t *tokens, int K, const int32_t *pos,
+                         float *out_z, float *out_logits, int32_t *out_tokens);
+    // Same with device inputs and outputs; no host synchronisation.
+    void enqueue_frame_batch_device(int n, const int32_t *sess_dev, const int32_t *tokens_dev, int K,
+                                    const int32_t *pos_dev, int32_t *out_tokens_dev);
+    int batch_kv_import(int sess, int layer, int slot0, int n, const float *k_rows, const float *v_rows);
+    int batch_reset(int sess);  // sess < 0: every session
+
 private:
     struct Layer {
         QMatDesc qkv{}, wo{}, ffn_in{}, ffn_out{};
@@ -130,6 +146,21 @@ private:
     };
     void build_programs();
     void enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal);
+    // batched sessions (batch_engine.cpp)
+    struct BatchState;
+    struct BatchDeleter {
+        void operator()(BatchState *b) const;
+    };
+    std::unique_ptr<BatchState, BatchDeleter> batch_;
+    void enqueue_batch_frame(cudaStream_t s, int n);
+    void enqueue_batch_temporal(cudaStream_t s, int n);
+    void enqueue_batch_cascade(cudaStream_t s, int n);
+    void batch_stage(cudaStream_t s, int n, const float *x, int cols, const QMatDesc &W, const float *gamma,
+                     float *xn_out, const TokenSrc *tok, int pairs_stride, int *tok_out);
+    void batch_gemm(cudaStream_t s, const BatchGemmArgs &a, int epi);
+    int kv_import_into(void *kc, void *vc, uint8_t *ks, uint8_t *vs, int layer, int slot0, int n, const float *k_rows,
+                       const float *v_rows);
+
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)> &fn);
     void launch(cudaGraphExec_t &g, const std::function<void(cudaStream_t)> &fn);
     void finish_call();

@@ -77,10 +77,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     Smem &S = *reinterpret_cast<Smem *>(smem_raw);
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int sp = blockIdx.x, nsp = gridDim.x, h = blockIdx.y;
+    const int sp = blockIdx.x, nsp = gridDim.x, h = blockIdx.y, sess = blockIdx.z;
+    // batched sessions: this session's q / raw v / output / ring / position
+    const float *qv = a.q + static_cast<long long>(sess) * a.qo_stride;
+    const float *vraw = a.v_raw + static_cast<long long>(sess) * a.vraw_stride;
+    float *outv = a.out + static_cast<long long>(sess) * a.qo_stride;
 
     // The position was copied to the device before this graph's first kernel.
-    const int pos = *a.pos;
+    const int pos = a.pos[sess * a.pos_stride];
     const int total = pos + 1;
     const int window = total > a.n_ctx ? a.n_ctx : total;
     const int start = total - window;
@@ -89,7 +93,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     const int n = max(0, min(window, i0 + per) - i0);
     const int nsub = (n + kAttnSub - 1) / kAttnSub;
     const int kh = (a.n_kv_heads == a.n_heads) ? h : h / (a.n_heads / a.n_kv_heads);
-    const long long head_row0 = a.kv_layer_off / HD + static_cast<long long>(kh) * a.n_ctx;  // ring row index
+    const long long head_row0 =
+        (a.kv_layer_off + (a.ring_of ? a.ring_of[sess] : sess) * a.kv_sess_stride) / HD +
+        static_cast<long long>(kh) * a.n_ctx;  // ring row index
     const uint8_t *kc = static_cast<const uint8_t *>(a.k_cache) + head_row0 * kRowBytes;
     const uint8_t *vc = static_cast<const uint8_t *>(a.v_cache) + head_row0 * kRowBytes;
     const __half *kdc = Q4 ? reinterpret_cast<const __half *>(a.k_scale) + head_row0 * kSc : nullptr;
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
 
     if (window == 1) {  // uniform over the cluster: no cluster barrier is reached
         if (sp == 0)
-            for (int d = tid; d < HD; d += kAttnThreads) a.out[h * HD + d] = a.v_raw[kh * HD + d];
+            for (int d = tid; d < HD; d += kAttnThreads) outv[h * HD + d] = vraw[kh * HD + d];
         if (prefetched) {
             mbar_wait(&S.kbar, 0);
             mbar_wait(&S.vbar, 0);
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     }
     bool ok = true;
     // q and (single-sub splits) the newest K/V rows: one memory round trip
-    for (int d = tid; d < HD; d += kAttnThreads) S.q[d] = __ldcg(a.q + h * HD + d);
+    for (int d = tid; d < HD; d += kAttnThreads) S.q[d] = __ldcg(qv + h * HD + d);
     const bool newest_here = n > 0 && i0 + n == window;
     if (prefetched && newest_here) {
         load_newest(S.k, S.kd, kc, kdc, n - 1);
@@ -277,12 +283,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
             ot += S.o_rank[r][tid];
             lt += S.l_rank[r];
         }
-        a.out[h * HD + tid] = __double2float_rn(__ddiv_rn(ot, lt));
+        outv[h * HD + tid] = __double2float_rn(__ddiv_rn(ot, lt));
     }
 }
 
 template <int HD, bool Q4>
-static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
+static cudaError_t launch_attn_t(const AttnArgs &a, int splits, int n_sess, cudaStream_t s, bool pdl) {
     static unsigned long long configured = 0;
     const size_t smem = sizeof(AttnSmem<HD, Q4>);
     int dev = 0;
@@ -294,7 +300,7 @@ static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, 
         configured |= 1ull << dev;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(splits, a.n_heads);
+    cfg.gridDim = dim3(splits, a.n_heads, n_sess);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -332,14 +338,17 @@ cudaError_t configure_attention() {
                                 static_cast<int>(sizeof(AttnSmem<64, true>)));
 }
 
-cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl) {
+cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl, int n_sess) {
     if (splits <= 0 || splits > kAttnMaxSplits || a.n_ctx <= 0 || a.n_ctx > kAttnMaxCtx) return cudaErrorInvalidValue;
     if ((a.n_ctx + splits - 1) / splits > kAttnMaxPos) return cudaErrorInvalidValue;
+    if (n_sess < 1 || n_sess > 65535 || (n_sess > 1 && a.qo_stride <= 0) ||
+        ((n_sess > 1 || a.ring_of) && a.kv_sess_stride <= 0) || a.kv_sess_stride % head_dim)
+        return cudaErrorInvalidValue;
     const bool q4 = a.kv_type == kKvQ4_0;
     if (head_dim == 128)
-        return q4 ? launch_attn_t<128, true>(a, splits, s, pdl) : launch_attn_t<128, false>(a, splits, s, pdl);
+        return q4 ? launch_attn_t<128, true>(a, splits, n_sess, s, pdl) : launch_attn_t<128, false>(a, splits, n_sess, s, pdl);
     if (head_dim == 64)
-        return q4 ? launch_attn_t<64, true>(a, splits, s, pdl) : launch_attn_t<64, false>(a, splits, s, pdl);
+        return q4 ? launch_attn_t<64, true>(a, splits, n_sess, s, pdl) : launch_attn_t<64, false>(a, splits, n_sess, s, pdl);
     return cudaErrorInvalidValue;
 }
 

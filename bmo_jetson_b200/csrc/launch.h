@@ -27,7 +27,8 @@ struct GemvPlan {
 GemvPlan plan_gemv(const QMatDesc &m, int sms);
 
 // Ring decode attention (kernels/attention.cu): one cluster of `splits` CTAs per head.
-cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl);
+// n_sess > 1: grid z runs that many sessions (AttnArgs strides).
+cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl, int n_sess = 1);
 int attn_splits_for(int n_ctx);
 int attn_max_ctx();
 
@@ -51,6 +52,25 @@ int frame_max_window();
 int frame_max_tiles_per_cta();
 int frame_dep_max_window();
 int frame_dep_head_dim();
+
+// Batched sessions (kernels/batch.cu).  Stage: per-session RMSNorm + Q8_1
+// into the block-major layout (and the embedding token); GEMM: the skinny
+// Q4_0 x Q8_1 product of all sessions with a fused epilogue, `grid` CTAs
+// owning whole row tiles (at most W.n_tiles).
+cudaError_t launch_batch_stage(const BatchStageArgs &a, cudaStream_t s);
+cudaError_t launch_batch_gemm(const BatchGemmArgs &a, int epilogue, int grid, cudaStream_t s);
+size_t batch_gemm_smem_bytes();
+int batch_gemm_grid(const QMatDesc &m, int sms);
+// Embedding sums out[s][n_embd] of the first n_sess rows of `in` and their
+// RoPE tables rope[s][head_dim / 2].
+cudaError_t launch_batch_embed(const EmbTable *tables, int n_tables, const BatchIn *in, int n_embd, float *out,
+                               int n_sess, float theta, int head_dim, float2 *rope, cudaStream_t s);
+// Fills `in` from device arrays sess[n] (null: 0..n-1), tokens[n][K], pos[n].
+cudaError_t launch_batch_set_inputs(BatchIn *in, const int *sess, const int *tokens, int K, const int *pos, int n,
+                                    cudaStream_t s);
+// Greedy token of each session: first maximum of pairs[s * pairs_stride + 0..n_pairs).
+cudaError_t launch_batch_finalize(const float2 *pairs, int pairs_stride, int n_pairs, int *out, int out_stride,
+                                  int n_sess, cudaStream_t s);
 
 // Frame-start embedding sum + RoPE table (kernels/misc.cu).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,

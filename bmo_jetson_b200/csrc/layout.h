@@ -87,6 +87,12 @@ struct AttnArgs {
     float scale;
     float *out;              // [n_heads][hd]
     int *status;
+    // batched sessions (grid z): row s reads q/v_raw/out at + s * qo_stride
+    // (vraw_stride), its position at pos[s * pos_stride], and the ring of
+    // session ring_of[s] (s when null) at + ring * kv_sess_stride elements
+    long long kv_sess_stride;
+    int qo_stride, vraw_stride, pos_stride;
+    const int *ring_of;
 };
 
 struct GemvArgs {
@@ -144,6 +150,72 @@ struct FramePhase {
     GemvArgs g;
     AttnArgs at;   // kPhAttn, and the attention of a kProDepAttn prologue
     TokenSrc tok;  // kPhTokenOut
+};
+
+// ---- batched sessions (config 4) ----
+// Q8_1 activations of S sessions, block-major: block b of session s at
+// xq[(b * S + s) * 32] and xds[b * S + s] = (d8, 4 * s8).  The 8 blocks of
+// chunk kc are then one contiguous run of S * 256 bytes.
+constexpr int kBatchMax = 64;  // sessions per launch
+constexpr int kBatchMaxTokens = 64;
+
+// Per-call inputs of a batched frame (one host->device copy): row s runs
+// session sess[s] at position pos[s] on tokens[s * kBatchMaxTokens + 0..n_tok).
+struct BatchIn {
+    int32_t sess[kBatchMax];
+    int32_t pos[kBatchMax];
+    int32_t tokens[kBatchMax * kBatchMaxTokens];
+    int32_t n_tok;
+    int32_t pad[3];
+};
+
+struct BatchStageArgs {
+    const float *x;          // [S][x_stride]
+    int x_stride, cols, nbx, n_sess;
+    const float *gamma;      // RMSNorm weight, or null (plain)
+    float eps;
+    float *xn_out;           // optional [S][cols]: the normalised vectors
+    int xn_stride;
+    int8_t *xq;
+    float2 *xds;
+    // optional token lookup for an embedding-add GEMV: session s's token is the
+    // first maximum of pairs[s * pairs_stride + 0..n_pairs), or tok_in[s]
+    const float2 *pairs;
+    int pairs_stride, n_pairs;
+    const int *tok_in;
+    int *tok;                // [S] resolved tokens
+    int *tok_out;            // optional: tok_out[s * tok_out_stride]
+    int tok_out_stride;
+};
+
+struct BatchGemmArgs {
+    QMatDesc W;
+    int n_sess;
+    const int8_t *xq;
+    const float2 *xds;
+    float *y;                // [S][y_stride]
+    int y_stride;
+    const float *resid;      // [S][resid_stride]
+    int resid_stride;
+    const float *bias;
+    float2 *pairs;           // logits: per-tile (max, argmax) at pairs[s * pairs_stride + t]
+    int pairs_stride, argmax_limit;
+    // qkv epilogue
+    int q_dim, kv_dim, head_dim;
+    const float2 *rope;      // [S][head_dim / 2] or null
+    void *k_cache, *v_cache;
+    uint8_t *k_scale, *v_scale;
+    long long kv_sess_stride, kv_layer_off;
+    int kv_type, n_ctx;
+    const int *pos;          // position of row s at pos[s * pos_stride]
+    int pos_stride;
+    const int *ring_of;      // KV ring of row s: ring_of[s] (s when null)
+    float *v_out;            // raw v [S][v_out_stride]
+    int v_out_stride;
+    // embedding-add epilogue
+    EmbTable emb;
+    const int *tok;          // [S]
+    int *status;
 };
 
 }  // namespace bmo

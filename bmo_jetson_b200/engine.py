@@ -86,6 +86,18 @@ def lib() -> ctypes.CDLL:
     L.bmo_enqueue_cascade.restype = i
     L.bmo_enqueue_frame.argtypes = [vp, vp, i, i, vp]
     L.bmo_enqueue_frame.restype = i
+    L.bmo_batch_init.argtypes = [vp, i]
+    L.bmo_batch_init.restype = i
+    L.bmo_batch_sessions.argtypes = [vp]
+    L.bmo_batch_sessions.restype = i
+    L.bmo_forward_frame_batch.argtypes = [vp, i, vp, vp, i, vp, vp, vp, vp]
+    L.bmo_forward_frame_batch.restype = i
+    L.bmo_enqueue_frame_batch.argtypes = [vp, i, vp, vp, i, vp, vp]
+    L.bmo_enqueue_frame_batch.restype = i
+    L.bmo_batch_kv_import_f32.argtypes = [vp, i, i, i, i, _c_f32p, _c_f32p]
+    L.bmo_batch_kv_import_f32.restype = i
+    L.bmo_batch_reset.argtypes = [vp, i]
+    L.bmo_batch_reset.restype = i
     L.bmo_last_error.argtypes = [vp]
     L.bmo_last_error.restype = ctypes.c_char_p
     L.bmo_rvq_decode.argtypes = [vp, vp, vp, vp]
@@ -306,6 +318,56 @@ class BMOEngine:
         rc = lib().bmo_enqueue_cascade(self._h, int(text_token))
         if rc != 0:
             raise RuntimeError(f"bmo_enqueue_cascade rc={rc}: {_err(self._h)}")
+
+    # ---- batched sessions ----
+    def batch_init(self, n_sessions: int) -> None:
+        """Allocates n_sessions independent session rings (bmo_batch_init)."""
+        rc = lib().bmo_batch_init(self._h, int(n_sessions))
+        if rc != 0:
+            raise RuntimeError(f"bmo_batch_init rc={rc}: {_err(self._h)}")
+
+    @property
+    def batch_sessions(self) -> int:
+        return lib().bmo_batch_sessions(self._h)
+
+    def forward_frame_batch(self, tokens: np.ndarray, pos, sess_ids=None, want_z: bool = False,
+                            want_logits: bool = False):
+        """One greedy frame for every row of tokens [n][K]: returns (text [n],
+        audio [n][dep_q], z [n][n_embd] or None, logits [n][text_vocab] or None)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        n, K = tokens.shape
+        pos = np.ascontiguousarray(pos, np.int32).reshape(n)
+        sid = None if sess_ids is None else np.ascontiguousarray(sess_ids, np.int32).reshape(n)
+        out = np.zeros((n, 1 + self.dep_q), np.int32)
+        z = np.zeros((n, self.n_embd), np.float32) if want_z else None
+        lg = np.zeros((n, self.text_vocab), np.float32) if want_logits else None
+        rc = lib().bmo_forward_frame_batch(self._h, n, None if sid is None else sid.ctypes.data,
+                                           tokens.ctypes.data, K, pos.ctypes.data,
+                                           None if z is None else z.ctypes.data,
+                                           None if lg is None else lg.ctypes.data, out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"bmo_forward_frame_batch rc={rc}: {_err(self._h)}")
+        return out[:, 0].copy(), out[:, 1:].copy(), z, lg
+
+    def enqueue_frame_batch(self, n: int, sess_dev_ptr: int, tokens_dev_ptr: int, K: int, pos_dev_ptr: int,
+                            out_tokens_dev_ptr: int) -> None:
+        rc = lib().bmo_enqueue_frame_batch(self._h, int(n), sess_dev_ptr or None, tokens_dev_ptr, int(K),
+                                           pos_dev_ptr, out_tokens_dev_ptr or None)
+        if rc != 0:
+            raise RuntimeError(f"bmo_enqueue_frame_batch rc={rc}: {_err(self._h)}")
+
+    def batch_kv_import(self, session: int, layer: int, slot0: int, k_rows: np.ndarray, v_rows: np.ndarray) -> None:
+        k = np.ascontiguousarray(k_rows, np.float32)
+        v = np.ascontiguousarray(v_rows, np.float32)
+        rc = lib().bmo_batch_kv_import_f32(self._h, int(session), layer, slot0, k.shape[0],
+                                           k.ctypes.data_as(_c_f32p), v.ctypes.data_as(_c_f32p))
+        if rc != 0:
+            raise RuntimeError(f"bmo_batch_kv_import_f32 rc={rc}: {_err(self._h)}")
+
+    def batch_reset(self, session: int = -1) -> None:
+        rc = lib().bmo_batch_reset(self._h, int(session))
+        if rc != 0:
+            raise RuntimeError(f"bmo_batch_reset rc={rc}: {_err(self._h)}")
 
     def sync(self) -> None:
         rc = lib().bmo_sync(self._h)

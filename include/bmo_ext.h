@@ -87,6 +87,36 @@ BMO_API int bmo_enqueue_frame(bmo_handle_t *h, const int32_t *tokens_dev, int nu
 BMO_API int bmo_enqueue_temporal(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos);
 BMO_API int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token);
 
+/* ---- batched sessions ----------------------------------------------------
+ * Up to 64 independent sessions share the handle's weights; each has its own
+ * temporal ring (n_ctx slots, the handle's KV format).  One batched frame
+ * steps any subset of them together, streaming every weight once for all. */
+
+/* Allocates the rings of n_sessions sessions (1..64), empty.  Returns 0; 2 for
+ * a bad count; 3 if sessions were already allocated with another count. */
+BMO_API int bmo_batch_init(bmo_handle_t *h, int n_sessions);
+BMO_API int bmo_batch_sessions(bmo_handle_t *h);
+/* One greedy frame (as bmo_forward_frame_greedy) for each of n_rows rows: row
+ * r runs session sess_ids[r] (NULL: r; ids distinct) at absolute position
+ * pos[r] on input_tokens[r * num_codebooks + 0..num_codebooks).
+ * out_tokens[r * (1 + dep_q)] receives the text token, then the dep_q audio
+ * tokens.  out_transformer [n_rows][n_embd] (the normed hidden z) and
+ * out_text_logits [n_rows][text_vocab] may be NULL.  The handle's own
+ * single-session position and ring are untouched. */
+BMO_API int bmo_forward_frame_batch(bmo_handle_t *h, int n_rows, const int32_t *sess_ids,
+                                    const int32_t *input_tokens, int num_codebooks, const int32_t *pos,
+                                    float *out_transformer, float *out_text_logits, int32_t *out_tokens);
+/* Asynchronous form with device arrays (sess_ids_dev may be NULL); tokens
+ * land in out_tokens_dev [n_rows][1 + dep_q] on the handle's stream. */
+BMO_API int bmo_enqueue_frame_batch(bmo_handle_t *h, int n_rows, const int32_t *sess_ids_dev,
+                                    const int32_t *tokens_dev, int num_codebooks, const int32_t *pos_dev,
+                                    int32_t *out_tokens_dev);
+/* bmo_kv_import_f32 into the ring of one session. */
+BMO_API int bmo_batch_kv_import_f32(bmo_handle_t *h, int session, int layer, int slot0, int n,
+                                    const float *k_rows, const float *v_rows);
+/* Empties one session's ring (session < 0: all).  Returns 0, 2 for a bad id. */
+BMO_API int bmo_batch_reset(bmo_handle_t *h, int session);
+
 /* Waits for the handle's stream; returns the device status word (0 = ok). */
 BMO_API int bmo_sync(bmo_handle_t *h);
 

@@ -555,6 +555,10 @@ struct orc_model {
     /* state */
     void *k_cache, *v_cache;           /* [layer][kv_head][slot][hd] */
     uint16_t *dk_cache, *dv_cache;     /* depth fp16 [layer][head][slot][hd] */
+    /* independent temporal rings of batched sessions; k_cache/v_cache point
+     * at ring `cur` (ring 0 is the one kv_alloc made) */
+    void **sk, **sv;
+    int n_sess, cur;
 };
 
 static const orc_block_q4_0 *q4(const gg_tensor *t) { return (const orc_block_q4_0 *)t->data; }
@@ -567,8 +571,17 @@ static size_t kv_elems(const orc_model *m) {
 void orc_model_free(orc_model *m) {
     if (!m) return;
     gg_close(&m->g);
-    free(m->k_cache);
-    free(m->v_cache);
+    if (m->sk) {
+        for (int i = 0; i < m->n_sess; ++i) {
+            free(m->sk[i]);
+            free(m->sv[i]);
+        }
+        free(m->sk);
+        free(m->sv);
+    } else {
+        free(m->k_cache);
+        free(m->v_cache);
+    }
     free(m->dk_cache);
     free(m->dv_cache);
     free(m);
@@ -589,6 +602,35 @@ void orc_reset(orc_model *m) {
     const size_t bytes = m->kv_type == ORC_KV_F16 ? n * 2 : n / 32 * sizeof(orc_block_q4_0);
     memset(m->k_cache, 0, bytes);
     memset(m->v_cache, 0, bytes);
+}
+
+/* Batched sessions (the session-batched frame of the build's ABI extension):
+ * n independent temporal rings over the same weights. */
+int orc_sessions(orc_model *m, int n) {
+    if (!m || n < 1 || m->sk) return 1;
+    const size_t e = kv_elems(m);
+    const size_t bytes = m->kv_type == ORC_KV_F16 ? e * 2 : e / 32 * sizeof(orc_block_q4_0);
+    m->sk = (void **)calloc((size_t)n, sizeof(void *));
+    m->sv = (void **)calloc((size_t)n, sizeof(void *));
+    if (!m->sk || !m->sv) return 2;
+    m->sk[0] = m->k_cache;
+    m->sv[0] = m->v_cache;
+    m->n_sess = n;
+    for (int i = 1; i < n; ++i) {
+        m->sk[i] = calloc(1, bytes);
+        m->sv[i] = calloc(1, bytes);
+        if (!m->sk[i] || !m->sv[i]) return 2;
+    }
+    m->cur = 0;
+    return 0;
+}
+
+int orc_select_session(orc_model *m, int s) {
+    if (!m || !m->sk || s < 0 || s >= m->n_sess) return 1;
+    m->cur = s;
+    m->k_cache = m->sk[s];
+    m->v_cache = m->sv[s];
+    return 0;
 }
 
 void orc_reset_depth_kv(orc_model *m) {

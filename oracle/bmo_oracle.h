@@ -88,6 +88,11 @@ int orc_forward_depth_cascade_greedy(orc_model *m, int32_t text_token,
  * [slot0, slot0+n) of one temporal layer; rows are [n][n_kv_heads*head_dim]. */
 int orc_kv_import(orc_model *m, int layer, int slot0, int n,
                   const float *k_rows, const float *v_rows);
+/* Batched sessions: orc_sessions(m, n) gives the model n independent
+ * temporal rings (ring 0 is its existing one, the others start empty);
+ * orc_select_session(m, s) points every call above at ring s. */
+int orc_sessions(orc_model *m, int n);
+int orc_select_session(orc_model *m, int s);
 /* Read the temporal cache back as fp32 [n][n_kv_heads*head_dim] (which: 0=K, 1=V). */
 int orc_kv_export(orc_model *m, int which, int layer, int slot0, int n,
                   float *out);

@@ -67,6 +67,8 @@ def lib() -> ctypes.CDLL:
         L.orc_forward_depth_cascade_greedy.argtypes = [ctypes.c_void_p, ctypes.c_int32, _f32p, _i32p]
         L.orc_kv_import.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
         L.orc_kv_export.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
+        L.orc_sessions.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.orc_select_session.argtypes = [ctypes.c_void_p, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -174,6 +176,22 @@ class OracleModel:
 
     def reset(self):
         self._L.orc_reset(self._m)
+
+    def sessions(self, n):
+        """Gives the model n independent temporal rings (ring 0 is the current one)."""
+        if self._L.orc_sessions(self._m, n):
+            raise RuntimeError("oracle sessions failed")
+
+    def select(self, s):
+        """Points every later call at ring s."""
+        if self._L.orc_select_session(self._m, s):
+            raise RuntimeError(f"oracle select_session({s}) failed")
+
+    def frame_greedy(self, tokens, pos):
+        """One greedy frame of the current ring: (z, logits, text token, audio tokens)."""
+        z, logits, _ = self.forward_temporal(tokens, pos)
+        text = int(np.argmax(logits[:self.text_vocab]))
+        return z, logits, text, self.depth_cascade_greedy(text, z)
 
     def embed(self, tokens):
         t = np.ascontiguousarray(tokens, np.int32)

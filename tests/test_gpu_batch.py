@@ -1,0 +1,149 @@
+"""GPU parity of batched sessions (bmo_forward_frame_batch): every row of a
+batched frame is the single-session greedy frame of its own session, checked
+against the CPU oracle running each session on its own ring.
+
+Bars as the single-session tests: hidden states and logits within 1e-5
+relative L2 of the oracle (north-star bar 1e-3), greedy text and audio
+tokens identical.  A row's result does not depend on which other rows share
+its frame, so rows of a 64-session frame are also checked bit-for-bit
+against the same rows run alone.
+"""
+import numpy as np
+import pytest
+
+from bmo_jetson_b200 import engine, synth
+from oracle import oracle as orc
+from tests.parity import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def tokens_for(rng, K, text_vocab, audio_vocab):
+    t = np.concatenate([[rng.integers(0, text_vocab)], rng.integers(0, audio_vocab, K - 1)]).astype(np.int32)
+    if rng.random() < 0.3:
+        t[1] = -1                 # "no token yet" channel is skipped
+    if rng.random() < 0.3:
+        t[-1] = audio_vocab + 5   # out-of-range channel is skipped
+    return t
+
+
+def check_rows(o, sess, pos, toks, text, audio, z, lg, what):
+    for r, s in enumerate(sess):
+        o.select(int(s))
+        zo, lo, to, ao = o.frame_greedy(toks[r], int(pos[r]))
+        assert rel_l2(z[r], zo) < TOL, (what, r, rel_l2(z[r], zo))
+        assert rel_l2(lg[r], lo) < TOL, (what, r, rel_l2(lg[r], lo))
+        assert int(text[r]) == to, (what, r)
+        np.testing.assert_array_equal(audio[r], ao, err_msg=f"{what} row {r}")
+
+
+@pytest.mark.parametrize("kv_type", [0, 1])
+def test_batched_frames_match_oracle_per_session(tiny_model, kv_type):
+    n_ctx, n_sess = 16, 6
+    e = engine.BMOEngine(tiny_model, n_ctx=n_ctx, kv_type=kv_type)
+    o = orc.OracleModel(tiny_model, n_ctx=n_ctx, kv_type=kv_type)
+    e.batch_init(n_sess)
+    assert e.batch_sessions == n_sess
+    o.sessions(n_sess)
+    rng = np.random.default_rng(100 + kv_type)
+    width = e.n_kv_heads * e.head_dim
+    # distinct seeded history per session, some rings full
+    for s in range(n_sess):
+        o.select(s)
+        n_hist = [0, 5, n_ctx, n_ctx, 9, n_ctx][s]
+        for layer in range(e.n_layers):
+            if n_hist == 0:
+                continue
+            k = rng.standard_normal((n_hist, width), dtype=np.float32)
+            v = rng.standard_normal((n_hist, width), dtype=np.float32)
+            e.batch_kv_import(s, layer, 0, k, v)
+            o.kv_import(layer, 0, k, v)
+    # positions: empty ring, partial window, exactly full, wrapped
+    pos = np.array([0, 5, n_ctx - 1, 40, 9, 100], np.int32)
+    K = e.n_codebooks
+    for frame in range(3):
+        # all rows, a permuted subset, then a single row
+        sess = [np.arange(n_sess), rng.permutation(n_sess)[:4], np.array([3])][frame]
+        toks = np.stack([tokens_for(rng, K, e.text_vocab, e.audio_vocab) for _ in sess])
+        p = pos[sess]
+        text, audio, z, lg = e.forward_frame_batch(toks, p, sess_ids=sess, want_z=True, want_logits=True)
+        assert text.shape == (len(sess),) and audio.shape == (len(sess), e.dep_q)
+        check_rows(o, sess, p, toks, text, audio, z, lg, f"frame {frame}")
+        pos[sess] += 1
+    e.close()
+    o.close()
+
+
+def test_batched_frame_argument_errors(tiny_model):
+    e = engine.BMOEngine(tiny_model, n_ctx=16)
+    toks = np.zeros((2, e.n_codebooks), np.int32)
+    with pytest.raises(RuntimeError):
+        e.forward_frame_batch(toks, [0, 0])            # no bmo_batch_init yet
+    with pytest.raises(RuntimeError):
+        e.batch_init(65)
+    e.batch_init(2)
+    with pytest.raises(RuntimeError):
+        e.batch_init(3)                                 # already allocated with another count
+    e.batch_init(2)                                     # same count: no-op
+    with pytest.raises(RuntimeError):
+        e.forward_frame_batch(toks, [0, 0], sess_ids=[1, 1])   # repeated session
+    with pytest.raises(RuntimeError):
+        e.forward_frame_batch(toks, [0, 0], sess_ids=[0, 2])   # unknown session
+    with pytest.raises(RuntimeError):
+        e.forward_frame_batch(toks, [0, -1])                   # negative position
+    with pytest.raises(RuntimeError):
+        e.forward_frame_batch(np.zeros((3, e.n_codebooks), np.int32), [0, 0, 0])  # more rows than sessions
+    text, audio, _, _ = e.forward_frame_batch(toks, [0, 0])
+    assert text.shape == (2,) and audio.shape == (2, e.dep_q)
+    # the single-session path is unaffected by the batch state
+    e.pos = 0
+    e.forward_frame_greedy(toks[0])
+    e.batch_reset()
+    e.close()
+
+
+@pytest.fixture(scope="module")
+def full_model(model_dir):
+    return synth.ensure_model("config2", model_dir)
+
+
+def test_full_size_batch_matches_oracle_and_is_row_independent(full_model):
+    """Config-2 model with Q4 rings: 4 sessions on the oracle, then a
+    64-session frame at positions uniform in [0, 3000) whose rows equal the
+    same rows run alone (a frame rewrites the same ring slot with the same
+    K/V, so re-running a row at its position is idempotent)."""
+    n_ctx = 512
+    e = engine.BMOEngine(full_model, n_ctx=n_ctx, kv_type=1)
+    e.batch_init(64)
+    o = orc.OracleModel(full_model, n_ctx=n_ctx, kv_type=1)
+    o.sessions(4)
+    rng = np.random.default_rng(7)
+    width = e.n_kv_heads * e.head_dim
+    hist = [rng.standard_normal((n_ctx, width), dtype=np.float32) for _ in range(2)]
+    for s in range(4):
+        o.select(s)
+        for layer in range(e.n_layers):
+            # shared history, rolled per session so the rings differ
+            k, v = np.roll(hist[0], 37 * s, axis=0), np.roll(hist[1], 11 * s, axis=0)
+            e.batch_kv_import(s, layer, 0, k, v)
+            o.kv_import(layer, 0, k, v)
+    K = e.n_codebooks
+    sess = np.array([2, 0, 3, 1], np.int32)
+    pos = np.array([700, 130, 2999, 511], np.int32)
+    toks = np.stack([tokens_for(rng, K, e.text_vocab, e.audio_vocab) for _ in sess])
+    text, audio, z, lg = e.forward_frame_batch(toks, pos, sess_ids=sess, want_z=True, want_logits=True)
+    check_rows(o, sess, pos, toks, text, audio, z, lg, "config2")
+    o.close()
+
+    pos64 = rng.integers(0, 3000, 64).astype(np.int32)
+    toks64 = np.stack([tokens_for(rng, K, e.text_vocab, e.audio_vocab) for _ in range(64)])
+    t64, a64, z64, _ = e.forward_frame_batch(toks64, pos64, want_z=True)
+    assert (t64 >= 0).all() and (t64 < e.text_vocab).all() and (a64 >= 0).all() and (a64 < 2048).all()
+    for r in (0, 17, 63):
+        t1, a1, z1, _ = e.forward_frame_batch(toks64[r:r + 1], pos64[r:r + 1], sess_ids=[r], want_z=True)
+        assert t1[0] == t64[r]
+        np.testing.assert_array_equal(a1[0], a64[r])
+        np.testing.assert_array_equal(z1[0], z64[r])
+    e.close()
