@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <stdexcept>
@@ -49,7 +50,7 @@ struct Engine::BatchState {
     float2 *rope = nullptr, *tpairs = nullptr;
     int tpairs_stride = 1;
     int8_t *xq = nullptr;
-    float2 *xds = nullptr;
+    float *xds = nullptr;
     int *tok = nullptr;
     // depformer, per row
     __half *dk = nullptr, *dv = nullptr;
@@ -62,6 +63,11 @@ struct Engine::BatchState {
     // host outputs (pinned)
     int *tok_h = nullptr;
     float *z_h = nullptr, *logits_h = nullptr;
+    // tensor-core GEMM: split-row-block partials and their counters
+    float *ws = nullptr;
+    int *cnt = nullptr;
+    int n_cnt = 0;
+    bool simt = true;  // CUDA-core GEMM with the batch-1 rounding (BMO_BATCH_SIMT=0: tensor cores)
     std::vector<void *> dev, host;
     std::map<int, cudaGraphExec_t> graphs;  // batched frame by row count
 };
@@ -76,6 +82,11 @@ void Engine::BatchDeleter::operator()(BatchState *b) const {
 }
 
 int Engine::batch_sessions() const { return batch_ ? batch_->n_max : 0; }
+
+void Engine::batch_clear_counters(cudaStream_t s) {
+    if (!batch_) return;
+    cudaMemsetAsync(batch_->cnt, 0, sizeof(int) * batch_->n_cnt, s);
+}
 
 int Engine::batch_init(int n_sessions) {
     if (n_sessions < 1 || n_sessions > kBatchMax) return 1;
@@ -137,8 +148,28 @@ int Engine::batch_init(int n_sessions) {
     for (int k = 0; k < kDepQMax; ++k) { widest(dep_in_[k]); widest(dep_head_[k]); }
     for (auto &d : D_)
         for (int s = 0; s < kDepQMax; ++s) { widest(d.qkv[s]); widest(d.wo[s]); widest(d.ffn_in[s]); widest(d.ffn_out[s]); }
+    // tensor-core GEMM workspace for the most split matrix
+    size_t ws_floats = 0;
+    int n_super = 1;
+    auto ws_need = [&](const QMatDesc &m) {
+        if (!m.tiles) return;
+        ws_floats = std::max(ws_floats, batch_mma_ws_floats(m, sm_count));
+        n_super = std::max(n_super, (m.n_tiles + 3) / 4);
+    };
+    for (auto &l : L_) { ws_need(l.qkv); ws_need(l.wo); ws_need(l.ffn_in); ws_need(l.ffn_out); }
+    ws_need(text_head_);
+    for (int k = 0; k < kDepQMax; ++k) { ws_need(dep_in_[k]); ws_need(dep_head_[k]); }
+    for (auto &d : D_)
+        for (int s = 0; s < kDepQMax; ++s) { ws_need(d.qkv[s]); ws_need(d.wo[s]); ws_need(d.ffn_in[s]); ws_need(d.ffn_out[s]); }
+    b->ws = static_cast<float *>(dalloc(sizeof(float) * ws_floats));
+    b->cnt = static_cast<int *>(dalloc(sizeof(int) * n_super));
+    b->n_cnt = n_super;
+    // the CUDA-core GEMM keeps the batch-1 rounding; BMO_BATCH_SIMT=0 selects the
+    // tensor-core GEMM with fp32 block scaling
+    const char *simt = std::getenv("BMO_BATCH_SIMT");
+    b->simt = !simt || std::atoi(simt) != 0;
     b->xq = static_cast<int8_t *>(dalloc(static_cast<size_t>(nbx) * S * 32));
-    b->xds = static_cast<float2 *>(dalloc(sizeof(float2) * static_cast<size_t>(nbx) * S));
+    b->xds = static_cast<float *>(dalloc(sizeof(float) * 2 * static_cast<size_t>(nbx) * S));
     b->tok = static_cast<int *>(dalloc(sizeof(int) * S));
 
     b->dsess_elems = static_cast<long long>(kDepLayers) * dep_heads * std::max(dep_n_ctx, 1) * dep_hd;
@@ -195,7 +226,16 @@ void Engine::batch_stage(cudaStream_t s, int n, const float *x, int cols, const 
 }
 
 void Engine::batch_gemm(cudaStream_t s, const BatchGemmArgs &a, int epi) {
-    ck(launch_batch_gemm(a, epi, batch_gemm_grid(a.W, sm_count), s), "launch batch gemm");
+    BatchState &b = *batch_;
+    if (b.simt) {
+        ck(launch_batch_gemm(a, epi, batch_gemm_grid(a.W, sm_count), s), "launch batch gemm");
+        return;
+    }
+    BatchGemmArgs m = a;
+    m.ws = b.ws;
+    m.cnt = b.cnt;
+    m.max_contrib = batch_mma_max_contrib(a.W, sm_count);
+    ck(launch_batch_mma(m, epi, sm_count, s), "launch batch mma");
 }
 
 void Engine::enqueue_batch_temporal(cudaStream_t s, int n) {

@@ -893,6 +893,7 @@ void Engine::finish_call() {
         const int st = *status_h_;
         cudaMemsetAsync(status_, 0, sizeof(int), stream);
         cudaMemsetAsync(gcount_, 0, gcount_bytes_, stream);
+        batch_clear_counters(stream);
         cudaStreamSynchronize(stream);
         std::string what;
         if (st & (1 << 1)) what += " a bulk copy wait timed out;";

@@ -153,6 +153,7 @@ private:
     };
     std::unique_ptr<BatchState, BatchDeleter> batch_;
     void enqueue_batch_frame(cudaStream_t s, int n);
+    void batch_clear_counters(cudaStream_t s);  // after a device error
     void enqueue_batch_temporal(cudaStream_t s, int n);
     void enqueue_batch_cascade(cudaStream_t s, int n);
     void batch_stage(cudaStream_t s, int n, const float *x, int cols, const QMatDesc &W, const float *gamma,

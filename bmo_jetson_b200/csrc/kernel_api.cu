@@ -132,6 +132,77 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
     return static_cast<int>(launch_gemv(a, pro, epi, static_cast<int>(g), static_cast<cudaStream_t>(stream), false));
 }
 
+namespace {
+struct BatchScratch {
+    size_t xq, xds, ws, cnt, status, total;
+};
+BatchScratch batch_scratch_layout(const QMatDesc &m, int n_sess, int sms) {
+    BatchScratch b{};
+    const size_t P = static_cast<size_t>(batch_pad(n_sess));
+    b.xq = 0;
+    b.xds = align256(static_cast<size_t>(m.nbx) * P * 32);
+    b.ws = b.xds + align256(static_cast<size_t>(m.nbx) * P * 2 * sizeof(float));
+    b.cnt = b.ws + align256(batch_mma_ws_floats(m, sms) * sizeof(float));
+    b.status = b.cnt + align256(static_cast<size_t>(m.n_tiles) * sizeof(int));
+    b.total = b.status + 256;
+    return b;
+}
+int device_sms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+}  // namespace
+
+size_t bmo_k_batch_gemm_scratch_bytes(int rows, int cols, int perm, int swiglu_f, int n_sess) {
+    if (!shape_ok(rows, cols, perm, swiglu_f) || n_sess < 1 || n_sess > kBatchMax) return 0;
+    return batch_scratch_layout(make_desc(nullptr, rows, cols, perm, swiglu_f), n_sess, device_sms()).total;
+}
+
+int bmo_k_batch_gemm_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
+                          const float *gamma_dev, float eps, const float *resid_dev, float *y_dev, int n_sess,
+                          int tensor_cores, void *scratch_dev, size_t scratch_bytes, void *stream) {
+    if (!tiled_dev || !x_dev || !y_dev || !scratch_dev || !shape_ok(rows, cols, perm, swiglu_f) || n_sess < 1 ||
+        n_sess > kBatchMax)
+        return static_cast<int>(cudaErrorInvalidValue);
+    const int sms = device_sms();
+    const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
+    const BatchScratch L = batch_scratch_layout(m, n_sess, sms);
+    if (scratch_bytes < L.total) return static_cast<int>(cudaErrorInvalidValue);
+    uint8_t *sc = static_cast<uint8_t *>(scratch_dev);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    BatchStageArgs st{};
+    st.x = x_dev;
+    st.x_stride = cols;
+    st.cols = cols;
+    st.nbx = m.nbx;
+    st.n_sess = n_sess;
+    st.gamma = gamma_dev;
+    st.eps = eps;
+    st.xq = reinterpret_cast<int8_t *>(sc + L.xq);
+    st.xds = reinterpret_cast<float *>(sc + L.xds);
+    cudaError_t e = launch_batch_stage(st, s);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    BatchGemmArgs a{};
+    a.W = m;
+    a.n_sess = n_sess;
+    a.xq = st.xq;
+    a.xds = st.xds;
+    a.y = y_dev;
+    a.y_stride = perm == kPermSwiGLU ? swiglu_f : rows;
+    a.resid = resid_dev;
+    a.resid_stride = rows;
+    a.argmax_limit = INT_MAX;
+    a.status = reinterpret_cast<int *>(sc + L.status);
+    a.ws = reinterpret_cast<float *>(sc + L.ws);
+    a.cnt = reinterpret_cast<int *>(sc + L.cnt);
+    a.max_contrib = batch_mma_max_contrib(m, sms);
+    const int epi = perm == kPermSwiGLU ? kEpiSwiGLU : (resid_dev ? kEpiResid : kEpiStore);
+    e = tensor_cores ? launch_batch_mma(a, epi, sms, s) : launch_batch_gemm(a, epi, batch_gemm_grid(m, sms), s);
+    return static_cast<int>(e);
+}
+
 int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
                            void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev, int head_dim,
                            int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev, int layer, int kv_type,

@@ -22,6 +22,8 @@
 //    (RoPE + KV append into the session's ring, SwiGLU, residual, logits +
 //    argmax, embedding add) runs per lane with no cross-warp reduction.
 // Every mbarrier wait is bounded; a timeout raises the status word.
+#include <atomic>
+
 #include "gemv_dev.cuh"
 #include "../launch.h"
 
@@ -32,7 +34,7 @@ constexpr int kBtThreads = kBtWarps * 32;
 constexpr int kBtTeams = 4;
 constexpr int kBtSlots = 2;
 constexpr int kBtXqBytes = kBatchMax * 8 * 32;   // Q8_1 quants of one chunk, all sessions
-constexpr int kBtXdsBytes = kBatchMax * 8 * 8;   // their (d8, 4 s8)
+constexpr int kBtXdsBytes = kBatchMax * 8 * 8;   // their scale pairs
 constexpr int kBtSlotBytes = kChunkBytes + kBtXqBytes + kBtXdsBytes;
 static_assert(kBtSlotBytes % 16 == 0, "bulk-copy destinations stay 16-byte aligned");
 static_assert(kBatchMax <= 2 * 32, "two warps of a team cover the sessions");
@@ -59,7 +61,7 @@ __global__ void __launch_bounds__(256) batch_stage_kernel(const __grid_constant_
     __shared__ int tok_i[8];
     const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float *x = a.x + static_cast<long long>(s) * a.x_stride;
-    const int nb = a.cols / 32, S = a.n_sess;
+    const int nb = a.cols / 32, P = batch_pad(a.n_sess);
     if (a.tok) {
         TokenSrc src{};
         src.pairs = a.pairs ? a.pairs + static_cast<long long>(s) * a.pairs_stride : nullptr;
@@ -90,12 +92,15 @@ __global__ void __launch_bounds__(256) batch_stage_kernel(const __grid_constant_
         scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(static_cast<double>(mean_eps))));
     }
     for (int b = tid; b < a.nbx; b += 256) {
-        int4 *qd = reinterpret_cast<int4 *>(a.xq + (static_cast<long long>(b) * S + s) * 32);
-        float2 *dd = a.xds + static_cast<long long>(b) * S + s;
+        // canonical K-major layout: the two 16-byte halves of a session's block are 128 bytes apart
+        int8_t *qb = a.xq + static_cast<long long>(b) * P * 32 + (s >> 3) * 256 + (s & 7) * 16;
+        int4 *q0 = reinterpret_cast<int4 *>(qb), *q1 = reinterpret_cast<int4 *>(qb + 128);
+        float *dd = a.xds + static_cast<long long>(b) * P * 2 + (s >> 1) * 4 + (s & 1);
         if (b >= nb) {
-            qd[0] = make_int4(0, 0, 0, 0);
-            qd[1] = make_int4(0, 0, 0, 0);
-            *dd = make_float2(0.0f, 0.0f);
+            *q0 = make_int4(0, 0, 0, 0);
+            *q1 = make_int4(0, 0, 0, 0);
+            dd[0] = 0.0f;
+            dd[2] = 0.0f;
             continue;
         }
         float v[32];
@@ -113,9 +118,10 @@ __global__ void __launch_bounds__(256) batch_stage_kernel(const __grid_constant_
         int8_t q[32];
         const __half2 ds = quant_block_q8_1(v, q);
         const int *qi = reinterpret_cast<const int *>(q);
-        qd[0] = make_int4(qi[0], qi[1], qi[2], qi[3]);
-        qd[1] = make_int4(qi[4], qi[5], qi[6], qi[7]);
-        *dd = make_float2(__low2float(ds), 4.0f * __high2float(ds));
+        *q0 = make_int4(qi[0], qi[1], qi[2], qi[3]);
+        *q1 = make_int4(qi[4], qi[5], qi[6], qi[7]);
+        dd[0] = __low2float(ds);
+        dd[2] = -8.0f * __high2float(ds);
     }
 }
 
@@ -245,12 +251,12 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int team = warp >> 1, g = warp & 1;
     const int G = gridDim.x, c = blockIdx.x;
-    const int cpt = a.W.cpt, ns = a.n_sess;
+    const int cpt = a.W.cpt, ns = a.n_sess, P = batch_pad(ns);
     const int t0 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * c / G);
     const int t1 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * (c + 1) / G);
     const int n_tiles_team = t1 - t0 > team ? (t1 - t0 - team + kBtTeams - 1) / kBtTeams : 0;
     const int units = n_tiles_team * cpt;
-    const uint32_t xqb = static_cast<uint32_t>(ns) * 256u, xdsb = static_cast<uint32_t>(ns) * 64u;
+    const uint32_t xqb = static_cast<uint32_t>(P) * 256u, xdsb = static_cast<uint32_t>(P) * 64u;
 
     if (tid < kBtTeams * kBtSlots) {
         mbar_init(&S.full[tid / kBtSlots][tid % kBtSlots], 1);
@@ -270,8 +276,8 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
         uint64_t *bar = &S.full[team][sl];
         mbar_arrive_expect_tx(bar, kChunkBytes + xqb + xdsb);
         bulk_load(dst, a.W.tiles + (static_cast<size_t>(t) * cpt + kc) * kChunkBytes, kChunkBytes, bar, pol_w);
-        bulk_load(dst + kChunkBytes, a.xq + static_cast<size_t>(kc) * 8 * ns * 32, xqb, bar, pol_x);
-        bulk_load(dst + kChunkBytes + kBtXqBytes, a.xds + static_cast<size_t>(kc) * 8 * ns, xdsb, bar, pol_x);
+        bulk_load(dst + kChunkBytes, a.xq + static_cast<size_t>(kc) * 8 * P * 32, xqb, bar, pol_x);
+        bulk_load(dst + kChunkBytes + kBtXqBytes, a.xds + static_cast<size_t>(kc) * 8 * P * 2, xdsb, bar, pol_x);
     };
     int issued = 0;  // meaningful in the issuing thread only
     if (issuer)
@@ -294,16 +300,17 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
         consumed = u + 1;
         const uint8_t *w = S.slot[team][sl];
         const int8_t *xq = reinterpret_cast<const int8_t *>(w + kChunkBytes);
-        const float2 *xds = reinterpret_cast<const float2 *>(w + kChunkBytes + kBtXqBytes);
+        const float *xds = reinterpret_cast<const float *>(w + kChunkBytes + kBtXqBytes);
 #pragma unroll 1
         for (int blk = 0; blk < kChunkBlocks; ++blk) {
             int4 xa = make_int4(0, 0, 0, 0), xb = make_int4(0, 0, 0, 0);
             float2 ds = make_float2(0.0f, 0.0f);
             if (act) {
-                const int4 *xp = reinterpret_cast<const int4 *>(xq + (blk * ns + sess) * 32);
-                xa = xp[0];
-                xb = xp[1];
-                ds = xds[blk * ns + sess];
+                const int8_t *xp = xq + blk * P * 32 + (sess >> 3) * 256 + (sess & 7) * 16;
+                xa = *reinterpret_cast<const int4 *>(xp);
+                xb = *reinterpret_cast<const int4 *>(xp + 128);
+                const float *dp = xds + blk * P * 2 + (sess >> 1) * 4 + (sess & 1);
+                ds = make_float2(dp[0], -0.5f * dp[2]);  // (d8, 4 s8)
             }
             const uint8_t *wb = w + blk * 512;
             const __half *db = reinterpret_cast<const __half *>(w + kChunkQsBytes + blk * 64);
@@ -431,17 +438,29 @@ static cudaError_t configure_bg() {
                                 static_cast<int>(sizeof(BatchSmem)));
 }
 
+static std::atomic<unsigned long long> g_bg_configured{0};  // bit per device
+
 cudaError_t configure_batch() {
     const cudaError_t es[] = {configure_bg<kEpiStore>(), configure_bg<kEpiResid>(), configure_bg<kEpiSwiGLU>(),
                               configure_bg<kEpiQKV>(),   configure_bg<kEpiLogits>(), configure_bg<kEpiEmbAdd>()};
     for (cudaError_t e : es)
         if (e != cudaSuccess) return e;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev < 64) g_bg_configured.fetch_or(1ull << dev);
     return cudaSuccess;
+}
+
+static cudaError_t ensure_bg_configured() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev < 64 && (g_bg_configured.load() & (1ull << dev))) return cudaSuccess;
+    return configure_batch();
 }
 
 cudaError_t launch_batch_gemm(const BatchGemmArgs &a, int epi, int grid, cudaStream_t s) {
     if (a.n_sess < 1 || a.n_sess > kBatchMax || grid <= 0 || grid > a.W.n_tiles || a.W.cpt <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(a.xq) & 15) || (reinterpret_cast<uintptr_t>(a.xds) & 15)) return cudaErrorInvalidValue;
+    const cudaError_t ce = ensure_bg_configured();
+    if (ce != cudaSuccess) return ce;
     switch (epi) {
     case kEpiStore: return launch_bg<kEpiStore>(a, grid, s);
     case kEpiResid: return launch_bg<kEpiResid>(a, grid, s);

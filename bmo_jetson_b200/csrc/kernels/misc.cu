@@ -123,11 +123,13 @@ __global__ void finalize_token_kernel(const float2 *pairs, int n, int *out) {
 cudaError_t configure_gemv();
 cudaError_t configure_attention();
 cudaError_t configure_batch();
+cudaError_t configure_batch_mma();
 
 cudaError_t configure_kernels() {
     cudaError_t e = configure_gemv();
     if (e == cudaSuccess) e = configure_attention();
-    return e != cudaSuccess ? e : configure_batch();
+    if (e == cudaSuccess) e = configure_batch();
+    return e != cudaSuccess ? e : configure_batch_mma();
 }
 
 cudaError_t launch_finalize_token(const float2 *pairs, int n, int *out, cudaStream_t s, bool pdl) {

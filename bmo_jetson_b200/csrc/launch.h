@@ -61,6 +61,15 @@ cudaError_t launch_batch_stage(const BatchStageArgs &a, cudaStream_t s);
 cudaError_t launch_batch_gemm(const BatchGemmArgs &a, int epilogue, int grid, cudaStream_t s);
 size_t batch_gemm_smem_bytes();
 int batch_gemm_grid(const QMatDesc &m, int sms);
+// Tensor-core form of the batched GEMM (kernels/batch_mma.cu): one CTA per SM
+// (at most the unit count), stream-K over (128-row block, chunk) units.
+// Split row blocks need a.ws (batch_mma_ws_floats) and a.cnt (one zeroed int
+// per 128-row block) with a.max_contrib >= batch_mma_max_contrib.
+cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epilogue, int sms, cudaStream_t s);
+int batch_mma_grid(const QMatDesc &m, int sms);
+int batch_mma_max_contrib(const QMatDesc &m, int sms);
+size_t batch_mma_ws_floats(const QMatDesc &m, int sms);
+size_t batch_mma_smem_bytes();
 // Embedding sums out[s][n_embd] of the first n_sess rows of `in` and their
 // RoPE tables rope[s][head_dim / 2].
 cudaError_t launch_batch_embed(const EmbTable *tables, int n_tables, const BatchIn *in, int n_embd, float *out,

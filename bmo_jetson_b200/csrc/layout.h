@@ -153,10 +153,19 @@ struct FramePhase {
 };
 
 // ---- batched sessions (config 4) ----
-// Q8_1 activations of S sessions, block-major: block b of session s at
-// xq[(b * S + s) * 32] and xds[b * S + s] = (d8, 4 * s8).  The 8 blocks of
-// chunk kc are then one contiguous run of S * 256 bytes.
+// Q8_1 activations of S sessions, block-major, padded to P = S rounded up to
+// 16 sessions.  Block b occupies P * 32 bytes at xq + b * P * 32 in the
+// tensor core's K-major canonical layout (8-session x 16-byte core
+// matrices): bytes 0-15 of session s at (s / 8) * 256 + (s % 8) * 16, bytes
+// 16-31 at the same + 128.  Its scales are P floats pairs at xds + b * P * 2:
+// session pair p = s / 2 holds {d8[2p], d8[2p+1], -8 s8[2p], -8 s8[2p+1]}.
+// The 8 blocks of chunk kc are one contiguous run of P * 256 bytes (and
+// P * 64 bytes of scales), one bulk copy each.
 constexpr int kBatchMax = 64;  // sessions per launch
+#if defined(__CUDACC__)
+__host__ __device__
+#endif
+constexpr int batch_pad(int n_sess) { return (n_sess + 15) & ~15; }
 constexpr int kBatchMaxTokens = 64;
 
 // Per-call inputs of a batched frame (one host->device copy): row s runs
@@ -177,7 +186,7 @@ struct BatchStageArgs {
     float *xn_out;           // optional [S][cols]: the normalised vectors
     int xn_stride;
     int8_t *xq;
-    float2 *xds;
+    float *xds;
     // optional token lookup for an embedding-add GEMV: session s's token is the
     // first maximum of pairs[s * pairs_stride + 0..n_pairs), or tok_in[s]
     const float2 *pairs;
@@ -192,7 +201,7 @@ struct BatchGemmArgs {
     QMatDesc W;
     int n_sess;
     const int8_t *xq;
-    const float2 *xds;
+    const float *xds;
     float *y;                // [S][y_stride]
     int y_stride;
     const float *resid;      // [S][resid_stride]
@@ -216,6 +225,12 @@ struct BatchGemmArgs {
     EmbTable emb;
     const int *tok;          // [S]
     int *status;
+    // tensor-core path: split row blocks combine through ws (fp32 partial
+    // sums, [row block][contributor][P][128]) and cnt (one zeroed counter per
+    // 128-row block)
+    float *ws;
+    int *cnt;
+    int max_contrib;
 };
 
 }  // namespace bmo

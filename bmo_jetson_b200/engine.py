@@ -118,6 +118,10 @@ def lib() -> ctypes.CDLL:
     L.bmo_k_gemv_q4_0.restype = i
     L.bmo_k_gemv_q4_0_static.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, vp, vp, i, vp]
     L.bmo_k_gemv_q4_0_static.restype = i
+    L.bmo_k_batch_gemm_scratch_bytes.argtypes = [i, i, i, i, i]
+    L.bmo_k_batch_gemm_scratch_bytes.restype = sz
+    L.bmo_k_batch_gemm_q4_0.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, i, i, vp, sz, vp]
+    L.bmo_k_batch_gemm_q4_0.restype = i
     L.bmo_k_decode_attention.argtypes = [vp] * 8 + [i] * 4 + [vp, i, i, vp]
     L.bmo_k_decode_attention.restype = i
     _lib = L

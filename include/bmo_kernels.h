@@ -77,6 +77,22 @@ BMO_API int bmo_k_gemv_q4_0_static(const void *tiled_dev, int rows, int cols, in
                                    const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
                                    float *y_dev, void *q8_out_dev, float *xn_out_dev, int grid, void *stream);
 
+/* Scratch bytes bmo_k_batch_gemm_q4_0 needs (on the current device). */
+BMO_API size_t bmo_k_batch_gemm_scratch_bytes(int rows, int cols, int perm, int swiglu_f, int n_sess);
+/* The batched decode's GEMM (no reference counterpart: the reference decodes
+ * one session): for each of n_sess (1..64) sessions, y[s] = W x[s] with the
+ * Q4_0 x Q8_1 arithmetic of bmo_k_gemv_q4_0.  x_dev [n_sess][cols], y_dev
+ * [n_sess][rows] ([n_sess][swiglu_f] for perm SWIGLU); gamma_dev and
+ * resid_dev ([n_sess][rows]) as in bmo_k_gemv_q4_0.  tensor_cores = 1: int8
+ * tcgen05 MMA per 32-column block into tensor memory, block scales applied
+ * in fp32 (agrees with the reference to fp32 rounding); 0: CUDA cores with
+ * the batch-1 GEMV's rounding.  scratch_dev must be zero on the first call
+ * and is left reusable by every call that returns 0. */
+BMO_API int bmo_k_batch_gemm_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                                  const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
+                                  float *y_dev, int n_sess, int tensor_cores, void *scratch_dev,
+                                  size_t scratch_bytes, void *stream);
+
 /* Appends k, v (fp32, [n_kv_heads][head_dim]) at ring slot pos % n_ctx of
  * `layer`, then attends q over the window (replaces launch_decode_attention,
  * bmo.h:414-428).  Caches are [n_layers][n_kv_heads][n_ctx][head_dim] in
