@@ -67,7 +67,7 @@ struct Engine::BatchState {
     float *ws = nullptr;
     int *cnt = nullptr;
     int n_cnt = 0;
-    bool simt = true;  // CUDA-core GEMM with the batch-1 rounding (BMO_BATCH_SIMT=0: tensor cores)
+    int gemm = 1;  // 0 CUDA cores, 1 tensor cores (batch-1 rounding), 2 tensor cores (fp32 block sums)
     std::vector<void *> dev, host;
     std::map<int, cudaGraphExec_t> graphs;  // batched frame by row count
 };
@@ -164,12 +164,17 @@ int Engine::batch_init(int n_sessions) {
     b->ws = static_cast<float *>(dalloc(sizeof(float) * ws_floats));
     b->cnt = static_cast<int *>(dalloc(sizeof(int) * n_super));
     b->n_cnt = n_super;
-    // the CUDA-core GEMM keeps the batch-1 rounding; BMO_BATCH_SIMT=0 selects the
-    // tensor-core GEMM with fp32 block scaling
-    const char *simt = std::getenv("BMO_BATCH_SIMT");
-    b->simt = !simt || std::atoi(simt) != 0;
-    b->xq = static_cast<int8_t *>(dalloc(static_cast<size_t>(nbx) * S * 32));
-    b->xds = static_cast<float *>(dalloc(sizeof(float) * 2 * static_cast<size_t>(nbx) * S));
+    // BMO_BATCH_GEMM: "tc" (default) tensor cores with the batch-1 rounding,
+    // "simt" the CUDA-core form of the same arithmetic, "tc_fast" tensor cores
+    // with full-block terms summed in fp32
+    const char *mode = std::getenv("BMO_BATCH_GEMM");
+    const std::string m = mode ? mode : "tc";
+    if (m == "simt") b->gemm = 0;
+    else if (m == "tc_fast") b->gemm = 2;
+    else if (m == "tc") b->gemm = 1;
+    else throw std::runtime_error("BMO_BATCH_GEMM must be tc, tc_fast or simt");
+    b->xq = static_cast<int8_t *>(dalloc(static_cast<size_t>(nbx) * S * 64));
+    b->xds = static_cast<float *>(dalloc(sizeof(float) * 3 * static_cast<size_t>(nbx) * S));
     b->tok = static_cast<int *>(dalloc(sizeof(int) * S));
 
     b->dsess_elems = static_cast<long long>(kDepLayers) * dep_heads * std::max(dep_n_ctx, 1) * dep_hd;
@@ -227,7 +232,7 @@ void Engine::batch_stage(cudaStream_t s, int n, const float *x, int cols, const 
 
 void Engine::batch_gemm(cudaStream_t s, const BatchGemmArgs &a, int epi) {
     BatchState &b = *batch_;
-    if (b.simt) {
+    if (b.gemm == 0) {
         ck(launch_batch_gemm(a, epi, batch_gemm_grid(a.W, sm_count), s), "launch batch gemm");
         return;
     }
@@ -235,7 +240,7 @@ void Engine::batch_gemm(cudaStream_t s, const BatchGemmArgs &a, int epi) {
     m.ws = b.ws;
     m.cnt = b.cnt;
     m.max_contrib = batch_mma_max_contrib(a.W, sm_count);
-    ck(launch_batch_mma(m, epi, sm_count, s), "launch batch mma");
+    ck(launch_batch_mma(m, epi, sm_count, b.gemm == 1, s), "launch batch mma");
 }
 
 void Engine::enqueue_batch_temporal(cudaStream_t s, int n) {

@@ -140,8 +140,8 @@ BatchScratch batch_scratch_layout(const QMatDesc &m, int n_sess, int sms) {
     BatchScratch b{};
     const size_t P = static_cast<size_t>(batch_pad(n_sess));
     b.xq = 0;
-    b.xds = align256(static_cast<size_t>(m.nbx) * P * 32);
-    b.ws = b.xds + align256(static_cast<size_t>(m.nbx) * P * 2 * sizeof(float));
+    b.xds = align256(static_cast<size_t>(m.nbx) * P * 64);
+    b.ws = b.xds + align256(static_cast<size_t>(m.nbx) * P * 3 * sizeof(float));
     b.cnt = b.ws + align256(batch_mma_ws_floats(m, sms) * sizeof(float));
     b.status = b.cnt + align256(static_cast<size_t>(m.n_tiles) * sizeof(int));
     b.total = b.status + 256;
@@ -199,7 +199,8 @@ int bmo_k_batch_gemm_q4_0(const void *tiled_dev, int rows, int cols, int perm, i
     a.cnt = reinterpret_cast<int *>(sc + L.cnt);
     a.max_contrib = batch_mma_max_contrib(m, sms);
     const int epi = perm == kPermSwiGLU ? kEpiSwiGLU : (resid_dev ? kEpiResid : kEpiStore);
-    e = tensor_cores ? launch_batch_mma(a, epi, sms, s) : launch_batch_gemm(a, epi, batch_gemm_grid(m, sms), s);
+    e = tensor_cores ? launch_batch_mma(a, epi, sms, tensor_cores == 1, s)
+                     : launch_batch_gemm(a, epi, batch_gemm_grid(m, sms), s);
     return static_cast<int>(e);
 }
 

@@ -9,15 +9,16 @@
 //    529-558), written in the block-major layout of layout.h; for the
 //    depformer input it also resolves the session's token from the previous
 //    head's per-tile argmax pairs;
-//  * batch_gemm_kernel: the skinny GEMM Y[S][rows] = X[S][cols] . W^T with the
-//    reference's Q4_0 x Q8_1 arithmetic per (session, row): the same
+//  * batch_gemm_kernel: the CUDA-core form of the skinny GEMM
+//    Y[S][rows] = X[S][cols] . W^T (the tensor-core form is batch_mma.cu)
+//    with the reference's Q4_0 x Q8_1 arithmetic per (session, row): the same
 //    half-block fp32 terms as the batch-1 GEMV (gemv_dev.cuh), summed in
-//    double and rounded once.  A CTA owns whole row tiles; its 8 warps form 4
+//    double and rounded once.  A CTA owns whole row tiles; its 4 warps form 2
 //    teams of 2, a team working on one row tile at a time, warp g of a team
 //    serving sessions [32g, 32g + 32) with one lane per session.  Per 8-block
 //    chunk a team's 2-slot ring receives, through the TMA bulk-copy engine,
-//    the weight chunk (4.6 KB) and the S sessions' Q8_1 blocks for it
-//    (S x 320 B, L2-resident).  Weight rows are shared-memory broadcasts; each
+//    the weight chunk (4.6 KB) and the sessions' Q8_1 codes and scales for it
+//    (P x 608 B, L2-resident).  Weight rows are shared-memory broadcasts; each
 //    lane keeps its session's 32 row sums in registers, so the fused epilogue
 //    (RoPE + KV append into the session's ring, SwiGLU, residual, logits +
 //    argmax, embedding add) runs per lane with no cross-warp reduction.
@@ -29,12 +30,12 @@
 
 namespace bmo {
 
-constexpr int kBtWarps = 8;
+constexpr int kBtTeams = 2;
+constexpr int kBtWarps = 2 * kBtTeams;
 constexpr int kBtThreads = kBtWarps * 32;
-constexpr int kBtTeams = 4;
 constexpr int kBtSlots = 2;
-constexpr int kBtXqBytes = kBatchMax * 8 * 32;   // Q8_1 quants of one chunk, all sessions
-constexpr int kBtXdsBytes = kBatchMax * 8 * 8;   // their scale pairs
+constexpr int kBtXqBytes = kBatchMax * 8 * 64;   // Q8_1 codes of one chunk, all sessions (half-split rows)
+constexpr int kBtXdsBytes = kBatchMax * 8 * 12;  // their scales
 constexpr int kBtSlotBytes = kChunkBytes + kBtXqBytes + kBtXdsBytes;
 static_assert(kBtSlotBytes % 16 == 0, "bulk-copy destinations stay 16-byte aligned");
 static_assert(kBatchMax <= 2 * 32, "two warps of a team cover the sessions");
@@ -92,15 +93,22 @@ __global__ void __launch_bounds__(256) batch_stage_kernel(const __grid_constant_
         scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(static_cast<double>(mean_eps))));
     }
     for (int b = tid; b < a.nbx; b += 256) {
-        // canonical K-major layout: the two 16-byte halves of a session's block are 128 bytes apart
-        int8_t *qb = a.xq + static_cast<long long>(b) * P * 32 + (s >> 3) * 256 + (s & 7) * 16;
-        int4 *q0 = reinterpret_cast<int4 *>(qb), *q1 = reinterpret_cast<int4 *>(qb + 128);
-        float *dd = a.xds + static_cast<long long>(b) * P * 2 + (s >> 1) * 4 + (s & 1);
+        // rows 2s (codes 0-7, 16-23) and 2s + 1 (codes 8-15, 24-31) of the block's B operand,
+        // 16-byte K slices k = 0 (elements 0-15) and k = 1 (elements 16-31)
+        int8_t *blk = a.xq + static_cast<long long>(b) * P * 64;
+        const int r0 = 2 * s, r1 = 2 * s + 1;
+        int4 *lo0 = reinterpret_cast<int4 *>(blk + (r0 >> 3) * 256 + (r0 & 7) * 16);
+        int4 *lo1 = reinterpret_cast<int4 *>(blk + (r0 >> 3) * 256 + 128 + (r0 & 7) * 16);
+        int4 *hi0 = reinterpret_cast<int4 *>(blk + (r1 >> 3) * 256 + (r1 & 7) * 16);
+        int4 *hi1 = reinterpret_cast<int4 *>(blk + (r1 >> 3) * 256 + 128 + (r1 & 7) * 16);
+        float *sc = a.xds + static_cast<long long>(b) * P * 3;
+        float *d4p = sc + (s >> 1) * 4 + (s & 1);      // d8 at [0], -M d8 at [2]
+        float *s4p = sc + 2 * P + (s >> 1) * 2 + (s & 1);
         if (b >= nb) {
-            *q0 = make_int4(0, 0, 0, 0);
-            *q1 = make_int4(0, 0, 0, 0);
-            dd[0] = 0.0f;
-            dd[2] = 0.0f;
+            *lo0 = *lo1 = *hi0 = *hi1 = make_int4(0, 0, 0, 0);
+            d4p[0] = 0.0f;
+            d4p[2] = 0.0f;
+            *s4p = 0.0f;
             continue;
         }
         float v[32];
@@ -118,10 +126,14 @@ __global__ void __launch_bounds__(256) batch_stage_kernel(const __grid_constant_
         int8_t q[32];
         const __half2 ds = quant_block_q8_1(v, q);
         const int *qi = reinterpret_cast<const int *>(q);
-        *q0 = make_int4(qi[0], qi[1], qi[2], qi[3]);
-        *q1 = make_int4(qi[4], qi[5], qi[6], qi[7]);
-        dd[0] = __low2float(ds);
-        dd[2] = -8.0f * __high2float(ds);
+        *lo0 = make_int4(qi[0], qi[1], 0, 0);
+        *lo1 = make_int4(qi[4], qi[5], 0, 0);
+        *hi0 = make_int4(0, 0, qi[2], qi[3]);
+        *hi1 = make_int4(0, 0, qi[6], qi[7]);
+        const float d8 = __low2float(ds);
+        d4p[0] = d8;
+        d4p[2] = -12582912.0f * d8;  // exact: 1.5 * 2^23 times an 11-bit significand
+        *s4p = -4.0f * __high2float(ds);
     }
 }
 
@@ -256,7 +268,7 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
     const int t1 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * (c + 1) / G);
     const int n_tiles_team = t1 - t0 > team ? (t1 - t0 - team + kBtTeams - 1) / kBtTeams : 0;
     const int units = n_tiles_team * cpt;
-    const uint32_t xqb = static_cast<uint32_t>(P) * 256u, xdsb = static_cast<uint32_t>(P) * 64u;
+    const uint32_t xqb = static_cast<uint32_t>(P) * 512u, xdsb = static_cast<uint32_t>(P) * 96u;
 
     if (tid < kBtTeams * kBtSlots) {
         mbar_init(&S.full[tid / kBtSlots][tid % kBtSlots], 1);
@@ -276,8 +288,8 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
         uint64_t *bar = &S.full[team][sl];
         mbar_arrive_expect_tx(bar, kChunkBytes + xqb + xdsb);
         bulk_load(dst, a.W.tiles + (static_cast<size_t>(t) * cpt + kc) * kChunkBytes, kChunkBytes, bar, pol_w);
-        bulk_load(dst + kChunkBytes, a.xq + static_cast<size_t>(kc) * 8 * P * 32, xqb, bar, pol_x);
-        bulk_load(dst + kChunkBytes + kBtXqBytes, a.xds + static_cast<size_t>(kc) * 8 * P * 2, xdsb, bar, pol_x);
+        bulk_load(dst + kChunkBytes, a.xq + static_cast<size_t>(kc) * 8 * P * 64, xqb, bar, pol_x);
+        bulk_load(dst + kChunkBytes + kBtXqBytes, a.xds + static_cast<size_t>(kc) * 8 * P * 3, xdsb, bar, pol_x);
     };
     int issued = 0;  // meaningful in the issuing thread only
     if (issuer)
@@ -306,11 +318,17 @@ __global__ void __launch_bounds__(kBtThreads, 1) batch_gemm_kernel(const __grid_
             int4 xa = make_int4(0, 0, 0, 0), xb = make_int4(0, 0, 0, 0);
             float2 ds = make_float2(0.0f, 0.0f);
             if (act) {
-                const int8_t *xp = xq + blk * P * 32 + (sess >> 3) * 256 + (sess & 7) * 16;
-                xa = *reinterpret_cast<const int4 *>(xp);
-                xb = *reinterpret_cast<const int4 *>(xp + 128);
-                const float *dp = xds + blk * P * 2 + (sess >> 1) * 4 + (sess & 1);
-                ds = make_float2(dp[0], -0.5f * dp[2]);  // (d8, 4 s8)
+                // codes 0-15 and 16-31 from the two half-block rows
+                const int8_t *xp = xq + blk * P * 64;
+                const int r0 = 2 * sess, r1 = 2 * sess + 1;
+                const int2 l0 = *reinterpret_cast<const int2 *>(xp + (r0 >> 3) * 256 + (r0 & 7) * 16);
+                const int2 h0 = *reinterpret_cast<const int2 *>(xp + (r1 >> 3) * 256 + (r1 & 7) * 16 + 8);
+                const int2 l1 = *reinterpret_cast<const int2 *>(xp + (r0 >> 3) * 256 + 128 + (r0 & 7) * 16);
+                const int2 h1 = *reinterpret_cast<const int2 *>(xp + (r1 >> 3) * 256 + 128 + (r1 & 7) * 16 + 8);
+                xa = make_int4(l0.x, l0.y, h0.x, h0.y);
+                xb = make_int4(l1.x, l1.y, h1.x, h1.y);
+                const float *sp = xds + blk * P * 3;
+                ds = make_float2(sp[(sess >> 1) * 4 + (sess & 1)], -sp[2 * P + (sess >> 1) * 2 + (sess & 1)]);  // (d8, 4 s8)
             }
             const uint8_t *wb = w + blk * 512;
             const __half *db = reinterpret_cast<const __half *>(w + kChunkQsBytes + blk * 64);

@@ -1,32 +1,40 @@
 // batch_mma.cu -- the batched skinny GEMM Y[S][rows] = X[S][cols] . W^T on
 // the 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
 //
-// Arithmetic (Q4_0 x Q8_1 per block b of 32 columns, row r, session s):
-//     y[s][r] = sum_b d4[r][b] * (sumi[r][s][b] * d8[s][b] - 8 * s8[s][b])
-// with sumi the integer dot of the row's 32 unsigned nibbles and the
-// session's 32 int8 codes -- the reference's vec_dot_q4_0_q8_1 term
-// (bmo_cuda_kernels.cu:560-683) taken over the whole block.  The tensor core
-// computes every sumi exactly (kind::i8, unsigned nibbles x signed codes,
-// int32 accumulators): one M=128 x N=P x K=32 MMA per block, each into its
-// own TMEM slot.  The CUDA cores then apply the two per-block scales in fp32
-// (sumi -> float exactly through the 2^23 + 2^22 bias, one fma with d8 and
-// -8 s8, one fma with d4 into the running sum), two sessions per packed
-// f32x2 instruction.  Unlike the batch-1 GEMV the block terms are rounded
-// once each and summed in fp32, so results agree with the reference to fp32
-// rounding (well inside the 1e-3 relative bar), not bit for bit.
+// Arithmetic per block b of 32 columns, row r, session s: the reference's
+// Q4_0 x Q8_1 half-block terms (vec_dot_q4_0_q8_1, bmo_cuda_kernels.cu:
+// 560-683)
+//     t = d4[r][b] * (sumi_h[r][s][b] * d8[s][b] - 4 s8[s][b]),  h = low, high half
+// with sumi_h the integer dot of 16 unsigned nibbles and 16 int8 codes (the
+// reference's halves: elements 0-7 + 16-23 and 8-15 + 24-31).  The tensor
+// core computes every sumi_h exactly: the activation rows are split into one
+// row per half (layout.h), so one kind::i8 MMA of
+// M = 128 rows x N = 2P rows x K = 32 per block (unsigned nibbles x signed
+// codes, int32 accumulators) yields both half sums of every session, each
+// block into its own TMEM slot.  The CUDA cores then form each term with the
+// reference's fp32 roundings, two sessions per packed f32x2 instruction
+// (sumi -> float exactly through the 2^23 + 2^22 bias, one fma against
+// -M d8 = fl(sumi d8), one add of -4 s8, one multiply by d4), and
+//   EXACT: sum the terms error-free in a float pair (Knuth's two-sum: the sum
+//          carried to ~48 bits and rounded once at the end), which agrees
+//          with the double-sum semantics of the batch-1 GEMV and the oracle
+//          except at rare rounding ties;
+//   !EXACT: one full-block term d4 (sumi d8 - 8 s8) per block, summed in
+//          fp32 (fp32-accurate, not reproducible bit for bit).
 //
-// CTA (one per SM, 14 warps):
-//   warp 12      bulk-copy producer: per 8-block chunk the four 32-row tiles'
-//                Q4_0 chunks of a 128-row block (4 x 4608 B, HBM), the
-//                sessions' Q8_1 codes (P x 256 B) and scales (P x 64 B, L2)
-//   warps 8-11   unpack nibbles into the MMA's K-major int8 layout (A)
-//   warp 13      TMEM owner and MMA issuer (one thread)
-//   warps 0-7    read the int32 block sums from TMEM (warp w: TMEM lanes
-//                32(w%4).., sessions 32(w/4)..), scale and accumulate, then
-//                run the fused epilogue of layout.h's Epilogue per (row, session)
+// CTA (one per SM, 10 warps):
+//   warp 9       TMEM owner; lane 0 the bulk-copy producer (per 8-block chunk
+//                the four 32-row tiles' Q4_0 chunks of a 128-row block, 4 x
+//                4608 B from HBM, the sessions' split Q8_1 codes, 512 P B, and
+//                scales, 96 P B, from L2), lane 1 the MMA issuer
+//   warp 8       unpacks nibbles into the MMA's K-major int8 layout (A)
+//   warps 0-7    read the int32 half-block sums from TMEM (warp w: TMEM lanes
+//                32(w%4).., sessions 32(w/4)..), two register buffers so the
+//                next read overlaps this one's arithmetic, form and sum the
+//                terms, then run the fused epilogue of layout.h's Epilogue
 // Work is split stream-K: the (128-row block, chunk) units are cut evenly
 // over the CTAs; a row block shared by several CTAs is combined by the last
-// one to finish, summing the fp32 partials in contributor order (so the
+// one to finish, adding the partial float pairs in contributor order (the
 // result does not depend on timing).  Every wait is bounded and any timeout
 // makes all roles stop, drain the copies and MMAs in flight, free TMEM and
 // raise the status word.
@@ -39,20 +47,22 @@ namespace bmo {
 
 constexpr int kMmaTiles = 4;                     // row tiles per 128-row block
 constexpr int kMmaRows = kMmaTiles * kTileRows;  // MMA M
-constexpr int kMmaStages = 4;
+constexpr int kMmaStages = 2;
 constexpr int kMmaABufs = 2;
-constexpr int kMmaSlots = kChunkBlocks;          // one TMEM slot per block of a chunk
-constexpr int kMmaSlotCols = 64;                 // >= P
+constexpr int kMmaSlots = 4;                     // TMEM slots, one block each
+constexpr int kMmaSlotCols = 128;                // >= N = 2P
 constexpr int kMmaTmemCols = kMmaSlots * kMmaSlotCols;  // 512: all of TMEM
 constexpr int kRawW = kMmaTiles * kChunkBytes;   // 18432
-constexpr int kRawB = kBatchMax * 8 * 32;        // 16384
-constexpr int kRawS = kBatchMax * 8 * 8;         // 4096
+constexpr int kRawB = kBatchMax * 8 * 64;        // 32768: split codes of one chunk
+constexpr int kRawS = kBatchMax * 8 * 12;        // 6144: their scales
 constexpr int kRawBytes = kRawW + kRawB + kRawS;
 constexpr int kABlockBytes = kMmaRows * 32;      // one block of A: 128 rows x 32 int8
 constexpr int kABytes = kChunkBlocks * kABlockBytes;
-constexpr int kEpiWarps = 8, kUnpackWarps = 4, kProdWarp = 12, kMmaWarp = 13;
-constexpr int kMmaThreads = 14 * 32;
+constexpr int kEpiWarps = 8, kUnpackWarps = 1;
+constexpr int kCtlWarp = 9;  // lane 0: bulk-copy producer, lane 1: MMA issuer; the warp owns TMEM
+constexpr int kMmaThreads = 10 * 32;
 static_assert(kRawBytes % 1024 == 0 && kABytes % 1024 == 0, "stage buffers stay 1 KB aligned");
+static_assert(2 * kBatchMax <= kMmaSlotCols, "a slot holds both halves of every session");
 
 struct MmaSmem {
     uint8_t raw[kMmaStages][kRawBytes];
@@ -107,6 +117,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "memory");
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+// 16 consecutive TMEM columns of this warp's 32 lanes (no wait).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, K-major without swizzle: 8-row x 16-byte
 // core matrices stored as 128 contiguous bytes, the K-neighbour core matrix
@@ -213,6 +235,7 @@ __device__ __forceinline__ void mma_row_epilogue(const BatchGemmArgs &a, int t, 
     }
 }
 
+// The 32 sessions [32h, 32h + 32) of tile t, one row per lane.
 template <int EPI>
 __device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t, int lane, int h, const float2 (&v)[16]) {
     if (t >= a.W.n_tiles) return;
@@ -227,7 +250,52 @@ __device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int EPI>
+// Knuth's two-sum of packed pairs: (s, c) += t with s + c carried error-free
+// to ~48 bits (fma(x, -1, y) is the exactly rounded y - x).
+__device__ __forceinline__ void two_sum_acc(float2 &s, float2 &c, float2 t) {
+    const float2 m1 = make_float2(-1.0f, -1.0f);
+    const float2 n = __fadd2_rn(s, t);
+    const float2 bb = __ffma2_rn(s, m1, n);   // n - s
+    const float2 a1 = __ffma2_rn(bb, m1, n);  // n - bb
+    const float2 a2 = __ffma2_rn(a1, m1, s);  // s - (n - bb)
+    const float2 b2 = __ffma2_rn(bb, m1, t);  // t - bb
+    c = __fadd2_rn(c, __fadd2_rn(a2, b2));
+    s = n;
+}
+
+// Terms of one 8-session register buffer r (r[2i] low-half sum, r[2i + 1]
+// high-half sum of session i) into the accumulators of pairs [4k, 4k + 4).
+template <bool EXACT>
+__device__ __forceinline__ void mma_terms(const uint32_t (&r)[16], const float4 *sc4, const float2 *sc2, float d4,
+                                          float2 (&S)[16], float2 (&C)[16], int k) {
+    const float2 d44 = make_float2(d4, d4);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const float4 p = sc4[4 * k + jj];   // d8, d8', -M d8, -M d8'
+        const float2 m4 = sc2[4 * k + jj];  // -4 s8, -4 s8'
+        const float2 d8 = make_float2(p.x, p.y), nm = make_float2(p.z, p.w);
+        const int J = 4 * k + jj;
+        if constexpr (EXACT) {
+            // bits of 2^23 + 2^22 + sumi; the fma against -M d8 leaves fl(sumi d8)
+            const float2 flo = make_float2(__int_as_float(static_cast<int>(r[4 * jj]) + 0x4B400000),
+                                           __int_as_float(static_cast<int>(r[4 * jj + 2]) + 0x4B400000));
+            const float2 fhi = make_float2(__int_as_float(static_cast<int>(r[4 * jj + 1]) + 0x4B400000),
+                                           __int_as_float(static_cast<int>(r[4 * jj + 3]) + 0x4B400000));
+            float2 t = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(flo, d8, nm), m4));
+            two_sum_acc(S[J], C[J], t);
+            t = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(fhi, d8, nm), m4));
+            two_sum_acc(S[J], C[J], t);
+        } else {
+            const float2 f = make_float2(
+                __int_as_float(static_cast<int>(r[4 * jj] + r[4 * jj + 1]) + 0x4B400000),
+                __int_as_float(static_cast<int>(r[4 * jj + 2] + r[4 * jj + 3]) + 0x4B400000));
+            const float2 u = __ffma2_rn(m4, make_float2(2.0f, 2.0f), __ffma2_rn(f, d8, nm));  // sumi d8 - 8 s8
+            S[J] = __ffma2_rn(d44, u, S[J]);
+        }
+    }
+}
+
+template <int EPI, bool EXACT>
 __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_constant__ BatchGemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     MmaSmem &S = *reinterpret_cast<MmaSmem *>(smem_raw);
@@ -238,13 +306,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
     const long long U = static_cast<long long>(n_super) * cpt;
     const long long u0 = unit_lo(U, G, c), u1 = unit_lo(U, G, c + 1);
     const int n_units = static_cast<int>(u1 - u0);
-    const int halves = (ns + 31) / 32;  // epilogue warp groups with sessions
+    const int groups = (ns + 31) / 32;  // epilogue warpgroups (32 sessions each) with sessions
     volatile int *abort = &S.abort;
 
     if (tid == 0) {
         for (int i = 0; i < kMmaStages; ++i) {
             mbar_init(&S.raw_full[i], 1);
-            mbar_init(&S.raw_empty[i], kUnpackWarps + 4 * halves + 1);
+            mbar_init(&S.raw_empty[i], kUnpackWarps + 4 * groups + 1);
         }
         for (int i = 0; i < kMmaABufs; ++i) {
             mbar_init(&S.a_full[i], kUnpackWarps);
@@ -252,14 +320,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
         }
         for (int i = 0; i < kMmaSlots; ++i) {
             mbar_init(&S.tm_full[i], 1);
-            mbar_init(&S.tm_empty[i], 4 * halves);
+            mbar_init(&S.tm_empty[i], 4 * groups);
         }
         mbar_init(&S.mma_done, 1);
         S.abort = 0;
         S.last = 0;
         fence_barrier_init();
     }
-    if (warp == kMmaWarp) {
+    if (warp == kCtlWarp) {
         tmem_alloc(&S.tmem_base, kMmaTmemCols);
         tmem_relinquish();
     }
@@ -268,8 +336,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
 
-    if (warp == kProdWarp) {
-        // ---------------- bulk-copy producer ----------------
+    if (warp == kCtlWarp) {
+        // ---------------- bulk-copy producer (lane 0) ----------------
         int issued = 0;
         if (lane == 0) {
             const uint64_t pol_w = l2_evict_first_policy(), pol_x = l2_evict_last_policy();
@@ -280,71 +348,37 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 if (g >= kMmaStages && !wait_ab(&S.raw_empty[sg], ((g / kMmaStages) + 1) & 1, abort)) break;
                 uint8_t *dst = S.raw[sg];
                 const int n_t = min(kMmaTiles, a.W.n_tiles - st * kMmaTiles);
-                mbar_arrive_expect_tx(&S.raw_full[sg],
-                                      static_cast<uint32_t>(n_t * kChunkBytes + P * 256 + P * 64));
+                mbar_arrive_expect_tx(&S.raw_full[sg], static_cast<uint32_t>(n_t * kChunkBytes + P * 512 + P * 96));
                 for (int q = 0; q < n_t; ++q)
                     bulk_load(dst + q * kChunkBytes,
                               a.W.tiles + (static_cast<size_t>(st * kMmaTiles + q) * cpt + kc) * kChunkBytes,
                               kChunkBytes, &S.raw_full[sg], pol_w);
-                bulk_load(dst + kRawW, a.xq + static_cast<size_t>(kc) * 8 * P * 32, P * 256, &S.raw_full[sg], pol_x);
-                bulk_load(dst + kRawW + kRawB, a.xds + static_cast<size_t>(kc) * 8 * P * 2, P * 64, &S.raw_full[sg],
+                bulk_load(dst + kRawW, a.xq + static_cast<size_t>(kc) * 8 * P * 64, P * 512, &S.raw_full[sg], pol_x);
+                bulk_load(dst + kRawW + kRawB, a.xds + static_cast<size_t>(kc) * 8 * P * 3, P * 96, &S.raw_full[sg],
                           pol_x);
                 ++issued;
             }
             // copies in flight land before the CTA can exit (bounded)
             for (int g = max(0, issued - kMmaStages); g < issued; ++g)
                 mbar_wait(&S.raw_full[g % kMmaStages], (g / kMmaStages) & 1);
-        }
-        __syncwarp();
-    } else if (warp >= kEpiWarps && warp < kEpiWarps + kUnpackWarps) {
-        // ---------------- unpack: Q4_0 nibbles -> K-major unsigned int8 ----------------
-        const int m = tid - kEpiWarps * 32;  // row of the 128-row block
-        const int q = m >> 5, rl = m & 31;
-        for (int g = 0; g < n_units; ++g) {
-            const long long u = u0 + g;
-            const int st = static_cast<int>(u / cpt);
-            const int sg = g % kMmaStages, ab = g % kMmaABufs;
-            bool ok = wait_ab(&S.raw_full[sg], (g / kMmaStages) & 1, abort);
-            if (ok && g >= kMmaABufs) ok = wait_ab(&S.a_empty[ab], ((g / kMmaABufs) + 1) & 1, abort);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            const bool present = st * kMmaTiles + q < a.W.n_tiles;
-            const uint8_t *src = S.raw[sg] + q * kChunkBytes + rl * 16;
-            uint8_t *dst = S.a[ab] + (m >> 3) * 256 + (m & 7) * 16;
-#pragma unroll
-            for (int b = 0; b < kChunkBlocks; ++b) {
-                uint4 w = present ? *reinterpret_cast<const uint4 *>(src + b * 512) : make_uint4(0, 0, 0, 0);
-                // byte j holds element j (low nibble) and element j + 16 (high nibble)
-                const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-                const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                            (w.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(dst + b * kABlockBytes) = lo;
-                *reinterpret_cast<uint4 *>(dst + b * kABlockBytes + 128) = hi;
-            }
-            fence_proxy_async();  // generic-proxy writes -> the tensor core's reads
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&S.a_full[ab]);
-                mbar_arrive(&S.raw_empty[sg]);
-            }
-        }
-    } else if (warp == kMmaWarp) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = idesc_i8(P);
+        } else if (lane == 1) {
+            // ---------------- MMA issuer (lane 1) ----------------
+            const uint32_t idesc = idesc_i8(2 * P);
             for (int g = 0; g < n_units; ++g) {
                 const int sg = g % kMmaStages, ab = g % kMmaABufs;
                 if (!wait_ab(&S.a_full[ab], (g / kMmaABufs) & 1, abort)) break;
                 tc_fence_after();
                 bool ok = true;
-                for (int b = 0; b < kMmaSlots; ++b) {
-                    if (g >= 1 && !wait_ab(&S.tm_empty[b], (g + 1) & 1, abort)) {
+                for (int b = 0; b < kChunkBlocks; ++b) {
+                    const int gb = g * kChunkBlocks + b, slot = gb % kMmaSlots, use = gb / kMmaSlots;
+                    if (use >= 1 && !wait_ab(&S.tm_empty[slot], (use + 1) & 1, abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    mma_i8(tmem + b * kMmaSlotCols, kmajor_desc(S.a[ab] + b * kABlockBytes),
-                           kmajor_desc(S.raw[sg] + kRawW + b * P * 32), idesc);
-                    mma_commit(&S.tm_full[b]);
+                    mma_i8(tmem + slot * kMmaSlotCols, kmajor_desc(S.a[ab] + b * kABlockBytes),
+                           kmajor_desc(S.raw[sg] + kRawW + b * P * 64), idesc);
+                    mma_commit(&S.tm_full[slot]);
                 }
                 if (!ok) break;
                 mma_commit(&S.a_empty[ab]);
@@ -355,44 +389,85 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
             mbar_wait(&S.mma_done, 0);
         }
         __syncwarp();
-    } else {
+    } else if (warp >= kEpiWarps && warp < kEpiWarps + kUnpackWarps) {
+        // ---------------- unpack: Q4_0 nibbles -> K-major unsigned int8 ----------------
+        const int ut = tid - kEpiWarps * 32;  // rows ut, ut + 32, ut + 64, ut + 96 of the 128-row block
+        for (int g = 0; g < n_units; ++g) {
+            const long long u = u0 + g;
+            const int st = static_cast<int>(u / cpt);
+            const int sg = g % kMmaStages, ab = g % kMmaABufs;
+            bool ok = wait_ab(&S.raw_full[sg], (g / kMmaStages) & 1, abort);
+            if (ok && g >= kMmaABufs) ok = wait_ab(&S.a_empty[ab], ((g / kMmaABufs) + 1) & 1, abort);
+            if (!__all_sync(0xffffffffu, ok)) break;
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) {
+                const int m = ut + 32 * rr;
+                const int q = m >> 5;
+                const bool present = st * kMmaTiles + q < a.W.n_tiles;
+                const uint8_t *src = S.raw[sg] + q * kChunkBytes + (m & 31) * 16;
+                uint8_t *dst = S.a[ab] + (m >> 3) * 256 + (m & 7) * 16;
+#pragma unroll
+                for (int b = 0; b < kChunkBlocks; ++b) {
+                    const uint4 w = present ? *reinterpret_cast<const uint4 *>(src + b * 512) : make_uint4(0, 0, 0, 0);
+                    // byte j holds element j (low nibble) and element j + 16 (high nibble)
+                    *reinterpret_cast<uint4 *>(dst + b * kABlockBytes) =
+                        make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+                    *reinterpret_cast<uint4 *>(dst + b * kABlockBytes + 128) =
+                        make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                   (w.w >> 4) & 0x0F0F0F0Fu);
+                }
+            }
+            fence_proxy_async();  // generic-proxy writes -> the tensor core's reads
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&S.a_full[ab]);
+                mbar_arrive(&S.raw_empty[sg]);
+            }
+        }
+    } else if (warp < kEpiWarps) {
         // ---------------- epilogue warps ----------------
         const int q = warp & 3, h = warp >> 2;
-        const bool active = h < halves;
-        float2 acc[16];
+        const bool active = h < groups;
+        float2 Sacc[16], Cacc[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
-        const float2 bias2 = make_float2(-12582912.0f, -12582912.0f);
+        for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + 64 * h;
+        uint32_t rA[16], rB[16];
+        bool ok = true;
         for (int g = 0; active && g < n_units; ++g) {
             const long long u = u0 + g;
             const int st = static_cast<int>(u / cpt), kc = static_cast<int>(u % cpt);
             const int sg = g % kMmaStages;
-            bool ok = wait_ab(&S.raw_full[sg], (g / kMmaStages) & 1, abort);
+            ok = wait_ab(&S.raw_full[sg], (g / kMmaStages) & 1, abort);
             if (!__all_sync(0xffffffffu, ok)) break;
             const uint8_t *raw = S.raw[sg];
             const __half *d4p = reinterpret_cast<const __half *>(raw + q * kChunkBytes + kChunkQsBytes) + lane;
-            for (int b = 0; b < kMmaSlots; ++b) {
-                ok = wait_ab(&S.tm_full[b], g & 1, abort);
+            for (int b = 0; b < kChunkBlocks; ++b) {
+                const int gb = g * kChunkBlocks + b, slot = gb % kMmaSlots, use = gb / kMmaSlots;
+                ok = wait_ab(&S.tm_full[slot], use & 1, abort);
                 if (!__all_sync(0xffffffffu, ok)) break;
                 tc_fence_after();
-                uint32_t r[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + b * kMmaSlotCols + 32 * h, r);
+                // four reads of 8 sessions (16 columns); each read overlaps the previous one's arithmetic
+                const uint32_t ta = lane_base + slot * kMmaSlotCols;
+                tmem_ld16_nowait(ta, rA);
+                tmem_wait_ld();
+                const float d4 = __half2float(d4p[b * 32]);
+                const uint8_t *scb = raw + kRawW + kRawB + b * P * 12;
+                const float4 *sc4 = reinterpret_cast<const float4 *>(scb) + 16 * h;
+                const float2 *sc2 = reinterpret_cast<const float2 *>(scb + P * 8) + 16 * h;
+                tmem_ld16_nowait(ta + 16, rB);
+                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Cacc, 0);
+                tmem_wait_ld();
+                tmem_ld16_nowait(ta + 32, rA);
+                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Cacc, 1);
+                tmem_wait_ld();
+                tmem_ld16_nowait(ta + 48, rB);
+                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Cacc, 2);
+                tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&S.tm_empty[b]);
-                const float d4 = __half2float(d4p[b * 32]);
-                const float2 d44 = make_float2(d4, d4);
-                const float4 *sc = reinterpret_cast<const float4 *>(raw + kRawW + kRawB + b * P * 8) + 16 * h;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float4 p = sc[j];  // (d8, d8', -8 s8, -8 s8') of sessions 32h+2j, +1
-                    // int32 -> float exactly: bits of 2^23 + 2^22 + sumi, minus the bias
-                    float2 f = make_float2(__int_as_float(static_cast<int>(r[2 * j]) + 0x4B400000),
-                                           __int_as_float(static_cast<int>(r[2 * j + 1]) + 0x4B400000));
-                    f = __fadd2_rn(f, bias2);
-                    const float2 t = __ffma2_rn(f, make_float2(p.x, p.y), make_float2(p.z, p.w));
-                    acc[j] = __ffma2_rn(d44, t, acc[j]);
-                }
+                if (lane == 0) mbar_arrive(&S.tm_empty[slot]);  // every read of the slot has completed
+                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Cacc, 3);
             }
             if (!ok) break;
             __syncwarp();
@@ -403,57 +478,65 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
             const int t = st * kMmaTiles + q;
             const long long first = static_cast<long long>(st) * cpt, lastu = first + cpt - 1;
             if (first >= u0 && lastu < u1) {
-                mma_block_epilogue<EPI>(a, t, lane, h, acc);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) Sacc[j] = __fadd2_rn(Sacc[j], Cacc[j]);
+                mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
             } else {
                 const int cf = cta_of(first, U, G), cl = cta_of(lastu, U, G);
                 const int n_c = cl - cf + 1;
-                const size_t slab = static_cast<size_t>(P) * kMmaRows;
-                float *part = a.ws + (static_cast<size_t>(st) * a.max_contrib + (c - cf)) * slab;
-                // the slab holds P sessions: rows of padding sessions beyond P are not stored
+                const size_t plane = static_cast<size_t>(P) * kMmaRows;  // one float per (session, row)
+                float *part = a.ws + (static_cast<size_t>(st) * a.max_contrib + (c - cf)) * 2 * plane;
+                // the partial holds P sessions: padding sessions beyond P are not stored
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     if (32 * h + 2 * j < P) {
-                        part[(32 * h + 2 * j) * kMmaRows + 32 * q + lane] = acc[j].x;
-                        part[(32 * h + 2 * j + 1) * kMmaRows + 32 * q + lane] = acc[j].y;
+                        const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
+                        part[i0] = Sacc[j].x;
+                        part[i0 + kMmaRows] = Sacc[j].y;
+                        part[plane + i0] = Cacc[j].x;
+                        part[plane + i0 + kMmaRows] = Cacc[j].y;
                     }
                 }
                 __threadfence();
-                named_sync(1, 128 * halves);
+                named_sync(1, 128 * groups);
                 if (tid == 0) {
                     const int old = atomicAdd(&a.cnt[st], 1);
                     S.last = old == n_c - 1;
                     if (S.last) a.cnt[st] = 0;  // every contributor has counted: ready for the next launch
                     __threadfence();
                 }
-                named_sync(1, 128 * halves);
+                named_sync(1, 128 * groups);
                 if (S.last) {
-                    float2 tot[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) tot[j] = make_float2(0.0f, 0.0f);
-                    const float *base = a.ws + static_cast<size_t>(st) * a.max_contrib * slab;
+                    for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
+                    const float *base = a.ws + static_cast<size_t>(st) * a.max_contrib * 2 * plane;
                     for (int k = 0; k < n_c; ++k) {
-                        const float *pk = base + k * slab;
+                        const float *pk = base + k * 2 * plane;
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             if (32 * h + 2 * j < P) {
-                                tot[j].x = __fadd_rn(tot[j].x, __ldcg(pk + (32 * h + 2 * j) * kMmaRows + 32 * q + lane));
-                                tot[j].y = __fadd_rn(tot[j].y, __ldcg(pk + (32 * h + 2 * j + 1) * kMmaRows + 32 * q + lane));
+                                const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
+                                two_sum_acc(Sacc[j], Cacc[j], make_float2(__ldcg(pk + i0), __ldcg(pk + i0 + kMmaRows)));
+                                Cacc[j] = __fadd2_rn(Cacc[j], make_float2(__ldcg(pk + plane + i0),
+                                                                          __ldcg(pk + plane + i0 + kMmaRows)));
                             }
                         }
                     }
-                    mma_block_epilogue<EPI>(a, t, lane, h, tot);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) Sacc[j] = __fadd2_rn(Sacc[j], Cacc[j]);
+                    mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
                 }
-                named_sync(1, 128 * halves);  // S.last is reused by the next block
+                named_sync(1, 128 * groups);  // S.last is reused by the next block
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
         }
         tc_fence_before();
     }
 
     __syncthreads();
     if (tid == 0 && S.abort) raise_error(a.status, kErrTmaTimeout);
-    if (warp == kMmaWarp) {
+    if (warp == kCtlWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kMmaTmemCols);
     }
@@ -488,13 +571,16 @@ int batch_mma_max_contrib(const QMatDesc &m, int sms) {
 
 size_t batch_mma_ws_floats(const QMatDesc &m, int sms) {
     const int n_super = (m.n_tiles + kMmaTiles - 1) / kMmaTiles;
-    return static_cast<size_t>(n_super) * batch_mma_max_contrib(m, sms) * kBatchMax * kMmaRows;
+    return static_cast<size_t>(n_super) * batch_mma_max_contrib(m, sms) * 2 * kBatchMax * kMmaRows;
 }
 
 template <int EPI>
 static cudaError_t configure_mma() {
-    return cudaFuncSetAttribute(batch_mma_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(sizeof(MmaSmem)));
+    const int bytes = static_cast<int>(sizeof(MmaSmem));
+    cudaError_t e = cudaFuncSetAttribute(batch_mma_kernel<EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(batch_mma_kernel<EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return e;
 }
 
 static std::atomic<unsigned long long> g_mma_configured{0};  // bit per device
@@ -516,7 +602,13 @@ static cudaError_t ensure_mma_configured() {
     return configure_batch_mma();
 }
 
-cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epi, int sms, cudaStream_t s) {
+template <int EPI>
+static void launch_mma_t(const BatchGemmArgs &a, int G, bool exact, cudaStream_t s) {
+    if (exact) batch_mma_kernel<EPI, true><<<G, kMmaThreads, sizeof(MmaSmem), s>>>(a);
+    else batch_mma_kernel<EPI, false><<<G, kMmaThreads, sizeof(MmaSmem), s>>>(a);
+}
+
+cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epi, int sms, bool exact, cudaStream_t s) {
     if (a.n_sess < 1 || a.n_sess > kBatchMax || a.W.cpt <= 0 || a.W.n_tiles <= 0 || sms <= 0)
         return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(a.xq) & 15) || (reinterpret_cast<uintptr_t>(a.xds) & 15) ||
@@ -528,14 +620,13 @@ cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epi, int sms, cudaStrea
     if (epi == kEpiQKV && (a.head_dim % 32 || a.q_dim % 32 || a.kv_dim % 32)) return cudaErrorInvalidValue;
     const cudaError_t ce = ensure_mma_configured();
     if (ce != cudaSuccess) return ce;
-    const size_t smem = sizeof(MmaSmem);
     switch (epi) {
-    case kEpiStore: batch_mma_kernel<kEpiStore><<<G, kMmaThreads, smem, s>>>(a); break;
-    case kEpiResid: batch_mma_kernel<kEpiResid><<<G, kMmaThreads, smem, s>>>(a); break;
-    case kEpiSwiGLU: batch_mma_kernel<kEpiSwiGLU><<<G, kMmaThreads, smem, s>>>(a); break;
-    case kEpiQKV: batch_mma_kernel<kEpiQKV><<<G, kMmaThreads, smem, s>>>(a); break;
-    case kEpiLogits: batch_mma_kernel<kEpiLogits><<<G, kMmaThreads, smem, s>>>(a); break;
-    case kEpiEmbAdd: batch_mma_kernel<kEpiEmbAdd><<<G, kMmaThreads, smem, s>>>(a); break;
+    case kEpiStore: launch_mma_t<kEpiStore>(a, G, exact, s); break;
+    case kEpiResid: launch_mma_t<kEpiResid>(a, G, exact, s); break;
+    case kEpiSwiGLU: launch_mma_t<kEpiSwiGLU>(a, G, exact, s); break;
+    case kEpiQKV: launch_mma_t<kEpiQKV>(a, G, exact, s); break;
+    case kEpiLogits: launch_mma_t<kEpiLogits>(a, G, exact, s); break;
+    case kEpiEmbAdd: launch_mma_t<kEpiEmbAdd>(a, G, exact, s); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -63,9 +63,11 @@ size_t batch_gemm_smem_bytes();
 int batch_gemm_grid(const QMatDesc &m, int sms);
 // Tensor-core form of the batched GEMM (kernels/batch_mma.cu): one CTA per SM
 // (at most the unit count), stream-K over (128-row block, chunk) units.
-// Split row blocks need a.ws (batch_mma_ws_floats) and a.cnt (one zeroed int
-// per 128-row block) with a.max_contrib >= batch_mma_max_contrib.
-cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epilogue, int sms, cudaStream_t s);
+// exact: the reference's half-block terms summed error-free (the batch-1
+// rounding); otherwise full-block terms summed in fp32.  Split row blocks
+// need a.ws (batch_mma_ws_floats) and a.cnt (one zeroed int per 128-row
+// block) with a.max_contrib >= batch_mma_max_contrib.
+cudaError_t launch_batch_mma(const BatchGemmArgs &a, int epilogue, int sms, bool exact, cudaStream_t s);
 int batch_mma_grid(const QMatDesc &m, int sms);
 int batch_mma_max_contrib(const QMatDesc &m, int sms);
 size_t batch_mma_ws_floats(const QMatDesc &m, int sms);

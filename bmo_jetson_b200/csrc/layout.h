@@ -154,13 +154,18 @@ struct FramePhase {
 
 // ---- batched sessions (config 4) ----
 // Q8_1 activations of S sessions, block-major, padded to P = S rounded up to
-// 16 sessions.  Block b occupies P * 32 bytes at xq + b * P * 32 in the
-// tensor core's K-major canonical layout (8-session x 16-byte core
-// matrices): bytes 0-15 of session s at (s / 8) * 256 + (s % 8) * 16, bytes
-// 16-31 at the same + 128.  Its scales are P floats pairs at xds + b * P * 2:
-// session pair p = s / 2 holds {d8[2p], d8[2p+1], -8 s8[2p], -8 s8[2p+1]}.
-// The 8 blocks of chunk kc are one contiguous run of P * 256 bytes (and
-// P * 64 bytes of scales), one bulk copy each.
+// 16 sessions, laid out as the tensor core's B operand with the two half
+// blocks of the reference's dot product (packed bytes 0-7 of a Q4_0 row hold
+// elements 0-7 and 16-23, bytes 8-15 elements 8-15 and 24-31) on separate
+// rows: block b occupies 64 P bytes at xq + b * 64 P; row R = 2s carries
+// session s's codes 0-7 and 16-23, row 2s + 1 its codes 8-15 and 24-31, each
+// at its own element position with zeros elsewhere, in the K-major canonical
+// layout of 8-row x 16-byte core matrices: bytes [16k, 16k + 16) of row R at
+// (R / 8) * 256 + k * 128 + (R % 8) * 16.  One MMA over the block then yields
+// both half-block sums of every session.  The block's scales are 3 P floats
+// at xds + 3 P b: P / 2 float4 {d8[2p], d8[2p+1], -M d8[2p], -M d8[2p+1]}
+// (M = 1.5 * 2^23), then P / 2 float2 {-4 s8[2p], -4 s8[2p+1]}.  The 8 blocks of
+// chunk kc are one contiguous run of 512 P bytes (and 96 P bytes of scales).
 constexpr int kBatchMax = 64;  // sessions per launch
 #if defined(__CUDACC__)
 __host__ __device__

@@ -84,10 +84,12 @@ BMO_API size_t bmo_k_batch_gemm_scratch_bytes(int rows, int cols, int perm, int 
  * Q4_0 x Q8_1 arithmetic of bmo_k_gemv_q4_0.  x_dev [n_sess][cols], y_dev
  * [n_sess][rows] ([n_sess][swiglu_f] for perm SWIGLU); gamma_dev and
  * resid_dev ([n_sess][rows]) as in bmo_k_gemv_q4_0.  tensor_cores = 1: int8
- * tcgen05 MMA per 32-column block into tensor memory, block scales applied
- * in fp32 (agrees with the reference to fp32 rounding); 0: CUDA cores with
- * the batch-1 GEMV's rounding.  scratch_dev must be zero on the first call
- * and is left reusable by every call that returns 0. */
+ * tcgen05 MMA per 32-column block into tensor memory, the reference's
+ * half-block terms summed error-free (the rounding of bmo_k_gemv_q4_0 up to
+ * rare ties); 2: tensor cores with full-block terms summed in fp32
+ * (fp32-accurate, not reproducible bit for bit); 0: CUDA cores with the
+ * batch-1 GEMV's rounding.  scratch_dev must be zero on the first call and
+ * is left reusable by every call that returns 0. */
 BMO_API int bmo_k_batch_gemm_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
                                   const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
                                   float *y_dev, int n_sess, int tensor_cores, void *scratch_dev,

@@ -2,11 +2,15 @@
 batched frame is the single-session greedy frame of its own session, checked
 against the CPU oracle running each session on its own ring.
 
-Two GEMM paths: the tensor-core path (default) computes every block's
-integer dot exactly and applies the block scales in fp32, so hidden states
-and logits agree with the oracle to the north-star bar (1e-3 relative L2);
-the CUDA-core path (BMO_BATCH_SIMT=1) keeps the batch-1 rounding and agrees
-to 1e-5.  Greedy text and audio tokens are identical.  A row's result does
+Both GEMM paths keep the batch-1 rounding -- the tensor-core path (default)
+computes the half-block integer dots exactly on the tensor cores and sums
+the reference-rounded terms error-free; the CUDA-core path
+(BMO_BATCH_GEMM=simt) sums them in double -- so hidden states and logits
+agree with the oracle to 1e-5 relative L2 (north-star bar 1e-3) through all
+32 layers, and greedy text and audio tokens are identical.  (The synthetic
+model is chaotic: a 1e-7 relative perturbation of the input grows to ~5% by
+the last layer through Q8_1 re-quantisation, so an fp32-accurate but
+differently rounded GEMM cannot meet the bar end to end.)  A row's result does
 not depend on which other rows share its frame, so rows of a 64-session
 frame are also checked bit-for-bit against the same rows run alone.
 """
@@ -19,12 +23,12 @@ from tests.parity import rel_l2
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"mma": 1e-3, "simt": 1e-5}
+TOL = {"tc": 1e-5, "simt": 1e-5}
 
 
-@pytest.fixture(params=["simt"])
+@pytest.fixture(params=["tc", "simt"])
 def path(request, monkeypatch):
-    monkeypatch.setenv("BMO_BATCH_SIMT", "1" if request.param == "simt" else "0")
+    monkeypatch.setenv("BMO_BATCH_GEMM", request.param)
     return request.param
 
 
