@@ -15,14 +15,17 @@
 // reference's fp32 roundings, two sessions per packed f32x2 instruction
 // (sumi -> float exactly through the 2^23 + 2^22 bias, one fma against
 // -M d8 = fl(sumi d8), one add of -4 s8, one multiply by d4), and
-//   EXACT: sum the terms error-free in a float pair (Knuth's two-sum: the sum
-//          carried to ~48 bits and rounded once at the end), which agrees
-//          with the double-sum semantics of the batch-1 GEMV and the oracle
-//          except at rare rounding ties;
+//   EXACT: sum the terms in double, rounded to fp32 once at the end -- the
+//          double-sum semantics of the batch-1 GEMV and the oracle (equal up
+//          to rare rounding ties from the summation order).  Each fp32 term
+//          becomes a double by rebuilding its bit pattern with integer
+//          operations (exact for every normal float and zero), which keeps the
+//          conversion off the slow fp32-to-fp64 conversion unit;
 //   !EXACT: one full-block term d4 (sumi d8 - 8 s8) per block, summed in
 //          fp32 (fp32-accurate, not reproducible bit for bit).
 //
-// CTA (one per SM, 10 warps):
+// CTA (one per SM, 12 warps; registers moved from the third warpgroup to the
+// two epilogue warpgroups with setmaxnreg):
 //   warp 9       TMEM owner; lane 0 the bulk-copy producer (per 8-block chunk
 //                the four 32-row tiles' Q4_0 chunks of a 128-row block, 4 x
 //                4608 B from HBM, the sessions' split Q8_1 codes, 512 P B, and
@@ -60,7 +63,13 @@ constexpr int kABlockBytes = kMmaRows * 32;      // one block of A: 128 rows x 3
 constexpr int kABytes = kChunkBlocks * kABlockBytes;
 constexpr int kEpiWarps = 8, kUnpackWarps = 1;
 constexpr int kCtlWarp = 9;  // lane 0: bulk-copy producer, lane 1: MMA issuer; the warp owns TMEM
-constexpr int kMmaThreads = 10 * 32;
+constexpr int kMmaThreads = 12 * 32;  // three warpgroups; warps 10-11 only complete the third
+// Register split (setmaxnreg, inside each role's branch): the launch gives
+// every thread 168 registers (12 warps x 32 x 168 = 64512); the third
+// warpgroup drops to 56 and the two epilogue warpgroups rise to 224:
+// 2 x 128 x 224 + 128 x 56 = 64512, all of the launch's registers.
+constexpr int kLaunchRegs = 168, kEpiRegs = 224, kCtlRegs = 56;
+static_assert(2 * 128 * kEpiRegs + 128 * kCtlRegs <= kMmaThreads * kLaunchRegs, "register split exceeds the launch");
 static_assert(kRawBytes % 1024 == 0 && kABytes % 1024 == 0, "stage buffers stay 1 KB aligned");
 static_assert(2 * kBatchMax <= kMmaSlotCols, "a slot holds both halves of every session");
 
@@ -145,12 +154,26 @@ __device__ __forceinline__ uint32_t idesc_i8(int n) {
            (static_cast<uint32_t>(kMmaRows >> 4) << 24);
 }
 
-// Bounded mbarrier wait that also gives up when another role has aborted.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// mbarrier wait for the pipeline hand-offs: spins on try_wait (which itself
+// suspends the thread for a short hardware-chosen time) without sleeping in
+// between -- a sleep here would add its latency to every stage of every unit
+// -- and gives up after 2 s, or as soon as another role has aborted.
+constexpr uint64_t kWaitNs = 2000000000ull;
 __device__ __forceinline__ bool wait_ab(uint64_t *bar, uint32_t parity, volatile int *abort) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (i > 32) __nanosleep(64);
+        if ((i & 63) == 0) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kWaitNs) break;
+        }
     }
     *abort = 1;
     return false;
@@ -250,24 +273,21 @@ __device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Knuth's two-sum of packed pairs: (s, c) += t with s + c carried error-free
-// to ~48 bits (fma(x, -1, y) is the exactly rounded y - x).
-__device__ __forceinline__ void two_sum_acc(float2 &s, float2 &c, float2 t) {
-    const float2 m1 = make_float2(-1.0f, -1.0f);
-    const float2 n = __fadd2_rn(s, t);
-    const float2 bb = __ffma2_rn(s, m1, n);   // n - s
-    const float2 a1 = __ffma2_rn(bb, m1, n);  // n - bb
-    const float2 a2 = __ffma2_rn(a1, m1, s);  // s - (n - bb)
-    const float2 b2 = __ffma2_rn(bb, m1, t);  // t - bb
-    c = __fadd2_rn(c, __fadd2_rn(a2, b2));
-    s = n;
+// fp32 -> fp64 from the bit pattern: sign, exponent rebiased by 1023 - 127,
+// mantissa shifted to the top of the 52-bit field.  Exact for normal floats
+// and zero; a subnormal float (|x| < 2^-126, never a decode term) comes out
+// within 2^-126 of its value.
+__device__ __forceinline__ double f2d_bits(float x) {
+    const unsigned f = __float_as_uint(x), mag = f & 0x7FFFFFFFu, sign = f & 0x80000000u;
+    const unsigned hi = mag ? (((mag >> 3) + 0x38000000u) | sign) : sign;
+    return __hiloint2double(static_cast<int>(hi), static_cast<int>(f << 29));
 }
 
 // Terms of one 8-session register buffer r (r[2i] low-half sum, r[2i + 1]
 // high-half sum of session i) into the accumulators of pairs [4k, 4k + 4).
 template <bool EXACT>
 __device__ __forceinline__ void mma_terms(const uint32_t (&r)[16], const float4 *sc4, const float2 *sc2, float d4,
-                                          float2 (&S)[16], float2 (&C)[16], int k) {
+                                          float2 (&S)[16], double (&D)[32], int k) {
     const float2 d44 = make_float2(d4, d4);
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
@@ -281,10 +301,12 @@ __device__ __forceinline__ void mma_terms(const uint32_t (&r)[16], const float4 
                                            __int_as_float(static_cast<int>(r[4 * jj + 2]) + 0x4B400000));
             const float2 fhi = make_float2(__int_as_float(static_cast<int>(r[4 * jj + 1]) + 0x4B400000),
                                            __int_as_float(static_cast<int>(r[4 * jj + 3]) + 0x4B400000));
-            float2 t = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(flo, d8, nm), m4));
-            two_sum_acc(S[J], C[J], t);
-            t = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(fhi, d8, nm), m4));
-            two_sum_acc(S[J], C[J], t);
+            const float2 tl = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(flo, d8, nm), m4));
+            const float2 th = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(fhi, d8, nm), m4));
+            D[2 * J] += f2d_bits(tl.x);
+            D[2 * J + 1] += f2d_bits(tl.y);
+            D[2 * J] += f2d_bits(th.x);
+            D[2 * J + 1] += f2d_bits(th.y);
         } else {
             const float2 f = make_float2(
                 __int_as_float(static_cast<int>(r[4 * jj] + r[4 * jj + 1]) + 0x4B400000),
@@ -336,6 +358,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
 
+    if (warp >= kEpiWarps) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtlRegs));
     if (warp == kCtlWarp) {
         // ---------------- bulk-copy producer (lane 0) ----------------
         int issued = 0;
@@ -424,13 +448,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 mbar_arrive(&S.raw_empty[sg]);
             }
         }
-    } else if (warp < kEpiWarps) {
+    }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kEpiRegs));
         // ---------------- epilogue warps ----------------
         const int q = warp & 3, h = warp >> 2;
         const bool active = h < groups;
-        float2 Sacc[16], Cacc[16];
+        float2 Sacc[16];  // fast: fp32 sums of session pairs
+        double Dacc[32];  // exact: double sums of each session
 #pragma unroll
-        for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + 64 * h;
         uint32_t rA[16], rB[16];
         bool ok = true;
@@ -456,18 +485,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 const float4 *sc4 = reinterpret_cast<const float4 *>(scb) + 16 * h;
                 const float2 *sc2 = reinterpret_cast<const float2 *>(scb + P * 8) + 16 * h;
                 tmem_ld16_nowait(ta + 16, rB);
-                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Cacc, 0);
+                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Dacc, 0);
                 tmem_wait_ld();
                 tmem_ld16_nowait(ta + 32, rA);
-                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Cacc, 1);
+                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Dacc, 1);
                 tmem_wait_ld();
                 tmem_ld16_nowait(ta + 48, rB);
-                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Cacc, 2);
+                mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Dacc, 2);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.tm_empty[slot]);  // every read of the slot has completed
-                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Cacc, 3);
+                mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Dacc, 3);
             }
             if (!ok) break;
             __syncwarp();
@@ -478,23 +507,30 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
             const int t = st * kMmaTiles + q;
             const long long first = static_cast<long long>(st) * cpt, lastu = first + cpt - 1;
             if (first >= u0 && lastu < u1) {
+                if constexpr (EXACT) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) Sacc[j] = __fadd2_rn(Sacc[j], Cacc[j]);
+                    for (int j = 0; j < 16; ++j)
+                        Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j]), __double2float_rn(Dacc[2 * j + 1]));
+                }
                 mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
             } else {
                 const int cf = cta_of(first, U, G), cl = cta_of(lastu, U, G);
                 const int n_c = cl - cf + 1;
-                const size_t plane = static_cast<size_t>(P) * kMmaRows;  // one float per (session, row)
-                float *part = a.ws + (static_cast<size_t>(st) * a.max_contrib + (c - cf)) * 2 * plane;
+                const size_t slab = static_cast<size_t>(P) * kMmaRows;  // one double (exact) or float per (session, row)
+                double *part_d = reinterpret_cast<double *>(a.ws) + (static_cast<size_t>(st) * a.max_contrib + (c - cf)) * slab;
+                float *part_f = reinterpret_cast<float *>(part_d);
                 // the partial holds P sessions: padding sessions beyond P are not stored
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     if (32 * h + 2 * j < P) {
                         const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
-                        part[i0] = Sacc[j].x;
-                        part[i0 + kMmaRows] = Sacc[j].y;
-                        part[plane + i0] = Cacc[j].x;
-                        part[plane + i0 + kMmaRows] = Cacc[j].y;
+                        if constexpr (EXACT) {
+                            part_d[i0] = Dacc[2 * j];
+                            part_d[i0 + kMmaRows] = Dacc[2 * j + 1];
+                        } else {
+                            part_f[i0] = Sacc[j].x;
+                            part_f[i0 + kMmaRows] = Sacc[j].y;
+                        }
                     }
                 }
                 __threadfence();
@@ -507,29 +543,38 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 }
                 named_sync(1, 128 * groups);
                 if (S.last) {
+                    // partials added in contributor order: the result does not depend on timing
+                    const double *base = reinterpret_cast<const double *>(a.ws) + static_cast<size_t>(st) * a.max_contrib * slab;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
-                    const float *base = a.ws + static_cast<size_t>(st) * a.max_contrib * 2 * plane;
-                    for (int k = 0; k < n_c; ++k) {
-                        const float *pk = base + k * 2 * plane;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            if (32 * h + 2 * j < P) {
-                                const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
-                                two_sum_acc(Sacc[j], Cacc[j], make_float2(__ldcg(pk + i0), __ldcg(pk + i0 + kMmaRows)));
-                                Cacc[j] = __fadd2_rn(Cacc[j], make_float2(__ldcg(pk + plane + i0),
-                                                                          __ldcg(pk + plane + i0 + kMmaRows)));
+                    for (int j = 0; j < 16; ++j) {
+                        if (32 * h + 2 * j < P) {
+                            const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
+                            if constexpr (EXACT) {
+                                double x = 0.0, y = 0.0;
+                                for (int k = 0; k < n_c; ++k) {
+                                    x += __ldcg(base + k * slab + i0);
+                                    y += __ldcg(base + k * slab + i0 + kMmaRows);
+                                }
+                                Sacc[j] = make_float2(__double2float_rn(x), __double2float_rn(y));
+                            } else {
+                                float x = 0.0f, y = 0.0f;
+                                for (int k = 0; k < n_c; ++k) {
+                                    const float *pk = reinterpret_cast<const float *>(base + k * slab);
+                                    x = __fadd_rn(x, __ldcg(pk + i0));
+                                    y = __fadd_rn(y, __ldcg(pk + i0 + kMmaRows));
+                                }
+                                Sacc[j] = make_float2(x, y);
                             }
                         }
                     }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) Sacc[j] = __fadd2_rn(Sacc[j], Cacc[j]);
                     mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
                 }
                 named_sync(1, 128 * groups);  // S.last is reused by the next block
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) Sacc[j] = Cacc[j] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
         }
         tc_fence_before();
     }
@@ -574,13 +619,23 @@ size_t batch_mma_ws_floats(const QMatDesc &m, int sms) {
     return static_cast<size_t>(n_super) * batch_mma_max_contrib(m, sms) * 2 * kBatchMax * kMmaRows;
 }
 
+// Sets the shared-memory opt-in and checks that the compiled kernel launches
+// with exactly the registers the setmaxnreg split is computed from (a launch
+// with fewer would leave the epilogue warpgroups waiting for registers).
+template <int EPI, bool EXACT>
+static cudaError_t configure_mma_one() {
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, batch_mma_kernel<EPI, EXACT>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kMmaThreads) return cudaErrorInvalidDeviceFunction;
+    return cudaFuncSetAttribute(batch_mma_kernel<EPI, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(sizeof(MmaSmem)));
+}
+
 template <int EPI>
 static cudaError_t configure_mma() {
-    const int bytes = static_cast<int>(sizeof(MmaSmem));
-    cudaError_t e = cudaFuncSetAttribute(batch_mma_kernel<EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(batch_mma_kernel<EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    return e;
+    const cudaError_t e = configure_mma_one<EPI, true>();
+    return e != cudaSuccess ? e : configure_mma_one<EPI, false>();
 }
 
 static std::atomic<unsigned long long> g_mma_configured{0};  // bit per device

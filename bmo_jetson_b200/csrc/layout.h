@@ -230,9 +230,9 @@ struct BatchGemmArgs {
     EmbTable emb;
     const int *tok;          // [S]
     int *status;
-    // tensor-core path: split row blocks combine through ws (fp32 partial
-    // sums, [row block][contributor][P][128]) and cnt (one zeroed counter per
-    // 128-row block)
+    // tensor-core path: split row blocks combine through ws (partial sums,
+    // one double per (session, row): [row block][contributor][P][128]) and
+    // cnt (one zeroed counter per 128-row block)
     float *ws;
     int *cnt;
     int max_contrib;
