@@ -299,6 +299,74 @@ def bench_batch(path, local, dist, sessions, steps, warmup, rank):
                       "greedy frame (temporal + text head + 8-step depformer) per session per step"}
 
 
+def run_tp(args, rank, world, local):
+    """Config 5: one session split over the world's GPUs (attention heads and
+    FFN columns per rank, a double all-reduce after each O-projection and
+    FFN-out).  Every rank decodes the same frames; rank 0 prints frames/s of
+    the single stream and p50/p99 frame times (device events, max over ranks)."""
+    import torch
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    path = prepare_model(rank, dist)
+    from bmo_jetson_b200 import engine
+    gid = torch.zeros(128, dtype=torch.uint8)
+    if rank == 0:
+        gid = torch.frombuffer(bytearray(engine.tp_unique_id()), dtype=torch.uint8)
+    if dist is not None:
+        g = gid.cuda()
+        dist.broadcast(g, 0)
+        gid = g.cpu()
+    kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
+    e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type, tp=(rank, world, bytes(gid.numpy())))
+    rng = np.random.default_rng(7)
+    width = e.n_kv_heads * e.head_dim
+    for layer in range(e.n_layers):  # the same history on every rank, each keeps its heads
+        k = rng.standard_normal((N_CTX, width * world), dtype=np.float32)
+        v = rng.standard_normal((N_CTX, width * world), dtype=np.float32)
+        e.kv_import(layer, 0, k[:, rank * width:(rank + 1) * width], v[:, rank * width:(rank + 1) * width])
+    assert e.capture_graphs() == 0
+    K = e.n_codebooks
+    dev = torch.device("cuda", local)
+    toks_d = torch.from_numpy(frame_tokens(args.warmup + args.steps, K, e.text_vocab, e.audio_vocab)).to(dev)
+    out_d = torch.zeros((args.warmup + args.steps, 1 + e.dep_q), dtype=torch.int32, device=dev)
+    stream = torch.cuda.ExternalStream(e.stream, device=dev)
+    pos = START_POS
+    for i in range(args.warmup):
+        e.enqueue_frame(toks_d[i].data_ptr(), K, pos, out_d[i].data_ptr())
+        pos += 1
+    e.sync()
+    barrier(dist)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record(stream)
+    for i in range(args.steps):
+        e.enqueue_frame(toks_d[args.warmup + i].data_ptr(), K, pos, out_d[args.warmup + i].data_ptr())
+        evs[i + 1].record(stream)
+        pos += 1
+    e.sync()
+    torch.cuda.synchronize(dev)
+    per = np.array([evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)])
+    ms = reduce_max(dist, float(per.mean()))
+    p50, p99 = reduce_max(dist, float(np.percentile(per, 50))), reduce_max(dist, float(np.percentile(per, 99)))
+    toks = out_d.cpu().numpy()
+    barrier(dist)
+    if rank == 0:
+        print(json.dumps({"metric": "Moshi decode frames/s (B=1, tensor parallel)", "value": 1000.0 / ms,
+                          "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": ms, "p50_ms": p50, "p99_ms": p99, "higher_is_better": True,
+                          "scaling": "strong", "vs_baseline": None, "impl": "ours",
+                          "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales), double partial sums over ranks",
+                          "data": "synthetic: seeded weights, tokens and KV history",
+                          "config": {"workload": "config5: one session, 32-layer temporal + text head + 8-step "
+                                                 "depformer per frame, heads and FFN columns split over the GPUs",
+                                     "parallelism": f"tp{world}", "n_ctx": N_CTX, "start_pos": START_POS,
+                                     "kv": args.kv},
+                          "text_tokens_head": toks[args.warmup:args.warmup + 4, 0].tolist()}), flush=True)
+    e.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def traffic_from_profile():
     p = os.path.join(ROOT, "profiles", "gemv_ffn_in_traffic.json")
     try:
@@ -387,6 +455,8 @@ def main():
     ap.add_argument("--sessions", type=int, default=64,
                     help="config 4: sessions per GPU of the batched measurement (0: skip it)")
     ap.add_argument("--batch-only", action="store_true", help="only the batched-sessions measurement")
+    ap.add_argument("--tp", action="store_true",
+                    help="config 5: one session tensor-parallel over the --gpus ranks (prints its own line)")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="profiling: run --warmup frames then this many device-resident frames, print nothing else")
     args = ap.parse_args()
@@ -394,6 +464,8 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.tp:
+        return run_tp(args, rank, world, local)
 
     import torch
     peak, peak_kind = measured_peaks()

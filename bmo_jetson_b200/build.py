@@ -89,7 +89,7 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
     lib_time = os.path.getmtime(LIB) if os.path.exists(LIB) else -1.0
     if cmds or force or lib_time < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        _compile([NVCC] + ARCH + ["-shared", "-ccbin", CXX, "-o", tmp] + objs + ["-cudart", "static", "-lpthread"])
+        _compile([NVCC] + ARCH + ["-shared", "-ccbin", CXX, "-o", tmp] + objs + ["-cudart", "static", "-lpthread", "-ldl"])
         os.replace(tmp, LIB)
     return LIB
 

@@ -105,6 +105,37 @@ bmo_handle_t *bmo_init_ex(const char *gguf_path, int n_ctx, int device, int kv_t
     return create(gguf_path, n_ctx, c);
 }
 
+int bmo_tp_unique_id(void *out_id) {
+    if (!out_id) return 1;
+    try {
+        bmo::tp_unique_id(out_id);
+        return 0;
+    } catch (const std::exception &e) {
+        std::fprintf(stderr, "[bmo_api] bmo_tp_unique_id: %s\n", e.what());
+        return 9;
+    }
+}
+
+bmo_handle_t *bmo_init_tp(const char *gguf_path, int n_ctx, int device, int kv_type, int flags, int tp_rank,
+                          int tp_size, const void *tp_id) {
+    if (!tp_id || tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) {
+        std::fprintf(stderr, "[bmo_api] bmo_init_tp: invalid rank, size or id\n");
+        return nullptr;
+    }
+    bmo::EngineConfig c;
+    c.device = device;
+    c.kv_type = kv_type;
+    c.graphs = !(flags & BMO_FLAG_NO_GRAPHS);
+    c.pdl = !(flags & BMO_FLAG_NO_PDL);
+    c.tp_rank = tp_rank;
+    c.tp_size = tp_size;
+    std::memcpy(c.tp_id, tp_id, sizeof c.tp_id);
+    return create(gguf_path, n_ctx, c);
+}
+
+int bmo_get_tp_size(bmo_handle_t *h) { return (h && h->eng) ? h->eng->tp_size : 0; }
+int bmo_get_tp_rank(bmo_handle_t *h) { return (h && h->eng) ? h->eng->tp_rank : 0; }
+
 void bmo_free(bmo_handle_t *h) {
     if (!h) return;
     try {

@@ -93,6 +93,7 @@ int Engine::batch_init(int n_sessions) {
     if (batch_) return batch_->n_max == n_sessions ? 0 : 3;
     if (!has_text_head || !has_dep_tables || dep_dim <= 0 || dep_q <= 0)
         throw std::runtime_error("batched frames need the text head and the depformer");
+    if (tensor_parallel) throw std::runtime_error("batched frames are not available on a tensor-parallel handle");
     ck(cudaSetDevice(device), "cudaSetDevice");
     std::unique_ptr<BatchState, BatchDeleter> b(new BatchState);
     const int S = kBatchMax;  // activation rows are sized for the largest batch

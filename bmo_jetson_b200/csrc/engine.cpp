@@ -76,11 +76,19 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
         const char *kt = std::getenv("BMO_KV_TYPE");
         kv_type = (kt && (std::strcmp(kt, "q4_0") == 0 || std::strcmp(kt, "q4") == 0)) ? kKvQ4_0 : kKvF16;
     }
+    if (cfg.tp_size >= 1) {
+        tensor_parallel = true;
+        tp_size = cfg.tp_size;
+        tp_rank = cfg.tp_rank;
+        if (tp_rank < 0 || tp_rank >= tp_size) throw std::runtime_error("tensor parallel: rank outside [0, size)");
+        cfg_.persistent = false;  // the frame kernel has no collective step
+    }
     load(gguf_path);
+    if (tensor_parallel) tp_comm_.reset(new TpComm(cfg.tp_id, tp_rank, tp_size));
     alloc_state();
     // BMO_DEP_FOLD=1: the depformer attention runs inside its O-projection GEMV
     // (measured slower than a separate attention kernel on B200, so off by default)
-    dep_fold_ = dep_hd == gemv_dep_attn_head_dim() && dep_n_ctx <= gemv_dep_attn_max_window() &&
+    dep_fold_ = !tensor_parallel && dep_hd == gemv_dep_attn_head_dim() && dep_n_ctx <= gemv_dep_attn_max_window() &&
                 dep_heads * dep_hd <= gemv_max_norm_cols() && env_int("BMO_DEP_FOLD", 0) != 0;
     build_programs();
 }
@@ -93,12 +101,13 @@ Engine::~Engine() {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
     };
-    drop(g_temporal_);
+    drop(g_temporal_);  // graphs holding NCCL calls go before the communicator
     drop(g_layers_);
     drop(g_cascade_z_);
     drop(g_cascade_);
     drop(g_frame_);
     for (auto &g : g_depth_) drop(g);
+    tp_comm_.reset();
     for (void *p : allocs_) cudaFree(p);
     for (void *p : {(void *)fin_h_, (void *)z_h_, (void *)logits_h_, (void *)zin_h_, (void *)dlogits_h_,
                     (void *)tok_h_, (void *)status_h_})
@@ -126,6 +135,36 @@ QMatDesc Engine::upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t 
     if (cols % 32) throw std::runtime_error("weight " + t->name + ": row length not a multiple of 32");
     if (rows < 0) rows = t->rows() - row0;
     if (row0 + rows > t->rows()) throw std::runtime_error("weight " + t->name + ": row slice out of range");
+    const size_t row_bytes = static_cast<size_t>(cols / 32) * 18;
+    return upload_q4_raw(t->name, t->data + static_cast<size_t>(row0) * row_bytes, rows, cols, perm, swiglu_f);
+}
+
+QMatDesc Engine::upload_q4_sel(const GgufTensor *t, int perm, int swiglu_f,
+                               const std::vector<std::pair<int64_t, int64_t>> &row_ranges, int64_t col0, int64_t ncols) {
+    if (!t) throw std::runtime_error("internal: null weight");
+    if (t->type != kTQ4_0) throw std::runtime_error("weight " + t->name + " is not Q4_0 (only Q4_0 GEMV weights are supported)");
+    const int64_t cols = t->ne[0];
+    if (cols % 32 || col0 % 32 || ncols % 32 || col0 < 0 || ncols <= 0 || col0 + ncols > cols)
+        throw std::runtime_error("weight " + t->name + ": column slice not on 32-column blocks");
+    int64_t rows = 0;
+    for (const auto &r : row_ranges) {
+        if (r.first < 0 || r.second <= 0 || r.first + r.second > t->rows())
+            throw std::runtime_error("weight " + t->name + ": row slice out of range");
+        rows += r.second;
+    }
+    // gather the selected rows' blocks on the host, then the regular upload + repack
+    const size_t src_row = static_cast<size_t>(cols / 32) * 18, dst_row = static_cast<size_t>(ncols / 32) * 18;
+    std::vector<uint8_t> host(static_cast<size_t>(rows) * dst_row);
+    size_t o = 0;
+    for (const auto &r : row_ranges)
+        for (int64_t i = 0; i < r.second; ++i, o += dst_row)
+            std::memcpy(&host[o], t->data + static_cast<size_t>(r.first + i) * src_row + static_cast<size_t>(col0 / 32) * 18,
+                        dst_row);
+    return upload_q4_raw(t->name, host.data(), rows, ncols, perm, swiglu_f);
+}
+
+QMatDesc Engine::upload_q4_raw(const std::string &name, const uint8_t *src, int64_t rows, int64_t cols, int perm,
+                               int swiglu_f) {
     QMatDesc m{};
     m.rows = static_cast<int>(perm == kPermSwiGLU ? 2 * swiglu_f : rows);
     m.cols = static_cast<int>(cols);
@@ -134,15 +173,13 @@ QMatDesc Engine::upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t 
     m.perm = perm;
     m.swiglu_f = swiglu_f;
     m.n_tiles = static_cast<int>(perm == kPermSwiGLU ? swiglu_f / 16 : (rows + kTileRows - 1) / kTileRows);
-    if (m.nbx > gemv_max_nbx()) throw std::runtime_error("weight " + t->name + ": row length exceeds the GEMV limit");
+    if (m.nbx > gemv_max_nbx()) throw std::runtime_error("weight " + name + ": row length exceeds the GEMV limit");
     const size_t bytes = static_cast<size_t>(m.n_tiles) * m.cpt * kChunkBytes;
     void *dst = arena(bytes);
     m.tiles = static_cast<const uint8_t *>(dst);
-    const size_t row_bytes = static_cast<size_t>(cols / 32) * 18;
-    const size_t raw = row_bytes * static_cast<size_t>(rows);
+    const size_t raw = static_cast<size_t>(cols / 32) * 18 * static_cast<size_t>(rows);
     if (raw > staging_bytes_) throw std::runtime_error("internal: staging buffer too small");
-    ck(cudaMemcpyAsync(staging_d_, t->data + static_cast<size_t>(row0) * row_bytes, raw, cudaMemcpyHostToDevice, stream),
-       "upload weight");
+    ck(cudaMemcpyAsync(staging_d_, src, raw, cudaMemcpyHostToDevice, stream), "upload weight");
     ck(launch_repack_q4_0(staging_d_, dst, static_cast<int>(rows), static_cast<int>(cols), m, stream), "repack");
     ck(cudaStreamSynchronize(stream), "repack sync");
     return m;
@@ -309,22 +346,41 @@ void Engine::load(const std::string &path) {
         dep_q = dq;  // geometry still reported; depth calls fail with a clear error
     }
 
+    // ---- tensor parallel: this rank's heads and FFN columns ----
+    const int T = tensor_parallel ? tp_size : 1, R = tensor_parallel ? tp_rank : 0;
+    const int kv_dim_g = n_kv_heads * head_dim, ffn_g = ffn, dep_ffn_g = dep_ffn;
+    if (tensor_parallel) {
+        if (n_heads % T || n_kv_heads % T || ffn % (32 * T) || (dep_ok && (dep_heads % T || dep_ffn % (32 * T))))
+            throw std::runtime_error("tensor parallel: heads and FFN widths must split into 32-column shards over " +
+                                     std::to_string(T) + " ranks");
+        n_heads /= T;
+        n_kv_heads /= T;
+        ffn /= T;
+        if (dep_ok) {
+            dep_heads /= T;
+            dep_ffn /= T;
+        }
+    }
+    const int q_l = n_heads * head_dim, kv_l = n_kv_heads * head_dim;  // this rank's q / kv widths
+    const int dq_l = dep_heads * dep_hd;                                  // depformer q width per rank
+
     // ---- size the weight arena ----
     size_t total = 0, staging = 0;
-    auto plan_q4 = [&](const GgufTensor *t, int perm, int f, int64_t rows) {
+    auto plan_q4c = [&](const GgufTensor *t, int perm, int f, int64_t rows, int64_t cols) {
         if (!t) return;
-        const int64_t r = rows < 0 ? t->rows() : rows;
-        total += round_up(q4_tiled_bytes(r, t->ne[0], perm, f), 256);
-        staging = std::max(staging, static_cast<size_t>(r * (t->ne[0] / 32) * 18));
+        const int64_t r = rows < 0 ? t->rows() : rows, c = cols < 0 ? t->ne[0] : cols;
+        total += round_up(q4_tiled_bytes(r, c, perm, f), 256);
+        staging = std::max(staging, static_cast<size_t>(r * (c / 32) * 18));
     };
+    auto plan_q4 = [&](const GgufTensor *t, int perm, int f, int64_t rows) { plan_q4c(t, perm, f, rows, -1); };
     auto plan_bytes = [&](const GgufTensor *t) {
         if (t) total += round_up(t->nbytes, 256);
     };
     for (int i = 0; i < n_layers; ++i) {
-        plan_q4(ln[i].qkv, kPermIdentity, 0, -1);
-        plan_q4(ln[i].wo, kPermIdentity, 0, -1);
-        plan_q4(ln[i].fin, kPermSwiGLU, ffn, -1);
-        plan_q4(ln[i].fout, kPermIdentity, 0, -1);
+        plan_q4(ln[i].qkv, kPermIdentity, 0, q_l + 2 * kv_l);
+        plan_q4c(ln[i].wo, kPermIdentity, 0, -1, q_l);
+        plan_q4(ln[i].fin, kPermSwiGLU, ffn, 2LL * ffn);
+        plan_q4c(ln[i].fout, kPermIdentity, 0, -1, ffn);
         plan_bytes(ln[i].n1);
         plan_bytes(ln[i].n2);
     }
@@ -342,10 +398,10 @@ void Engine::load(const std::string &path) {
         plan_bytes(dep_text_t);
         for (int i = 0; i < kDepLayers; ++i) {
             for (int s = 0; s < dep_q; ++s) {
-                plan_q4(dn[i].in, kPermIdentity, 0, 3LL * dep_dim);
-                plan_q4(dn[i].out, kPermIdentity, 0, dep_dim);
-                plan_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, -1);
-                plan_q4(dn[i].gout[s], kPermIdentity, 0, -1);
+                plan_q4(dn[i].in, kPermIdentity, 0, 3LL * dq_l);
+                plan_q4c(dn[i].out, kPermIdentity, 0, dep_dim, dq_l);
+                plan_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, 2LL * dep_ffn);
+                plan_q4c(dn[i].gout[s], kPermIdentity, 0, -1, dep_ffn);
             }
             plan_bytes(dn[i].n1);
             plan_bytes(dn[i].n2);
@@ -360,16 +416,31 @@ void Engine::load(const std::string &path) {
     // ---- upload ----
     L_.resize(n_layers);
     for (int i = 0; i < n_layers; ++i) {
-        L_[i].qkv = upload_q4(ln[i].qkv, kPermIdentity, 0, 0, -1);
-        L_[i].wo = upload_q4(ln[i].wo, kPermIdentity, 0, 0, -1);
-        if (ln[i].fin->rows() != 2LL * ffn) throw std::runtime_error("FFN-in width differs between layers");
-        L_[i].ffn_in = upload_q4(ln[i].fin, kPermSwiGLU, ffn, 0, -1);
-        L_[i].ffn_out = upload_q4(ln[i].fout, kPermIdentity, 0, 0, -1);
+        if (ln[i].fin->rows() != 2LL * ffn_g) throw std::runtime_error("FFN-in width differs between layers");
+        if (ln[i].qkv->rows() != qkv_w || ln[i].wo->rows() != n_embd || ln[i].wo->ne[0] != q_dim ||
+            ln[i].fout->ne[0] != ffn_g || ln[i].fout->rows() != n_embd)
+            throw std::runtime_error("inconsistent temporal weight shapes in layer " + std::to_string(i));
+        if (tensor_parallel) {
+            // q rows of this rank's heads, then its k rows, then its v rows; O-proj and
+            // FFN-out columns of the same heads / FFN slice; FFN-in gate and up rows
+            L_[i].qkv = upload_q4_sel(ln[i].qkv, kPermIdentity, 0,
+                                      {{static_cast<int64_t>(R) * q_l, q_l},
+                                       {q_dim + static_cast<int64_t>(R) * kv_l, kv_l},
+                                       {q_dim + kv_dim_g + static_cast<int64_t>(R) * kv_l, kv_l}},
+                                      0, n_embd);
+            L_[i].wo = upload_q4_sel(ln[i].wo, kPermIdentity, 0, {{0, n_embd}}, static_cast<int64_t>(R) * q_l, q_l);
+            L_[i].ffn_in = upload_q4_sel(ln[i].fin, kPermSwiGLU, ffn,
+                                         {{static_cast<int64_t>(R) * ffn, ffn}, {ffn_g + static_cast<int64_t>(R) * ffn, ffn}},
+                                         0, n_embd);
+            L_[i].ffn_out = upload_q4_sel(ln[i].fout, kPermIdentity, 0, {{0, n_embd}}, static_cast<int64_t>(R) * ffn, ffn);
+        } else {
+            L_[i].qkv = upload_q4(ln[i].qkv, kPermIdentity, 0, 0, -1);
+            L_[i].wo = upload_q4(ln[i].wo, kPermIdentity, 0, 0, -1);
+            L_[i].ffn_in = upload_q4(ln[i].fin, kPermSwiGLU, ffn, 0, -1);
+            L_[i].ffn_out = upload_q4(ln[i].fout, kPermIdentity, 0, 0, -1);
+        }
         L_[i].norm1 = upload_f32(ln[i].n1, n_embd);
         L_[i].norm2 = upload_f32(ln[i].n2, n_embd);
-        if (L_[i].qkv.rows != qkv_w || L_[i].wo.rows != n_embd || L_[i].wo.cols != q_dim ||
-            L_[i].ffn_out.cols != ffn || L_[i].ffn_out.rows != n_embd)
-            throw std::runtime_error("inconsistent temporal weight shapes in layer " + std::to_string(i));
     }
     if (tl) {
         if (tl->ne[0] != n_embd) throw std::runtime_error("text_linear width does not match n_embd");
@@ -400,10 +471,25 @@ void Engine::load(const std::string &path) {
         for (int i = 0; i < kDepLayers; ++i) {
             for (int s = 0; s < dep_q; ++s) {
                 // per-step row slices of the stacked projections (bmo_compute.cpp:2908-2932)
-                D_[i].qkv[s] = upload_q4(dn[i].in, kPermIdentity, 0, 3LL * dep_dim * s, 3LL * dep_dim);
-                D_[i].wo[s] = upload_q4(dn[i].out, kPermIdentity, 0, static_cast<int64_t>(dep_dim) * s, dep_dim);
-                D_[i].ffn_in[s] = upload_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, 0, -1);
-                D_[i].ffn_out[s] = upload_q4(dn[i].gout[s], kPermIdentity, 0, 0, -1);
+                if (tensor_parallel) {
+                    const int64_t b = 3LL * dep_dim * s, hr = static_cast<int64_t>(R) * dq_l;
+                    D_[i].qkv[s] = upload_q4_sel(dn[i].in, kPermIdentity, 0,
+                                                 {{b + hr, dq_l}, {b + dep_dim + hr, dq_l}, {b + 2LL * dep_dim + hr, dq_l}},
+                                                 0, dep_dim);
+                    D_[i].wo[s] = upload_q4_sel(dn[i].out, kPermIdentity, 0, {{static_cast<int64_t>(dep_dim) * s, dep_dim}},
+                                                hr, dq_l);
+                    D_[i].ffn_in[s] = upload_q4_sel(dn[i].gin[s], kPermSwiGLU, dep_ffn,
+                                                    {{static_cast<int64_t>(R) * dep_ffn, dep_ffn},
+                                                     {dep_ffn_g + static_cast<int64_t>(R) * dep_ffn, dep_ffn}},
+                                                    0, dep_dim);
+                    D_[i].ffn_out[s] = upload_q4_sel(dn[i].gout[s], kPermIdentity, 0, {{0, dep_dim}},
+                                                     static_cast<int64_t>(R) * dep_ffn, dep_ffn);
+                } else {
+                    D_[i].qkv[s] = upload_q4(dn[i].in, kPermIdentity, 0, 3LL * dep_dim * s, 3LL * dep_dim);
+                    D_[i].wo[s] = upload_q4(dn[i].out, kPermIdentity, 0, static_cast<int64_t>(dep_dim) * s, dep_dim);
+                    D_[i].ffn_in[s] = upload_q4(dn[i].gin[s], kPermSwiGLU, dep_ffn, 0, -1);
+                    D_[i].ffn_out[s] = upload_q4(dn[i].gout[s], kPermIdentity, 0, 0, -1);
+                }
             }
             D_[i].norm1 = upload_f32(dn[i].n1, dep_dim);
             D_[i].norm2 = upload_f32(dn[i].n2, dep_dim);
@@ -488,6 +574,7 @@ void Engine::alloc_state() {
     gpart_ = static_cast<double *>(dalloc(gp));
     gcount_ = static_cast<int *>(dalloc(gc));
 
+    tp_part_ = static_cast<double *>(dalloc(sizeof(double) * std::max(n_embd, std::max(dep_dim, 1))));
     attn_splits_ = attn_splits_for(n_ctx);
     status_ =static_cast<int *>(dalloc(sizeof(int)));
     fin_d_ = static_cast<FrameIn *>(dalloc(sizeof(FrameIn)));
@@ -528,6 +615,27 @@ static FramePhase gemv_op(const GemvArgs &g, int pro, int epi) {
     p.epi = epi;
     p.g = g;
     return p;
+}
+
+// Tensor parallel: the split projection g (whose output rows are partial over
+// the ranks) as a GEMV storing double partials, their sum over the ranks, and
+// y = resid + the sum rounded once.
+void Engine::ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n) const {
+    GemvArgs p = g;
+    p.ypart = tp_part_;
+    v.push_back(gemv_op(p, kProPlain, kEpiPartial));
+    FramePhase ar{};
+    ar.kind = kPhAllReduce;
+    ar.g.ypart = tp_part_;
+    ar.count = n;
+    v.push_back(ar);
+    FramePhase ra{};
+    ra.kind = kPhResidAdd;
+    ra.g.ypart = tp_part_;
+    ra.g.resid = resid;
+    ra.g.y = y;
+    ra.count = n;
+    v.push_back(ra);
 }
 
 // One temporal layer (bmo_compute.cpp:2188-2640): reads resid[l], writes resid[l+1].
@@ -582,7 +690,8 @@ void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     o.x = attn_;
     o.y = xmid_;
     o.resid = x_in;
-    v.push_back(gemv_op(o, kProPlain, kEpiResid));
+    if (tensor_parallel) ops_tp_reduce(v, o, x_in, xmid_, n_embd);
+    else v.push_back(gemv_op(o, kProPlain, kEpiResid));
 
     GemvArgs fi = gemv_base(L_[l].ffn_in);
     fi.x = xmid_;
@@ -595,7 +704,8 @@ void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     fo.x = act_;
     fo.y = x_out;
     fo.resid = xmid_;
-    v.push_back(gemv_op(fo, kProPlain, kEpiResid));
+    if (tensor_parallel) ops_tp_reduce(v, fo, xmid_, x_out, n_embd);
+    else v.push_back(gemv_op(fo, kProPlain, kEpiResid));
 }
 
 // Output norm, text logits and per-tile argmax (the greedy text token).
@@ -636,8 +746,8 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
         a.gamma = D_[i].norm1;
         a.eps = norm_eps;
         a.y = dq_;
-        a.q_dim = dep_dim;
-        a.kv_dim = dep_dim;
+        a.q_dim = dep_heads * dep_hd;  // this rank's heads (all of them without tensor parallelism)
+        a.kv_dim = dep_heads * dep_hd;
         a.head_dim = dep_hd;
         a.rope_cs = nullptr;
         a.k_cache = dk_cache_;
@@ -681,7 +791,8 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
             ap.head_dim = dep_hd;
             ap.splits = 1;
             v.push_back(ap);
-            v.push_back(gemv_op(o, kProPlain, kEpiResid));
+            if (tensor_parallel) ops_tp_reduce(v, o, dxa_, dxb_, dep_dim);
+            else v.push_back(gemv_op(o, kProPlain, kEpiResid));
         }
 
         GemvArgs fi = gemv_base(D_[i].ffn_in[cb]);
@@ -695,7 +806,8 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
         fo.x = dact_;
         fo.y = dxa_;
         fo.resid = dxb_;
-        v.push_back(gemv_op(fo, kProPlain, kEpiResid));
+        if (tensor_parallel) ops_tp_reduce(v, fo, dxb_, dxa_, dep_dim);
+        else v.push_back(gemv_op(fo, kProPlain, kEpiResid));
     }
     GemvArgs h = gemv_base(dep_head_[cb]);
     h.x = dxa_;
@@ -743,6 +855,8 @@ void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
         case kPhTokenOut:
             ck(launch_finalize_token(op.tok.pairs, op.tok.n_pairs, op.tok.tok_out, s, cfg_.pdl), "launch finalize");
             break;
+        case kPhAllReduce: tp_comm_->all_reduce_sum(op.g.ypart, static_cast<size_t>(op.count), s); break;
+        case kPhResidAdd: ck(launch_tp_resid(op.g.ypart, op.g.resid, op.g.y, op.count, s), "launch tp resid"); break;
         default: throw std::runtime_error("internal: unknown op");
         }
     }
@@ -790,7 +904,7 @@ void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &fir
 // programs.  Anything the kernel does not cover keeps the per-op path.
 void Engine::build_programs() {
     persistent_ = false;
-    if (!cfg_.persistent || kv_type != kKvF16) return;
+    if (!cfg_.persistent || kv_type != kKvF16 || tensor_parallel) return;
     frame_grid_ = frame_max_grid();
     if (frame_grid_ <= 0) return;
     if (n_ctx > frame_max_window() || (head_dim != 64 && head_dim != 128) || n_heads > frame_grid_) return;

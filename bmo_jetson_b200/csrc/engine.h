@@ -22,6 +22,7 @@
 
 #include "gguf.h"
 #include "layout.h"
+#include "tp_comm.h"
 
 namespace bmo {
 
@@ -36,6 +37,11 @@ struct EngineConfig {
     bool graphs = true;
     bool pdl = true;
     bool persistent = false;  // run frames as one persistent kernel where the model allows
+    // tensor parallel (batch-1 latency mode): tp_size >= 1 makes this engine
+    // rank tp_rank of tp_size, holding the attention heads and FFN columns of
+    // its shard; tp_id is the group's NCCL unique id
+    int tp_rank = 0, tp_size = 0;
+    unsigned char tp_id[128] = {};
 };
 
 // Per-call inputs, copied to the device in one transfer.
@@ -66,6 +72,9 @@ public:
     int device = 0, sm_count = 148;
     cudaStream_t stream = nullptr;
     size_t device_bytes = 0;
+    // tensor parallel: head, KV-head and FFN counts above are this rank's shard
+    bool tensor_parallel = false;
+    int tp_rank = 0, tp_size = 1;
 
     // ---- synchronous operations (caller serialises) ----
     void run_temporal(const int32_t *tokens, int K, int pos);
@@ -121,6 +130,11 @@ private:
     void alloc_state();
     void *arena(size_t bytes);
     QMatDesc upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t row0, int64_t rows);
+    // rows from several ranges (concatenated) and 32-aligned columns [col0, col0 + ncols)
+    QMatDesc upload_q4_sel(const GgufTensor *t, int perm, int swiglu_f,
+                           const std::vector<std::pair<int64_t, int64_t>> &row_ranges, int64_t col0, int64_t ncols);
+    QMatDesc upload_q4_raw(const std::string &name, const uint8_t *src, int64_t rows, int64_t cols, int perm,
+                           int swiglu_f);
     float *upload_f32(const GgufTensor *t, int64_t n);
     EmbTable upload_table(const GgufTensor *t);
     GemvArgs gemv_base(const QMatDesc &m) const;
@@ -146,6 +160,10 @@ private:
     };
     void build_programs();
     void enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal);
+    // tensor parallel
+    std::unique_ptr<TpComm> tp_comm_;
+    double *tp_part_ = nullptr;  // partial sums of the split projections, summed over the ranks
+    void ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n) const;
     // batched sessions (batch_engine.cpp)
     struct BatchState;
     struct BatchDeleter {

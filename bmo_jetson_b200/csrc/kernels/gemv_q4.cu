@@ -234,7 +234,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_const
             for (int o = 0; o <= l - f; ++o) v += __ldcg(gp + o * 32 + lane);
             if (lane == 0) a.gcount[t] = 0;
         }
-        tile_epilogue<EPI>(a, t, lane, __double2float_rn(v), tok, a.rope_cs);
+        if constexpr (EPI == kEpiPartial) {
+            const int r = t * kTileRows + lane;
+            if (r < a.W.rows) a.ypart[r] = v;  // rounded once, after the sum over ranks
+        } else {
+            tile_epilogue<EPI>(a, t, lane, __double2float_rn(v), tok, a.rope_cs);
+        }
     }
 }
 
@@ -284,7 +289,8 @@ static cudaError_t configure_one() {
     X(kProPlain, kEpiStore)   \
     X(kProNorm, kEpiStore)    \
     X(kProPlain, kEpiSwiGLU)  \
-    X(kProNorm, kEpiResid)
+    X(kProNorm, kEpiResid)    \
+    X(kProPlain, kEpiPartial)
 
 cudaError_t configure_gemv() {
     cudaError_t e = cudaSuccess;

@@ -120,6 +120,19 @@ __global__ void finalize_token_kernel(const float2 *pairs, int n, int *out) {
     }
 }
 
+// Tensor-parallel residual add: y = resid + fl(sum of the ranks' double
+// partials), the single rounding of the batch-1 GEMV's residual epilogue.
+__global__ void tp_resid_kernel(const double *part, const float *resid, float *y, int n) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fadd_rn(resid[i], __double2float_rn(part[i]));
+}
+
+cudaError_t launch_tp_resid(const double *part, const float *resid, float *y, int n, cudaStream_t s) {
+    tp_resid_kernel<<<(n + 255) / 256, 256, 0, s>>>(part, resid, y, n);
+    return cudaGetLastError();
+}
+
 cudaError_t configure_gemv();
 cudaError_t configure_attention();
 cudaError_t configure_batch();

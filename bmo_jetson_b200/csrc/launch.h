@@ -83,6 +83,9 @@ cudaError_t launch_batch_set_inputs(BatchIn *in, const int *sess, const int *tok
 cudaError_t launch_batch_finalize(const float2 *pairs, int pairs_stride, int n_pairs, int *out, int out_stride,
                                   int n_sess, cudaStream_t s);
 
+// Tensor parallel: y = resid + (float)part (kernels/misc.cu).
+cudaError_t launch_tp_resid(const double *part, const float *resid, float *y, int n, cudaStream_t s);
+
 // Frame-start embedding sum + RoPE table (kernels/misc.cu).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,
                          float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, cudaStream_t s);

@@ -41,6 +41,7 @@ enum Epilogue : int {
     kEpiQKV = 3,     // RoPE on q/k, append k/v into the ring cache, q out
     kEpiLogits = 4,  // logits (+ bias) and per-tile (max, argmax)
     kEpiEmbAdd = 5,  // y = acc + embedding row of a token
+    kEpiPartial = 6, // ypart = acc in double, unrounded (tensor-parallel partial sums)
 };
 
 enum KvType : int { kKvF16 = 0, kKvQ4_0 = 1 };
@@ -121,6 +122,8 @@ struct GemvArgs {
     // embedding-add epilogue
     EmbTable emb;
     TokenSrc tok;
+    // partial-sum epilogue: [rows] doubles
+    double *ypart;
     // kProDepAttn prologue: the decode attention whose output is the activation
     AttnArgs att;
     // work split: tile_aligned = 1 gives every CTA whole row tiles (no
@@ -140,6 +143,8 @@ enum PhaseKind : int {
     kPhGemv = 0,      // g with prologue `pro`, epilogue `epi`
     kPhAttn = 1,      // decode attention `at` (head_dim, `splits` CTAs per head in the per-op path)
     kPhTokenOut = 2,  // CTA 0 writes the first maximum over tok.pairs into tok.tok_out
+    kPhAllReduce = 3, // tensor parallel: sum g.ypart[0..count) over the ranks (double, in place)
+    kPhResidAdd = 4,  // tensor parallel: g.y[i] = g.resid[i] + (float)g.ypart[i], i < count
 };
 
 struct FramePhase {
@@ -150,6 +155,7 @@ struct FramePhase {
     GemvArgs g;
     AttnArgs at;   // kPhAttn, and the attention of a kProDepAttn prologue
     TokenSrc tok;  // kPhTokenOut
+    int count;     // kPhAllReduce, kPhResidAdd
 };
 
 // ---- batched sessions (config 4) ----

@@ -86,6 +86,14 @@ def lib() -> ctypes.CDLL:
     L.bmo_enqueue_cascade.restype = i
     L.bmo_enqueue_frame.argtypes = [vp, vp, i, i, vp]
     L.bmo_enqueue_frame.restype = i
+    L.bmo_tp_unique_id.argtypes = [vp]
+    L.bmo_tp_unique_id.restype = i
+    L.bmo_init_tp.argtypes = [ctypes.c_char_p, i, i, i, i, i, i, vp]
+    L.bmo_init_tp.restype = vp
+    L.bmo_get_tp_size.argtypes = [vp]
+    L.bmo_get_tp_size.restype = i
+    L.bmo_get_tp_rank.argtypes = [vp]
+    L.bmo_get_tp_rank.restype = i
     L.bmo_batch_init.argtypes = [vp, i]
     L.bmo_batch_init.restype = i
     L.bmo_batch_sessions.argtypes = [vp]
@@ -128,6 +136,15 @@ def lib() -> ctypes.CDLL:
     return L
 
 
+def tp_unique_id() -> bytes:
+    """A fresh tensor-parallel group id (NCCL unique id, 128 bytes)."""
+    buf = ctypes.create_string_buffer(128)
+    rc = lib().bmo_tp_unique_id(buf)
+    if rc != 0:
+        raise RuntimeError(f"bmo_tp_unique_id rc={rc}")
+    return buf.raw
+
+
 def _err(h) -> str:
     e = lib().bmo_last_error(h)
     return e.decode() if e else "unknown"
@@ -136,9 +153,19 @@ def _err(h) -> str:
 class BMOEngine:
     """Handle on one model in one GPU's HBM (reference bmo_engine.py:112-285)."""
 
-    def __init__(self, gguf_path: str, n_ctx: int = 1024, device: int = -1, kv_type: int = -1, flags: int = 0):
+    def __init__(self, gguf_path: str, n_ctx: int = 1024, device: int = -1, kv_type: int = -1, flags: int = 0,
+                 tp=None):
+        """tp = (rank, size, group_id): rank of a tensor-parallel group (bmo_init_tp);
+        group_id is the 128-byte tp_unique_id() of one rank, shared by all."""
         L = lib()
-        if device < 0 and kv_type < 0 and flags == 0:
+        if tp is not None:
+            rank, size, gid = tp
+            gid = bytes(gid)
+            if len(gid) != 128:
+                raise ValueError("tensor-parallel group id must be 128 bytes")
+            self._h = L.bmo_init_tp(gguf_path.encode("utf-8"), n_ctx, device, kv_type, flags, int(rank), int(size),
+                                    ctypes.c_char_p(gid))
+        elif device < 0 and kv_type < 0 and flags == 0:
             self._h = L.bmo_init(gguf_path.encode("utf-8"), n_ctx)
         else:
             self._h = L.bmo_init_ex(gguf_path.encode("utf-8"), n_ctx, device, kv_type, flags)
@@ -160,6 +187,9 @@ class BMOEngine:
         self._buf_text = np.empty(max(self.text_vocab, 1), dtype=np.float32)
         self._buf_audio = np.empty(max(self.audio_vocab, 1), dtype=np.float32)
         self._buf_depth_audio = np.empty(max(self.dep_q, 8), dtype=np.int32)
+
+        self.tp_size = L.bmo_get_tp_size(self._h) or 1
+        self.tp_rank = L.bmo_get_tp_rank(self._h)
 
     # ---- reference methods -------------------------------------------------
     def reset(self) -> None:

@@ -87,6 +87,26 @@ BMO_API int bmo_enqueue_frame(bmo_handle_t *h, const int32_t *tokens_dev, int nu
 BMO_API int bmo_enqueue_temporal(bmo_handle_t *h, const int32_t *tokens_dev, int num_codebooks, int pos);
 BMO_API int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token);
 
+/* ---- tensor parallel (batch-1 latency mode) ---------------------------------
+ * tp_size processes, one per GPU, each open a handle with bmo_init_tp on the
+ * same GGUF and the same group id (from bmo_tp_unique_id on one process,
+ * passed to the others).  Rank r holds attention heads [r H/T, (r+1) H/T),
+ * their KV ring and O-projection columns, and FFN columns [r F/T, (r+1) F/T)
+ * of every temporal and depformer layer; embeddings, norms and heads are
+ * replicated.  After the O-projection and the FFN-out of every layer the
+ * ranks sum their partial outputs in double over NCCL (in the frame's CUDA
+ * graph) and round once, so every rank holds the same hidden state and the
+ * tokens equal the single-GPU handle's.  Every rank must make the same calls
+ * in the same order.  The handle's geometry getters report its shard's head
+ * and FFN counts; bmo_kv_import_f32 takes the shard's KV heads.  Needs H, the
+ * KV heads, the depformer heads and both FFN widths to split into
+ * 32-column shards.  Returns NULL (reason on stderr) on failure. */
+BMO_API int bmo_tp_unique_id(void *out_id /* 128 bytes */);
+BMO_API bmo_handle_t *bmo_init_tp(const char *gguf_path, int n_ctx, int device, int kv_type, int flags, int tp_rank,
+                                  int tp_size, const void *tp_id);
+BMO_API int bmo_get_tp_size(bmo_handle_t *h);
+BMO_API int bmo_get_tp_rank(bmo_handle_t *h);
+
 /* ---- batched sessions ----------------------------------------------------
  * Up to 64 independent sessions share the handle's weights; each has its own
  * temporal ring (n_ctx slots, the handle's KV format).  One batched frame
