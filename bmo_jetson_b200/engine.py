@@ -136,8 +136,26 @@ def lib() -> ctypes.CDLL:
     return L
 
 
+def _preload_nccl() -> None:
+    """libbmo resolves NCCL (libnccl.so.2) at run time and reuses a copy the
+    process already loaded.  Load the NCCL that this Python environment ships
+    (the one PyTorch links) first, so that a later `import torch` finds the
+    NCCL it was built against instead of an older system copy."""
+    import importlib.util
+    import sys
+    if "torch" in sys.modules:
+        return  # torch has loaded its NCCL already
+    spec = importlib.util.find_spec("nvidia.nccl")
+    for base in (list(spec.submodule_search_locations) if spec and spec.submodule_search_locations else []):
+        cand = os.path.join(base, "lib", "libnccl.so.2")
+        if os.path.isfile(cand):
+            ctypes.CDLL(cand, mode=ctypes.RTLD_GLOBAL)
+            return
+
+
 def tp_unique_id() -> bytes:
     """A fresh tensor-parallel group id (NCCL unique id, 128 bytes)."""
+    _preload_nccl()
     buf = ctypes.create_string_buffer(128)
     rc = lib().bmo_tp_unique_id(buf)
     if rc != 0:
@@ -159,6 +177,7 @@ class BMOEngine:
         group_id is the 128-byte tp_unique_id() of one rank, shared by all."""
         L = lib()
         if tp is not None:
+            _preload_nccl()
             rank, size, gid = tp
             gid = bytes(gid)
             if len(gid) != 128:
