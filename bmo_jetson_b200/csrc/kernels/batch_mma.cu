@@ -188,6 +188,40 @@ __device__ __forceinline__ int cta_of(long long u, long long U, int G) {
 // ---------------------------------------------------------------------------
 // per (row, session) epilogue; lane = row of tile t, all lanes take part
 // ---------------------------------------------------------------------------
+// QKV rows with the session's position and ring already in hand.
+__device__ __forceinline__ void mma_qkv_row(const BatchGemmArgs &a, int t, int lane, int s, float v, int pos, int ring,
+                                            float2 cs) {
+    const int r = t * kTileRows + lane;
+    const int hd = a.head_dim;
+    float out = v;
+    const bool is_q = r < a.q_dim;
+    const bool is_k = !is_q && r < a.q_dim + a.kv_dim;
+    if ((is_q || is_k) && a.rope) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+        out = (lane & 1) ? __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x))
+                         : __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
+    }
+    const long long ys = static_cast<long long>(s) * a.y_stride;
+    if (is_q) {
+        a.y[ys + r] = out;
+        return;
+    }
+    const int rr = is_k ? r - a.q_dim : r - a.q_dim - a.kv_dim;
+    if (!is_k && a.v_out) a.v_out[static_cast<long long>(s) * a.v_out_stride + rr] = v;
+    const int kh = rr / hd, d = rr % hd;
+    const int slot = pos % a.n_ctx;
+    const long long e = static_cast<long long>(ring) * a.kv_sess_stride + a.kv_layer_off +
+                        (static_cast<long long>(kh) * a.n_ctx + slot) * hd + d;
+    void *cache = is_k ? a.k_cache : a.v_cache;
+    if (a.kv_type == kKvF16) {
+        static_cast<__half *>(cache)[e] = __float2half_rn(out);
+    } else {
+        const long long e0 = e - lane;
+        warp_store_q4_0(out, lane, static_cast<uint8_t *>(cache) + e0 / 2,
+                        reinterpret_cast<__half *>(is_k ? a.k_scale : a.v_scale) + e0 / 32);
+    }
+}
+
 template <int EPI>
 __device__ __forceinline__ void mma_row_epilogue(const BatchGemmArgs &a, int t, int lane, int s, float v) {
     const int r = t * kTileRows + lane;
@@ -258,15 +292,62 @@ __device__ __forceinline__ void mma_row_epilogue(const BatchGemmArgs &a, int t, 
     }
 }
 
-// The 32 sessions [32h, 32h + 32) of tile t, one row per lane.
+// The 32 sessions [32h, 32h + 32) of tile t, one row per lane.  Every
+// per-session operand (residual, token, position, ring, RoPE pair) is loaded
+// for all 32 sessions before the first store, so the loads overlap instead of
+// queueing behind stores they might alias.
 template <int EPI>
 __device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t, int lane, int h, const float2 (&v)[16]) {
     if (t >= a.W.n_tiles) return;
+    const int r = t * kTileRows + lane;
+    const int ns = a.n_sess - 32 * h;  // sessions of this warp (may exceed 32)
+    float op[32];                      // per-session operand of this lane's row
+    int tok = 0, pos = 0, ring = 0;    // lane i: session 32h + i
+    const int sl = 32 * h + lane;
+    if constexpr (EPI == kEpiResid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            op[j] = (j < ns && r < a.W.rows) ? __ldcg(a.resid + static_cast<long long>(32 * h + j) * a.resid_stride + r) : 0.0f;
+    } else if constexpr (EPI == kEpiEmbAdd) {
+        tok = sl < a.n_sess ? __ldcg(a.tok + sl) : -1;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int tj = __shfl_sync(0xffffffffu, tok, j);
+            const bool ok = j < ns && r < a.W.rows && tj >= 0 && tj < a.emb.rows && a.emb.dim == a.W.rows;
+            op[j] = ok ? emb_elem(a.emb, tj, r) : 0.0f;
+        }
+    }
+    float2 rp[32];  // QKV: the (cos, sin) pair of this row's RoPE frequency per session
+    if constexpr (EPI == kEpiQKV) {
+        if (sl < a.n_sess) {
+            pos = __ldcg(a.pos + sl * a.pos_stride);
+            ring = a.ring_of ? __ldcg(a.ring_of + sl) : sl;
+        }
+        const bool rot = r < a.q_dim + a.kv_dim && a.rope;
+        const int d = (r < a.q_dim ? r : r - a.q_dim) % a.head_dim;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            rp[j] = (rot && j < ns) ? __ldcg(a.rope + static_cast<long long>(32 * h + j) * (a.head_dim / 2) + (d >> 1))
+                                    : make_float2(1.0f, 0.0f);
+    }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        const int s = 32 * h + 2 * j;
-        if (s < a.n_sess) mma_row_epilogue<EPI>(a, t, lane, s, v[j].x);
-        if (s + 1 < a.n_sess) mma_row_epilogue<EPI>(a, t, lane, s + 1, v[j].y);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int jj = 2 * j + e, s = 32 * h + jj;
+            if (s >= a.n_sess) continue;
+            const float val = e ? v[j].y : v[j].x;
+            if constexpr (EPI == kEpiResid) {
+                if (r < a.W.rows) a.y[static_cast<long long>(s) * a.y_stride + r] = __fadd_rn(op[jj], val);
+            } else if constexpr (EPI == kEpiEmbAdd) {
+                if (r < a.W.rows) a.y[static_cast<long long>(s) * a.y_stride + r] = __fadd_rn(val, op[jj]);
+            } else if constexpr (EPI == kEpiQKV) {
+                mma_qkv_row(a, t, lane, s, val, __shfl_sync(0xffffffffu, pos, jj), __shfl_sync(0xffffffffu, ring, jj),
+                            rp[jj]);
+            } else {
+                mma_row_epilogue<EPI>(a, t, lane, s, val);
+            }
+        }
     }
 }
 
@@ -545,27 +626,34 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 if (S.last) {
                     // partials added in contributor order: the result does not depend on timing
                     const double *base = reinterpret_cast<const double *>(a.ws) + static_cast<size_t>(st) * a.max_contrib * slab;
+                    // contributor by contributor, all of a contributor's loads in flight together
+                    const size_t r0 = static_cast<size_t>(32 * h) * kMmaRows + 32 * q + lane;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        if (32 * h + 2 * j < P) {
-                            const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
-                            if constexpr (EXACT) {
-                                double x = 0.0, y = 0.0;
-                                for (int k = 0; k < n_c; ++k) {
-                                    x += __ldcg(base + k * slab + i0);
-                                    y += __ldcg(base + k * slab + i0 + kMmaRows);
-                                }
-                                Sacc[j] = make_float2(__double2float_rn(x), __double2float_rn(y));
-                            } else {
-                                float x = 0.0f, y = 0.0f;
-                                for (int k = 0; k < n_c; ++k) {
-                                    const float *pk = reinterpret_cast<const float *>(base + k * slab);
-                                    x = __fadd_rn(x, __ldcg(pk + i0));
-                                    y = __fadd_rn(y, __ldcg(pk + i0 + kMmaRows));
-                                }
-                                Sacc[j] = make_float2(x, y);
-                            }
+                    for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+                    for (int k = 0; k < n_c; ++k) {
+                        const double *pk = base + k * slab + r0;
+                        if constexpr (EXACT) {
+                            double v[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = 32 * h + j < P ? __ldcg(pk + j * kMmaRows) : 0.0;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) Dacc[j] += v[j];
+                        } else {
+                            const float *pf = reinterpret_cast<const float *>(base + k * slab) + r0;
+                            float v[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = 32 * h + j < P ? __ldcg(pf + j * kMmaRows) : 0.0f;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                Sacc[j] = make_float2(__fadd_rn(Sacc[j].x, v[2 * j]), __fadd_rn(Sacc[j].y, v[2 * j + 1]));
                         }
+                    }
+                    if constexpr (EXACT) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j]), __double2float_rn(Dacc[2 * j + 1]));
                     }
                     mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
                 }
