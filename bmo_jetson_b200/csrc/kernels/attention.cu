@@ -55,6 +55,12 @@ struct AttnSmem {
     double l_warp;
     double o_rank[kAttnMaxSplits][HD];   // rank 0: every split's partial output (pushed)
     double l_rank[kAttnMaxSplits];
+    // Q4_0 rings: (n - 8) as doubles, and per staged row the block scales (pass 1)
+    // or p times the block scales (pass 2) as doubles -- every K/V element then
+    // enters the double sums through one fma with no per-element conversion
+    double tbl[16];
+    double kdd[Q4 ? kAttnSub : 1][kScales];
+    double pd[Q4 ? kAttnSub : 1][kScales];
 };
 
 template <int HD, bool Q4>
@@ -141,6 +147,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
         mbar_init(&S.vbar, 1);
         fence_barrier_init();
     }
+    if (Q4 && tid < 16) S.tbl[tid] = static_cast<double>(tid - 8);
     __syncthreads();
     // Every CTA of the cluster must be running before any writes into its
     // shared memory: arrive now, wait just before the first remote store.
@@ -187,6 +194,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
         ok &= mbar_wait(&S.kbar, kphase);
         kphase ^= 1u;
         __syncthreads();
+        if constexpr (Q4) {
+            for (int e = tid; e < nj * kSc; e += kAttnThreads)
+                S.kdd[e / kSc][e % kSc] = static_cast<double>(__half2float(S.kd[e / kSc][e % kSc]));
+            __syncthreads();
+        }
         for (int jb = warp * kAttnPosPerWarp; jb < nj; jb += kAttnThreads / 32 * kAttnPosPerWarp) {
             double dot[kAttnPosPerWarp];
 #pragma unroll
@@ -194,9 +206,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
                 const int j = min(jb + u, nj - 1);
                 dot[u] = 0.0;
 #pragma unroll
-                for (int i = 0; i < HD / 32; ++i)
-                    dot[u] = fma(static_cast<double>(qr[i]),
-                                 static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], lane + 32 * i)), dot[u]);
+                for (int i = 0; i < HD / 32; ++i) {
+                    if constexpr (Q4) {
+                        // element lane + 32i is in block i: q * d exact in double, times (n - 8) exact
+                        const uint8_t byte = S.k[j][i * 16 + (lane & 15)];
+                        const int nib = lane < 16 ? (byte & 0x0F) : (byte >> 4);
+                        dot[u] = fma(static_cast<double>(qr[i]) * S.kdd[j][i], S.tbl[nib], dot[u]);
+                    } else {
+                        dot[u] = fma(static_cast<double>(qr[i]),
+                                     static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], lane + 32 * i)), dot[u]);
+                    }
+                }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1)
@@ -247,15 +267,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
         ok &= mbar_wait(&S.vbar, vphase);
         vphase ^= 1u;
         __syncthreads();
-        auto pv = [&](int j) {
-            return static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], dim));
+        if constexpr (Q4) {
+            // p times the block scale, exact in double (fp32 x fp16)
+            for (int e = tid; e < nj * kSc; e += kAttnThreads)
+                S.pd[e / kSc][e % kSc] = static_cast<double>(S.s[j0 + e / kSc]) *
+                                         static_cast<double>(__half2float(S.vd[e / kSc][e % kSc]));
+            __syncthreads();
+        }
+        // one weighted term: p v in double, v = (n - 8) d exact
+        auto term = [&](int j, double o) {
+            if constexpr (Q4) {
+                const uint8_t byte = S.v[j][(dim >> 5) * 16 + (dim & 15)];
+                const int nib = (dim & 31) < 16 ? (byte & 0x0F) : (byte >> 4);
+                return fma(S.pd[j][dim >> 5], S.tbl[nib], o);
+            } else {
+                return fma(static_cast<double>(S.s[j0 + j]), static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], dim)), o);
+            }
         };
         int j = grp;
         for (; j + 3 * kG < nj; j += 4 * kG) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) o4[u] = fma(static_cast<double>(S.s[j0 + j + u * kG]), pv(j + u * kG), o4[u]);
+            for (int u = 0; u < 4; ++u) o4[u] = term(j + u * kG, o4[u]);
         }
-        for (; j < nj; j += kG) o4[0] = fma(static_cast<double>(S.s[j0 + j]), pv(j), o4[0]);
+        for (; j < nj; j += kG) o4[0] = term(j, o4[0]);
         if (warp == kAttnWarps - 1)
             for (int j = lane; j < nj; j += 32) l += static_cast<double>(S.s[j0 + j]);
         __syncthreads();

@@ -354,15 +354,21 @@ __device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// fp32 -> fp64 from the bit pattern: sign, exponent rebiased by 1023 - 127,
-// mantissa shifted to the top of the 52-bit field.  Exact for normal floats
-// and zero; a subnormal float (|x| < 2^-126, never a decode term) comes out
-// within 2^-126 of its value.
-__device__ __forceinline__ double f2d_bits(float x) {
-    const unsigned f = __float_as_uint(x), mag = f & 0x7FFFFFFFu, sign = f & 0x80000000u;
-    const unsigned hi = mag ? (((mag >> 3) + 0x38000000u) | sign) : sign;
-    return __hiloint2double(static_cast<int>(hi), static_cast<int>(f << 29));
+// fp32 -> fp64 times 2^-896, from the bit pattern alone: the sign stays in
+// bit 63, the 8-bit exponent lands in the low bits of the 11-bit field and the
+// mantissa at the top of the 52-bit field, so the double's value is exactly
+// x * 2^(127 - 1023) for every finite x -- zero and subnormal floats included
+// (a subnormal float becomes a subnormal double).  Sums of these scaled terms
+// round exactly like the unscaled double sums: every fp32 value is a multiple
+// of 2^-149, so scaled partial sums below the double normal range are multiples
+// of 2^-1045 and add exactly, and above it double addition commutes with the
+// power-of-two scale.  kUnscale restores the value before the fp32 rounding.
+__device__ __forceinline__ double f2d_scaled(float x) {
+    const int f = __float_as_int(x);
+    const unsigned hi = static_cast<unsigned>(f >> 3) & 0x8FFFFFFFu;  // sign, then exponent and mantissa bits 30..3
+    return __hiloint2double(static_cast<int>(hi), f << 29);
 }
+constexpr double kUnscale = 0x1p896;
 
 // Terms of one 8-session register buffer r (r[2i] low-half sum, r[2i + 1]
 // high-half sum of session i) into the accumulators of pairs [4k, 4k + 4).
@@ -384,10 +390,10 @@ __device__ __forceinline__ void mma_terms(const uint32_t (&r)[16], const float4 
                                            __int_as_float(static_cast<int>(r[4 * jj + 3]) + 0x4B400000));
             const float2 tl = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(flo, d8, nm), m4));
             const float2 th = __fmul2_rn(d44, __fadd2_rn(__ffma2_rn(fhi, d8, nm), m4));
-            D[2 * J] += f2d_bits(tl.x);
-            D[2 * J + 1] += f2d_bits(tl.y);
-            D[2 * J] += f2d_bits(th.x);
-            D[2 * J + 1] += f2d_bits(th.y);
+            D[2 * J] += f2d_scaled(tl.x);
+            D[2 * J + 1] += f2d_scaled(tl.y);
+            D[2 * J] += f2d_scaled(th.x);
+            D[2 * J + 1] += f2d_scaled(th.y);
         } else {
             const float2 f = make_float2(
                 __int_as_float(static_cast<int>(r[4 * jj] + r[4 * jj + 1]) + 0x4B400000),
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
         const int q = warp & 3, h = warp >> 2;
         const bool active = h < groups;
         float2 Sacc[16];  // fast: fp32 sums of session pairs
-        double Dacc[32];  // exact: double sums of each session
+        double Dacc[32];  // exact: double sums of each session, scaled by 2^-896
 #pragma unroll
         for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
 #pragma unroll
@@ -591,7 +597,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 if constexpr (EXACT) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j]), __double2float_rn(Dacc[2 * j + 1]));
+                        Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j] * kUnscale),
+                                           __double2float_rn(Dacc[2 * j + 1] * kUnscale));
                 }
                 mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
             } else {
@@ -653,7 +660,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                     if constexpr (EXACT) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j)
-                            Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j]), __double2float_rn(Dacc[2 * j + 1]));
+                            Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j] * kUnscale),
+                                           __double2float_rn(Dacc[2 * j + 1] * kUnscale));
                     }
                     mma_block_epilogue<EPI>(a, t, lane, h, Sacc);
                 }
