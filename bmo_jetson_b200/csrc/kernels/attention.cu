@@ -41,7 +41,9 @@ template <int HD, bool Q4>
 struct AttnSmem {
     static constexpr int kRowBytes = Q4 ? HD / 2 : HD * 2;
     static constexpr int kScales = Q4 ? HD / 32 : 1;
-    static constexpr int kGroups = kAttnThreads / HD;  // position groups of the weighted sum
+    // position groups of the weighted sum: fp16 rows one dimension per thread,
+    // Q4_0 rows one 32-bit word (8 dimensions) per thread
+    static constexpr int kGroups = Q4 ? kAttnThreads / (HD / 8) : kAttnThreads / HD;
     uint64_t kbar, vbar;
     alignas(128) uint8_t k[kAttnSub][kRowBytes];
     alignas(128) uint8_t v[kAttnSub][kRowBytes];
@@ -57,8 +59,9 @@ struct AttnSmem {
     double l_rank[kAttnMaxSplits];
     // Q4_0 rings: (n - 8) as doubles, and per staged row the block scales (pass 1)
     // or p times the block scales (pass 2) as doubles -- every K/V element then
-    // enters the double sums through one fma with no per-element conversion
-    double tbl[16];
+    // enters the double sums through one table read and one fma, with no
+    // per-element conversion
+    alignas(128) double tbl[16];
     double kdd[Q4 ? kAttnSub : 1][kScales];
     double pd[Q4 ? kAttnSub : 1][kScales];
 };
@@ -72,6 +75,14 @@ __device__ __forceinline__ float kv_elem(const uint8_t *row, const __half *sc, i
     } else {
         return __half2float(reinterpret_cast<const __half *>(row)[d]);
     }
+}
+
+// (n - 8) as a double for the Q4_0 nibble at bit SH of x, read from the
+// 16-entry table: the nibble shifted to a byte offset (n * 8) in one step.
+template <int SH>
+__device__ __forceinline__ double nib_val(const double *tbl, uint32_t x) {
+    const uint32_t off = SH >= 3 ? (x >> (SH - 3)) & 0x78u : (x << (3 - SH)) & 0x78u;
+    return *reinterpret_cast<const double *>(reinterpret_cast<const char *>(tbl) + off);
 }
 
 template <int HD, bool Q4>
@@ -183,6 +194,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     float qr[HD / 32];
 #pragma unroll
     for (int i = 0; i < HD / 32; ++i) qr[i] = S.q[lane + 32 * i];
+    // Q4_0: kLP lanes per position, lane pb holding q's block pb as doubles
+    constexpr int kLP = HD / 32, kPP = 32 / kLP;
+    const int pb = lane % kLP, pl = lane / kLP;
+    double qd[Q4 ? 32 : 1];
+    if constexpr (Q4) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) qd[i] = static_cast<double>(S.q[32 * pb + i]);
+    }
 
     // ---- pass 1: scores of this split, kAttnPosPerWarp positions per warp at a time ----
     for (int sub = 0; sub < nsub; ++sub) {
@@ -199,6 +218,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
                 S.kdd[e / kSc][e % kSc] = static_cast<double>(__half2float(S.kd[e / kSc][e % kSc]));
             __syncthreads();
         }
+        if constexpr (Q4) {
+            // kPP positions per warp step; per lane the 32 products of one block,
+            // sum_i q_i (n_i - 8) in double, times the block scale, then the
+            // kLP blocks of the position added across lanes
+            for (int jb = warp * kPP; jb < nj; jb += kAttnWarps * kPP) {
+                const int j = jb + pl;
+                double dot = 0.0;
+                if (j < nj) {
+                    const uint4 x = *reinterpret_cast<const uint4 *>(&S.k[j][16 * pb]);
+                    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+                    double c[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        // byte 4w + k: element 4w + k (low nibble), 4w + k + 16 (high nibble)
+                        c[0] = fma(qd[4 * w + 0], nib_val<0>(S.tbl, xw[w]), c[0]);
+                        c[1] = fma(qd[4 * w + 1], nib_val<8>(S.tbl, xw[w]), c[1]);
+                        c[2] = fma(qd[4 * w + 2], nib_val<16>(S.tbl, xw[w]), c[2]);
+                        c[3] = fma(qd[4 * w + 3], nib_val<24>(S.tbl, xw[w]), c[3]);
+                        c[0] = fma(qd[16 + 4 * w + 0], nib_val<4>(S.tbl, xw[w]), c[0]);
+                        c[1] = fma(qd[16 + 4 * w + 1], nib_val<12>(S.tbl, xw[w]), c[1]);
+                        c[2] = fma(qd[16 + 4 * w + 2], nib_val<20>(S.tbl, xw[w]), c[2]);
+                        c[3] = fma(qd[16 + 4 * w + 3], nib_val<28>(S.tbl, xw[w]), c[3]);
+                    }
+                    dot = ((c[0] + c[1]) + (c[2] + c[3])) * S.kdd[j][pb];
+                }
+#pragma unroll
+                for (int o = 1; o < kLP; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                if (pb == 0 && j < nj) S.s[j0 + j] = __fmul_rn(__double2float_rn(dot), a.scale);
+            }
+            __syncthreads();
+            continue;
+        }
         for (int jb = warp * kAttnPosPerWarp; jb < nj; jb += kAttnThreads / 32 * kAttnPosPerWarp) {
             double dot[kAttnPosPerWarp];
 #pragma unroll
@@ -206,17 +257,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
                 const int j = min(jb + u, nj - 1);
                 dot[u] = 0.0;
 #pragma unroll
-                for (int i = 0; i < HD / 32; ++i) {
-                    if constexpr (Q4) {
-                        // element lane + 32i is in block i: q * d exact in double, times (n - 8) exact
-                        const uint8_t byte = S.k[j][i * 16 + (lane & 15)];
-                        const int nib = lane < 16 ? (byte & 0x0F) : (byte >> 4);
-                        dot[u] = fma(static_cast<double>(qr[i]) * S.kdd[j][i], S.tbl[nib], dot[u]);
-                    } else {
-                        dot[u] = fma(static_cast<double>(qr[i]),
-                                     static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], lane + 32 * i)), dot[u]);
-                    }
-                }
+                for (int i = 0; i < HD / 32; ++i)
+                    dot[u] = fma(static_cast<double>(qr[i]),
+                                 static_cast<double>(kv_elem<HD, Q4>(S.k[j], S.kd[j], lane + 32 * i)), dot[u]);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1)
@@ -257,6 +300,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
     constexpr int kG = Smem::kGroups;
     const int dim = tid % HD, grp = tid / HD;
     double o4[4] = {0.0, 0.0, 0.0, 0.0};
+    // Q4_0: thread = (32-bit word wd of the row, position group g2); the word
+    // holds dimensions 32 b2 + 4 (wd % 4) + k (low nibbles) and + 16 (high)
+    constexpr int kWPR = HD / 8;
+    const int wd = tid % kWPR, g2 = tid / kWPR, b2 = wd / 4;
+    double o8[Q4 ? 8 : 1];
+#pragma unroll
+    for (int k = 0; k < (Q4 ? 8 : 1); ++k) o8[k] = 0.0;
     double l = 0.0;
     for (int sub = 0; sub < nsub; ++sub) {
         const int j0 = sub * kAttnSub, nj = min(kAttnSub, n - j0);
@@ -274,27 +324,46 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __grid_constan
                                          static_cast<double>(__half2float(S.vd[e / kSc][e % kSc]));
             __syncthreads();
         }
-        // one weighted term: p v in double, v = (n - 8) d exact
-        auto term = [&](int j, double o) {
-            if constexpr (Q4) {
-                const uint8_t byte = S.v[j][(dim >> 5) * 16 + (dim & 15)];
-                const int nib = (dim & 31) < 16 ? (byte & 0x0F) : (byte >> 4);
-                return fma(S.pd[j][dim >> 5], S.tbl[nib], o);
-            } else {
-                return fma(static_cast<double>(S.s[j0 + j]), static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], dim)), o);
+        if constexpr (Q4) {
+            // p v = (p d) (n - 8), both factors exact in double
+            for (int j = g2; j < nj; j += kG) {
+                const uint32_t x = reinterpret_cast<const uint32_t *>(S.v[j])[wd];
+                const double pdj = S.pd[j][b2];
+                o8[0] = fma(pdj, nib_val<0>(S.tbl, x), o8[0]);
+                o8[1] = fma(pdj, nib_val<8>(S.tbl, x), o8[1]);
+                o8[2] = fma(pdj, nib_val<16>(S.tbl, x), o8[2]);
+                o8[3] = fma(pdj, nib_val<24>(S.tbl, x), o8[3]);
+                o8[4] = fma(pdj, nib_val<4>(S.tbl, x), o8[4]);
+                o8[5] = fma(pdj, nib_val<12>(S.tbl, x), o8[5]);
+                o8[6] = fma(pdj, nib_val<20>(S.tbl, x), o8[6]);
+                o8[7] = fma(pdj, nib_val<28>(S.tbl, x), o8[7]);
             }
-        };
-        int j = grp;
-        for (; j + 3 * kG < nj; j += 4 * kG) {
+        } else {
+            // one weighted term: p v in double
+            auto term = [&](int j, double o) {
+                return fma(static_cast<double>(S.s[j0 + j]), static_cast<double>(kv_elem<HD, Q4>(S.v[j], S.vd[j], dim)), o);
+            };
+            int j = grp;
+            for (; j + 3 * kG < nj; j += 4 * kG) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) o4[u] = term(j + u * kG, o4[u]);
+                for (int u = 0; u < 4; ++u) o4[u] = term(j + u * kG, o4[u]);
+            }
+            for (; j < nj; j += kG) o4[0] = term(j, o4[0]);
         }
-        for (; j < nj; j += kG) o4[0] = term(j, o4[0]);
         if (warp == kAttnWarps - 1)
             for (int j = lane; j < nj; j += 32) l += static_cast<double>(S.s[j0 + j]);
         __syncthreads();
     }
-    S.o_grp[grp][dim] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    if constexpr (Q4) {
+        const int d0 = 32 * b2 + 4 * (wd % 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            S.o_grp[g2][d0 + k] = o8[k];
+            S.o_grp[g2][d0 + 16 + k] = o8[4 + k];
+        }
+    } else {
+        S.o_grp[grp][dim] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    }
     if (warp == kAttnWarps - 1) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);

@@ -24,17 +24,18 @@
 //   !EXACT: one full-block term d4 (sumi d8 - 8 s8) per block, summed in
 //          fp32 (fp32-accurate, not reproducible bit for bit).
 //
-// CTA (one per SM, 12 warps; registers moved from the third warpgroup to the
-// two epilogue warpgroups with setmaxnreg):
-//   warp 9       TMEM owner; lane 0 the bulk-copy producer (per 8-block chunk
+// CTA (one per SM, 20 warps; registers moved from the fifth warpgroup to the
+// four epilogue warpgroups with setmaxnreg):
+//   warp 17      TMEM owner; lane 0 the bulk-copy producer (per 8-block chunk
 //                the four 32-row tiles' Q4_0 chunks of a 128-row block, 4 x
 //                4608 B from HBM, the sessions' split Q8_1 codes, 512 P B, and
 //                scales, 96 P B, from L2), lane 1 the MMA issuer
-//   warp 8       unpacks nibbles into the MMA's K-major int8 layout (A)
-//   warps 0-7    read the int32 half-block sums from TMEM (warp w: TMEM lanes
-//                32(w%4).., sessions 32(w/4)..), two register buffers so the
-//                next read overlaps this one's arithmetic, form and sum the
-//                terms, then run the fused epilogue of layout.h's Epilogue
+//   warp 16      unpacks nibbles into the MMA's K-major int8 layout (A)
+//   warps 0-15   read the int32 half-block sums from TMEM (warp w: TMEM lanes
+//                32(w%4).., sessions 16(w/4)..), release the slot, form and
+//                sum the terms, then run the fused epilogue of layout.h's
+//                Epilogue; four such warps per SM sub-partition hide each
+//                other's TMEM-read and arithmetic latencies
 // Work is split stream-K: the (128-row block, chunk) units are cut evenly
 // over the CTAs; a row block shared by several CTAs is combined by the last
 // one to finish, adding the partial float pairs in contributor order (the
@@ -61,15 +62,19 @@ constexpr int kRawS = kBatchMax * 8 * 12;        // 6144: their scales
 constexpr int kRawBytes = kRawW + kRawB + kRawS;
 constexpr int kABlockBytes = kMmaRows * 32;      // one block of A: 128 rows x 32 int8
 constexpr int kABytes = kChunkBlocks * kABlockBytes;
-constexpr int kEpiWarps = 8, kUnpackWarps = 1;
-constexpr int kCtlWarp = 9;  // lane 0: bulk-copy producer, lane 1: MMA issuer; the warp owns TMEM
-constexpr int kMmaThreads = 12 * 32;  // three warpgroups; warps 10-11 only complete the third
+constexpr int kGrpSess = 16;                       // sessions per epilogue warp
+constexpr int kEpiGroups = kBatchMax / kGrpSess;   // epilogue warpgroups
+constexpr int kEpiWarps = 4 * kEpiGroups, kUnpackWarps = 1;
+constexpr int kCtlWarp = kEpiWarps + kUnpackWarps;  // lane 0: bulk-copy producer, lane 1: MMA issuer; owns TMEM
+constexpr int kMmaThreads = (kEpiWarps + 4) * 32;   // five warpgroups; the last two warps only complete the fifth
 // Register split (setmaxnreg, inside each role's branch): the launch gives
-// every thread 168 registers (12 warps x 32 x 168 = 64512); the third
-// warpgroup drops to 56 and the two epilogue warpgroups rise to 224:
-// 2 x 128 x 224 + 128 x 56 = 64512, all of the launch's registers.
-constexpr int kLaunchRegs = 168, kEpiRegs = 224, kCtlRegs = 56;
-static_assert(2 * 128 * kEpiRegs + 128 * kCtlRegs <= kMmaThreads * kLaunchRegs, "register split exceeds the launch");
+// every thread 96 registers (20 warps x 32 x 96 = 61440); the fifth
+// warpgroup drops to 56 and the four epilogue warpgroups rise to 104:
+// 4 x 128 x 104 + 128 x 56 = 60416 of the launch's 61440.
+constexpr int kLaunchRegs = 96, kEpiRegs = 104, kCtlRegs = 56;
+static_assert(kEpiGroups * 128 * kEpiRegs + 128 * kCtlRegs <= kMmaThreads * kLaunchRegs,
+              "register split exceeds the launch");
+static_assert(kGrpSess == 16, "an epilogue warp reads its sessions' half sums as four 8-column loads");
 static_assert(kRawBytes % 1024 == 0 && kABytes % 1024 == 0, "stage buffers stay 1 KB aligned");
 static_assert(2 * kBatchMax <= kMmaSlotCols, "a slot holds both halves of every session");
 
@@ -136,6 +141,13 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr)
         : "memory");
+}
+// 8 consecutive TMEM columns of this warp's 32 lanes (no wait).
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -292,58 +304,73 @@ __device__ __forceinline__ void mma_row_epilogue(const BatchGemmArgs &a, int t, 
     }
 }
 
-// The 32 sessions [32h, 32h + 32) of tile t, one row per lane.  Every
+// The kGrpSess sessions [kGrpSess h, kGrpSess (h + 1)) of tile t, one row per lane.  Every
 // per-session operand (residual, token, position, ring, RoPE pair) is loaded
 // for all 32 sessions before the first store, so the loads overlap instead of
 // queueing behind stores they might alias.
 template <int EPI>
-__device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t, int lane, int h, const float2 (&v)[16]) {
+__device__ __forceinline__ void mma_block_epilogue(const BatchGemmArgs &a, int t, int lane, int h,
+                                                   const float2 (&v)[kGrpSess / 2]) {
     if (t >= a.W.n_tiles) return;
     const int r = t * kTileRows + lane;
-    const int ns = a.n_sess - 32 * h;  // sessions of this warp (may exceed 32)
-    float op[32];                      // per-session operand of this lane's row
-    int tok = 0, pos = 0, ring = 0;    // lane i: session 32h + i
-    const int sl = 32 * h + lane;
+    const int s0 = kGrpSess * h;
+    const int ns = a.n_sess - s0;      // sessions of this warp (may exceed kGrpSess)
+    float op[kGrpSess];                // per-session operand of this lane's row
+    int tok = 0, pos = 0, ring = 0;    // lane i < kGrpSess: session s0 + i
+    const int sl = s0 + lane;
+    const bool mine = lane < kGrpSess && sl < a.n_sess;
     if constexpr (EPI == kEpiResid) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            op[j] = (j < ns && r < a.W.rows) ? __ldcg(a.resid + static_cast<long long>(32 * h + j) * a.resid_stride + r) : 0.0f;
+        for (int j = 0; j < kGrpSess; ++j)
+            op[j] = (j < ns && r < a.W.rows) ? __ldcg(a.resid + static_cast<long long>(s0 + j) * a.resid_stride + r) : 0.0f;
     } else if constexpr (EPI == kEpiEmbAdd) {
-        tok = sl < a.n_sess ? __ldcg(a.tok + sl) : -1;
+        tok = mine ? __ldcg(a.tok + sl) : -1;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < kGrpSess; ++j) {
             const int tj = __shfl_sync(0xffffffffu, tok, j);
             const bool ok = j < ns && r < a.W.rows && tj >= 0 && tj < a.emb.rows && a.emb.dim == a.W.rows;
             op[j] = ok ? emb_elem(a.emb, tj, r) : 0.0f;
         }
     }
-    float2 rp[32];  // QKV: the (cos, sin) pair of this row's RoPE frequency per session
     if constexpr (EPI == kEpiQKV) {
-        if (sl < a.n_sess) {
+        if (mine) {
             pos = __ldcg(a.pos + sl * a.pos_stride);
             ring = a.ring_of ? __ldcg(a.ring_of + sl) : sl;
         }
         const bool rot = r < a.q_dim + a.kv_dim && a.rope;
         const int d = (r < a.q_dim ? r : r - a.q_dim) % a.head_dim;
+        // eight sessions at a time: their RoPE pairs (cos, sin) of this row's frequency, then their stores
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            rp[j] = (rot && j < ns) ? __ldcg(a.rope + static_cast<long long>(32 * h + j) * (a.head_dim / 2) + (d >> 1))
-                                    : make_float2(1.0f, 0.0f);
+        for (int hf = 0; hf < 2; ++hf) {
+            float2 rp[kGrpSess / 2];
+#pragma unroll
+            for (int j = 0; j < kGrpSess / 2; ++j) {
+                const int jj = hf * (kGrpSess / 2) + j;
+                rp[j] = (rot && jj < ns) ? __ldcg(a.rope + static_cast<long long>(s0 + jj) * (a.head_dim / 2) + (d >> 1))
+                                         : make_float2(1.0f, 0.0f);
+            }
+#pragma unroll
+            for (int j = 0; j < kGrpSess / 2; ++j) {
+                const int jj = hf * (kGrpSess / 2) + j;
+                if (jj >= ns) continue;
+                const float val = (jj & 1) ? v[jj >> 1].y : v[jj >> 1].x;
+                mma_qkv_row(a, t, lane, s0 + jj, val, __shfl_sync(0xffffffffu, pos, jj), __shfl_sync(0xffffffffu, ring, jj),
+                            rp[j]);
+            }
+        }
+        return;
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < kGrpSess / 2; ++j) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const int jj = 2 * j + e, s = 32 * h + jj;
+            const int jj = 2 * j + e, s = s0 + jj;
             if (s >= a.n_sess) continue;
             const float val = e ? v[j].y : v[j].x;
             if constexpr (EPI == kEpiResid) {
                 if (r < a.W.rows) a.y[static_cast<long long>(s) * a.y_stride + r] = __fadd_rn(op[jj], val);
             } else if constexpr (EPI == kEpiEmbAdd) {
                 if (r < a.W.rows) a.y[static_cast<long long>(s) * a.y_stride + r] = __fadd_rn(val, op[jj]);
-            } else if constexpr (EPI == kEpiQKV) {
-                mma_qkv_row(a, t, lane, s, val, __shfl_sync(0xffffffffu, pos, jj), __shfl_sync(0xffffffffu, ring, jj),
-                            rp[jj]);
             } else {
                 mma_row_epilogue<EPI>(a, t, lane, s, val);
             }
@@ -370,18 +397,18 @@ __device__ __forceinline__ double f2d_scaled(float x) {
 }
 constexpr double kUnscale = 0x1p896;
 
-// Terms of one 8-session register buffer r (r[2i] low-half sum, r[2i + 1]
-// high-half sum of session i) into the accumulators of pairs [4k, 4k + 4).
+// Terms of one 4-session register buffer r (r[2i] low-half sum, r[2i + 1]
+// high-half sum of session i) into the accumulators of pairs [2k, 2k + 2).
 template <bool EXACT>
-__device__ __forceinline__ void mma_terms(const uint32_t (&r)[16], const float4 *sc4, const float2 *sc2, float d4,
-                                          float2 (&S)[16], double (&D)[32], int k) {
+__device__ __forceinline__ void mma_terms(const uint32_t (&r)[8], const float4 *sc4, const float2 *sc2, float d4,
+                                          float2 (&S)[kGrpSess / 2], double (&D)[kGrpSess], int k) {
     const float2 d44 = make_float2(d4, d4);
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-        const float4 p = sc4[4 * k + jj];   // d8, d8', -M d8, -M d8'
-        const float2 m4 = sc2[4 * k + jj];  // -4 s8, -4 s8'
+    for (int jj = 0; jj < 2; ++jj) {
+        const float4 p = sc4[2 * k + jj];   // d8, d8', -M d8, -M d8'
+        const float2 m4 = sc2[2 * k + jj];  // -4 s8, -4 s8'
         const float2 d8 = make_float2(p.x, p.y), nm = make_float2(p.z, p.w);
-        const int J = 4 * k + jj;
+        const int J = 2 * k + jj;
         if constexpr (EXACT) {
             // bits of 2^23 + 2^22 + sumi; the fma against -M d8 leaves fl(sumi d8)
             const float2 flo = make_float2(__int_as_float(static_cast<int>(r[4 * jj]) + 0x4B400000),
@@ -415,7 +442,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
     const long long U = static_cast<long long>(n_super) * cpt;
     const long long u0 = unit_lo(U, G, c), u1 = unit_lo(U, G, c + 1);
     const int n_units = static_cast<int>(u1 - u0);
-    const int groups = (ns + 31) / 32;  // epilogue warpgroups (32 sessions each) with sessions
+    const int groups = (ns + kGrpSess - 1) / kGrpSess;  // epilogue warpgroups (kGrpSess sessions a warp) with sessions
     volatile int *abort = &S.abort;
 
     if (tid == 0) {
@@ -541,14 +568,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
         // ---------------- epilogue warps ----------------
         const int q = warp & 3, h = warp >> 2;
         const bool active = h < groups;
-        float2 Sacc[16];  // fast: fp32 sums of session pairs
-        double Dacc[32];  // exact: double sums of each session, scaled by 2^-896
+        float2 Sacc[kGrpSess / 2];  // fast: fp32 sums of session pairs
+        double Dacc[kGrpSess];      // exact: double sums of each session, scaled by 2^-896
 #pragma unroll
-        for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < kGrpSess / 2; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + 64 * h;
-        uint32_t rA[16], rB[16];
+        for (int j = 0; j < kGrpSess; ++j) Dacc[j] = 0.0;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + 2 * kGrpSess * h;
+        uint32_t rA[8], rB[8];
         bool ok = true;
         for (int g = 0; active && g < n_units; ++g) {
             const long long u = u0 + g;
@@ -563,21 +590,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 ok = wait_ab(&S.tm_full[slot], use & 1, abort);
                 if (!__all_sync(0xffffffffu, ok)) break;
                 tc_fence_after();
-                // four reads of 8 sessions (16 columns); each read overlaps the previous one's arithmetic
+                // four reads of 4 sessions (8 columns); each read overlaps the previous one's arithmetic
                 const uint32_t ta = lane_base + slot * kMmaSlotCols;
-                tmem_ld16_nowait(ta, rA);
-                tmem_wait_ld();
+                tmem_ld8_nowait(ta, rA);
                 const float d4 = __half2float(d4p[b * 32]);
                 const uint8_t *scb = raw + kRawW + kRawB + b * P * 12;
-                const float4 *sc4 = reinterpret_cast<const float4 *>(scb) + 16 * h;
-                const float2 *sc2 = reinterpret_cast<const float2 *>(scb + P * 8) + 16 * h;
-                tmem_ld16_nowait(ta + 16, rB);
+                const float4 *sc4 = reinterpret_cast<const float4 *>(scb) + (kGrpSess / 2) * h;
+                const float2 *sc2 = reinterpret_cast<const float2 *>(scb + P * 8) + (kGrpSess / 2) * h;
+                tmem_wait_ld();
+                tmem_ld8_nowait(ta + 8, rB);
                 mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Dacc, 0);
                 tmem_wait_ld();
-                tmem_ld16_nowait(ta + 32, rA);
+                tmem_ld8_nowait(ta + 16, rA);
                 mma_terms<EXACT>(rB, sc4, sc2, d4, Sacc, Dacc, 1);
                 tmem_wait_ld();
-                tmem_ld16_nowait(ta + 48, rB);
+                tmem_ld8_nowait(ta + 24, rB);
                 mma_terms<EXACT>(rA, sc4, sc2, d4, Sacc, Dacc, 2);
                 tmem_wait_ld();
                 tc_fence_before();
@@ -596,7 +623,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
             if (first >= u0 && lastu < u1) {
                 if constexpr (EXACT) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
+                    for (int j = 0; j < kGrpSess / 2; ++j)
                         Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j] * kUnscale),
                                            __double2float_rn(Dacc[2 * j + 1] * kUnscale));
                 }
@@ -609,9 +636,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 float *part_f = reinterpret_cast<float *>(part_d);
                 // the partial holds P sessions: padding sessions beyond P are not stored
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    if (32 * h + 2 * j < P) {
-                        const size_t i0 = static_cast<size_t>(32 * h + 2 * j) * kMmaRows + 32 * q + lane;
+                for (int j = 0; j < kGrpSess / 2; ++j) {
+                    if (kGrpSess * h + 2 * j < P) {
+                        const size_t i0 = static_cast<size_t>(kGrpSess * h + 2 * j) * kMmaRows + 32 * q + lane;
                         if constexpr (EXACT) {
                             part_d[i0] = Dacc[2 * j];
                             part_d[i0 + kMmaRows] = Dacc[2 * j + 1];
@@ -634,32 +661,33 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                     // partials added in contributor order: the result does not depend on timing
                     const double *base = reinterpret_cast<const double *>(a.ws) + static_cast<size_t>(st) * a.max_contrib * slab;
                     // contributor by contributor, all of a contributor's loads in flight together
-                    const size_t r0 = static_cast<size_t>(32 * h) * kMmaRows + 32 * q + lane;
+                    const int s0 = kGrpSess * h;
+                    const size_t r0 = static_cast<size_t>(s0) * kMmaRows + 32 * q + lane;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
+                    for (int j = 0; j < kGrpSess; ++j) Dacc[j] = 0.0;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+                    for (int j = 0; j < kGrpSess / 2; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
                     for (int k = 0; k < n_c; ++k) {
                         const double *pk = base + k * slab + r0;
                         if constexpr (EXACT) {
-                            double v[32];
+                            double v[kGrpSess];
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = 32 * h + j < P ? __ldcg(pk + j * kMmaRows) : 0.0;
+                            for (int j = 0; j < kGrpSess; ++j) v[j] = s0 + j < P ? __ldcg(pk + j * kMmaRows) : 0.0;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) Dacc[j] += v[j];
+                            for (int j = 0; j < kGrpSess; ++j) Dacc[j] += v[j];
                         } else {
                             const float *pf = reinterpret_cast<const float *>(base + k * slab) + r0;
-                            float v[32];
+                            float v[kGrpSess];
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = 32 * h + j < P ? __ldcg(pf + j * kMmaRows) : 0.0f;
+                            for (int j = 0; j < kGrpSess; ++j) v[j] = s0 + j < P ? __ldcg(pf + j * kMmaRows) : 0.0f;
 #pragma unroll
-                            for (int j = 0; j < 16; ++j)
+                            for (int j = 0; j < kGrpSess / 2; ++j)
                                 Sacc[j] = make_float2(__fadd_rn(Sacc[j].x, v[2 * j]), __fadd_rn(Sacc[j].y, v[2 * j + 1]));
                         }
                     }
                     if constexpr (EXACT) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
+                        for (int j = 0; j < kGrpSess / 2; ++j)
                             Sacc[j] = make_float2(__double2float_rn(Dacc[2 * j] * kUnscale),
                                            __double2float_rn(Dacc[2 * j + 1] * kUnscale));
                     }
@@ -668,9 +696,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) batch_mma_kernel(const __grid_
                 named_sync(1, 128 * groups);  // S.last is reused by the next block
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < kGrpSess / 2; ++j) Sacc[j] = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) Dacc[j] = 0.0;
+            for (int j = 0; j < kGrpSess; ++j) Dacc[j] = 0.0;
         }
         tc_fence_before();
     }
