@@ -243,81 +243,104 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
 // p = fl(exp(s - M) in double), out = fl(sum p v / sum p) with the sums in
 // double; a window of one returns the raw fp32 v.  One warp per head, lanes
 // split head_dim, the window (<= MAXWIN rows) held in registers; warps
-// [0, NWARPS) take part, the output goes to xout[n_heads * HD].
+// [0, NWARPS) take part, each taking kHpw heads at a time whose q, K and V
+// loads are all issued before any arithmetic (one memory round trip), and the
+// window's dot products reduced across lanes together (independent shuffle
+// chains); the output goes to xout[n_heads * HD].
 template <int NWARPS, int HD, int MAXWIN>
 __device__ void dep_attention_block(const AttnArgs &at, float *xout) {
     constexpr int kP = HD / 64;  // half2 pairs per lane per row
+    constexpr int kHpw = 2;      // heads per warp in flight
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *at.pos;
     const int window = pos + 1 > at.n_ctx ? at.n_ctx : pos + 1;
     const int start = pos + 1 - window;
-    for (int h = warp; h < at.n_heads; h += NWARPS) {
-        const int kh = at.n_kv_heads == at.n_heads ? h : h / (at.n_heads / at.n_kv_heads);
-        float *x = xout + h * HD;
-        if (window == 1) {
-            for (int d = lane; d < HD; d += 32) x[d] = __ldcg(at.v_raw + kh * HD + d);
-            continue;
-        }
-        const long long head_row0 = at.kv_layer_off / HD + static_cast<long long>(kh) * at.n_ctx;
-        const __half2 *kc = static_cast<const __half2 *>(at.k_cache);
-        const __half2 *vc = static_cast<const __half2 *>(at.v_cache);
-        float2 q[kP];
-        __half2 kk[MAXWIN][kP], vv[MAXWIN][kP];
+    const __half2 *kc = static_cast<const __half2 *>(at.k_cache);
+    const __half2 *vc = static_cast<const __half2 *>(at.v_cache);
+    for (int hb = warp; hb < at.n_heads; hb += NWARPS * kHpw) {
+        float2 q[kHpw][kP];
+        __half2 kk[kHpw][MAXWIN][kP], vv[kHpw][MAXWIN][kP];
+        float rawv[kHpw][HD / 32];
 #pragma unroll
-        for (int i = 0; i < kP; ++i) q[i] = __ldcg(reinterpret_cast<const float2 *>(at.q + h * HD) + lane + 32 * i);
+        for (int u = 0; u < kHpw; ++u) {
+            const int h = hb + u * NWARPS;
+            const bool on = h < at.n_heads;
+            const int kh = at.n_kv_heads == at.n_heads ? h : h / (at.n_heads / at.n_kv_heads);
+            if (window == 1) {
 #pragma unroll
-        for (int j = 0; j < MAXWIN; ++j) {
-            if (j < window) {
+                for (int i = 0; i < HD / 32; ++i) rawv[u][i] = on ? __ldcg(at.v_raw + kh * HD + lane + 32 * i) : 0.0f;
+                continue;
+            }
+            const long long head_row0 = at.kv_layer_off / HD + static_cast<long long>(kh) * at.n_ctx;
+#pragma unroll
+            for (int i = 0; i < kP; ++i)
+                q[u][i] = on ? __ldcg(reinterpret_cast<const float2 *>(at.q + h * HD) + lane + 32 * i) : make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < MAXWIN; ++j) {
+                const bool in = on && j < window;
                 const long long row = head_row0 + (start + j) % at.n_ctx;
 #pragma unroll
                 for (int i = 0; i < kP; ++i) {
                     const long long e2 = (row * HD) / 2 + lane + 32 * i;
-                    kk[j][i] = __ldcg(kc + e2);
-                    vv[j][i] = __ldcg(vc + e2);
+                    kk[u][j][i] = in ? __ldcg(kc + e2) : __floats2half2_rn(0.0f, 0.0f);
+                    vv[u][j][i] = in ? __ldcg(vc + e2) : __floats2half2_rn(0.0f, 0.0f);
                 }
             }
         }
-        float my_s = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < MAXWIN; ++j) {
-            if (j < window) {
-                double dot = 0.0;
+        for (int u = 0; u < kHpw; ++u) {
+            const int h = hb + u * NWARPS;
+            if (h >= at.n_heads) continue;
+            float *x = xout + h * HD;
+            if (window == 1) {
+#pragma unroll
+                for (int i = 0; i < HD / 32; ++i) x[lane + 32 * i] = rawv[u][i];
+                continue;
+            }
+            double dot[MAXWIN];
+#pragma unroll
+            for (int j = 0; j < MAXWIN; ++j) {
+                dot[j] = 0.0;
 #pragma unroll
                 for (int i = 0; i < kP; ++i) {
-                    const float2 kf = __half22float2(kk[j][i]);
-                    dot = fma(static_cast<double>(q[i].x), static_cast<double>(kf.x), dot);
-                    dot = fma(static_cast<double>(q[i].y), static_cast<double>(kf.y), dot);
+                    const float2 kf = __half22float2(kk[u][j][i]);
+                    dot[j] = fma(static_cast<double>(q[u][i].x), static_cast<double>(kf.x), dot[j]);
+                    dot[j] = fma(static_cast<double>(q[u][i].y), static_cast<double>(kf.y), dot[j]);
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-                const float sj = __fmul_rn(__double2float_rn(dot), at.scale);
-                if (lane == j) my_s = sj;
             }
-        }
-        const float M = warp_max(lane < window ? my_s : -INFINITY);
-        const float p = lane < window ? __double2float_rn(exp(static_cast<double>(__fsub_rn(my_s, M)))) : 0.0f;
-        double l = static_cast<double>(p);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        double ox[kP], oy[kP];
+            for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int i = 0; i < kP; ++i) ox[i] = oy[i] = 0.0;
+                for (int j = 0; j < MAXWIN; ++j) dot[j] += __shfl_xor_sync(0xffffffffu, dot[j], o);
+            float my_s = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < MAXWIN; ++j) {
-            if (j < window) {
+            for (int j = 0; j < MAXWIN; ++j)
+                if (lane == j && j < window) my_s = __fmul_rn(__double2float_rn(dot[j]), at.scale);
+            const float M = warp_max(my_s);
+            const float p = lane < window ? __double2float_rn(exp(static_cast<double>(__fsub_rn(my_s, M)))) : 0.0f;
+            double l = static_cast<double>(p);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            double ox[kP], oy[kP];
+#pragma unroll
+            for (int i = 0; i < kP; ++i) ox[i] = oy[i] = 0.0;
+#pragma unroll
+            for (int j = 0; j < MAXWIN; ++j) {
                 const double pj = static_cast<double>(__shfl_sync(0xffffffffu, p, j));
+                if (j < window) {
 #pragma unroll
-                for (int i = 0; i < kP; ++i) {
-                    const float2 vf = __half22float2(vv[j][i]);
-                    ox[i] = fma(pj, static_cast<double>(vf.x), ox[i]);
-                    oy[i] = fma(pj, static_cast<double>(vf.y), oy[i]);
+                    for (int i = 0; i < kP; ++i) {
+                        const float2 vf = __half22float2(vv[u][j][i]);
+                        ox[i] = fma(pj, static_cast<double>(vf.x), ox[i]);
+                        oy[i] = fma(pj, static_cast<double>(vf.y), oy[i]);
+                    }
                 }
             }
-        }
 #pragma unroll
-        for (int i = 0; i < kP; ++i) {
-            x[2 * (lane + 32 * i)] = __double2float_rn(__ddiv_rn(ox[i], l));
-            x[2 * (lane + 32 * i) + 1] = __double2float_rn(__ddiv_rn(oy[i], l));
+            for (int i = 0; i < kP; ++i) {
+                x[2 * (lane + 32 * i)] = __double2float_rn(__ddiv_rn(ox[i], l));
+                x[2 * (lane + 32 * i) + 1] = __double2float_rn(__ddiv_rn(oy[i], l));
+            }
         }
     }
 }
