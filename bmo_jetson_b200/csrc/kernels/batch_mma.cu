@@ -172,16 +172,31 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// mbarrier wait for the pipeline hand-offs: spins on try_wait (which itself
-// suspends the thread for a short hardware-chosen time) without sleeping in
-// between -- a sleep here would add its latency to every stage of every unit
-// -- and gives up after 2 s, or as soon as another role has aborted.
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (it wakes then, not at the end of the hint) or kSuspendNs
+// pass, so a waiting role takes no issue slots from the epilogue warps.
+constexpr uint32_t kSuspendNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+
+// mbarrier wait for the pipeline hand-offs: repeated suspending try_waits, no
+// sleep in between (a sleep would add its latency to every stage of every
+// unit); gives up after 2 s, or as soon as another role has aborted.
 constexpr uint64_t kWaitNs = 2000000000ull;
 __device__ __forceinline__ bool wait_ab(uint64_t *bar, uint32_t parity, volatile int *abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_hint(bar, parity)) return true;
         if ((i & 63) == 0) {
             if (*abort) return false;
             if (global_ns() - t0 > kWaitNs) break;
