@@ -271,4 +271,9 @@ def ref_lib() -> ctypes.CDLL:
     L.ref_attention.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 7
     L.ref_time_gemv.argtypes = [_u8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     L.ref_time_gemv.restype = ctypes.c_float
+    L.ref_time_gemv_cold.argtypes = [_u8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                     ctypes.c_int]
+    L.ref_time_gemv_cold.restype = ctypes.c_float
+    L.ref_time_attention_cold.argtypes = [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    L.ref_time_attention_cold.restype = ctypes.c_float
     return L

@@ -127,4 +127,74 @@ float ref_time_gemv(const void *W, const float *x, int rows, int cols, int warmu
     return finish() == 0 ? ts[iters / 2] * 1000.0f : -1.0f;
 }
 
+// Cold-L2 timings: before every timed launch the caller's flush buffer (larger
+// than L2) is rewritten, so each launch streams its operands from HBM as in a
+// decode frame.  Median over `iters` launches, microseconds, CUDA events on
+// the default stream (the reference launchers' stream here).
+static float median_us(float *ts, int n) {
+    for (int i = 1; i < n; ++i)
+        for (int j = i; j > 0 && ts[j] < ts[j - 1]; --j) { float t = ts[j]; ts[j] = ts[j - 1]; ts[j - 1] = t; }
+    return ts[n / 2] * 1000.0f;
+}
+
+// The reference's Q8_1 quantise + GEMV pair (launch_gemv_q4_0_q8_1 launches both).
+float ref_time_gemv_cold(const void *W, const float *x, int rows, int cols, void *flush_dev, size_t flush_bytes,
+                         int iters) {
+    const size_t wb = (size_t)rows * (cols / 32) * 18, qb = (size_t)(cols / 32) * 36;
+    dbuf dW(wb), dx((size_t)cols * 4), dy((size_t)rows * 4), dq(qb);
+    cudaMemcpy(dW.p, W, wb, cudaMemcpyHostToDevice);
+    cudaMemcpy(dx.p, x, (size_t)cols * 4, cudaMemcpyHostToDevice);
+    for (int i = 0; i < 3; ++i) launch_gemv_q4_0_q8_1(dW.p, dx.as<float>(), dy.as<float>(), rows, cols, dq.p, nullptr);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    float ts[256];
+    if (iters > 256) iters = 256;
+    for (int i = 0; i < iters; ++i) {
+        cudaMemsetAsync(flush_dev, i & 0xFF, flush_bytes, nullptr);
+        cudaEventRecord(a);
+        launch_gemv_q4_0_q8_1(dW.p, dx.as<float>(), dy.as<float>(), rows, cols, dq.p, nullptr);
+        cudaEventRecord(b);
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&ts[i], a, b);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return finish() == 0 ? median_us(ts, iters) : -1.0f;
+}
+
+// The reference decode attention (append K/V at pos % n_ctx, attend over the
+// window) for one layer of an fp16 cache of n_ctx slots; inputs are zeros (the
+// work does not depend on the values).
+float ref_time_attention_cold(int head_dim, int n_heads, int n_ctx, int pos, void *flush_dev, size_t flush_bytes,
+                              int iters) {
+    const size_t qn = (size_t)n_heads * head_dim * 4, cn = (size_t)n_heads * n_ctx * head_dim * 2;
+    dbuf dq(qn), dk(qn), dv(qn), dkc(cn), dvc(cn), dout(qn);
+    cudaMemset(dq.p, 0, qn);
+    cudaMemset(dk.p, 0, qn);
+    cudaMemset(dv.p, 0, qn);
+    cudaMemset(dkc.p, 0, cn);
+    cudaMemset(dvc.p, 0, cn);
+    for (int i = 0; i < 3; ++i)
+        launch_decode_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dkc.p, dvc.p, dout.as<float>(), head_dim,
+                                n_heads, n_heads, n_ctx, pos, 0, nullptr, nullptr);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    float ts[256];
+    if (iters > 256) iters = 256;
+    for (int i = 0; i < iters; ++i) {
+        cudaMemsetAsync(flush_dev, i & 0xFF, flush_bytes, nullptr);
+        cudaEventRecord(a);
+        launch_decode_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dkc.p, dvc.p, dout.as<float>(), head_dim,
+                                n_heads, n_heads, n_ctx, pos, 0, nullptr, nullptr);
+        cudaEventRecord(b);
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&ts[i], a, b);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return finish() == 0 ? median_us(ts, iters) : -1.0f;
+}
+
 }  // extern "C"
