@@ -301,8 +301,9 @@ def bench_batch(path, local, dist, sessions, steps, warmup, rank):
 
 def run_tp(args, rank, world, local):
     """Config 5: one session split over the world's GPUs (attention heads and
-    FFN columns per rank, a double all-reduce after each O-projection and
-    FFN-out).  Every rank decodes the same frames; rank 0 prints frames/s of
+    FFN columns per rank, the double partial sums of each O-projection and
+    FFN-out summed over the ranks -- over peer memory by default, NCCL with
+    BMO_TP_P2P=0).  Every rank decodes the same frames; rank 0 prints frames/s of
     the single stream and p50/p99 frame times (device events, max over ranks)."""
     import torch
     dist = init_dist(world, local)
@@ -359,7 +360,9 @@ def run_tp(args, rank, world, local):
                           "config": {"workload": "config5: one session, 32-layer temporal + text head + 8-step "
                                                  "depformer per frame, heads and FFN columns split over the GPUs",
                                      "parallelism": f"tp{world}", "n_ctx": N_CTX, "start_pos": START_POS,
-                                     "kv": args.kv},
+                                     "kv": args.kv,
+                                     "exchange": "NVLink peer memory (IPC-mapped partial buffers, fused sum + "
+                                                 "residual kernel)" if e.tp_peer_exchange else "NCCL all-reduce"},
                           "text_tokens_head": toks[args.warmup:args.warmup + 4, 0].tolist()}), flush=True)
     e.close()
     if dist is not None:

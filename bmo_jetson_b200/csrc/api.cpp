@@ -135,6 +135,7 @@ bmo_handle_t *bmo_init_tp(const char *gguf_path, int n_ctx, int device, int kv_t
 
 int bmo_get_tp_size(bmo_handle_t *h) { return (h && h->eng) ? h->eng->tp_size : 0; }
 int bmo_get_tp_rank(bmo_handle_t *h) { return (h && h->eng) ? h->eng->tp_rank : 0; }
+int bmo_get_tp_exchange(bmo_handle_t *h) { return (h && h->eng && h->eng->tp_exchange()) ? 1 : 0; }
 
 void bmo_free(bmo_handle_t *h) {
     if (!h) return;

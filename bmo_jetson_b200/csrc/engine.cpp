@@ -86,6 +86,7 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     load(gguf_path);
     if (tensor_parallel) tp_comm_.reset(new TpComm(cfg.tp_id, tp_rank, tp_size));
     alloc_state();
+    setup_tp_exchange();
     // BMO_DEP_FOLD=1: the depformer attention runs inside its O-projection GEMV
     // (measured slower than a separate attention kernel on B200, so off by default)
     dep_fold_ = !tensor_parallel && dep_hd == gemv_dep_attn_head_dim() && dep_n_ctx <= gemv_dep_attn_max_window() &&
@@ -107,6 +108,7 @@ Engine::~Engine() {
     drop(g_cascade_);
     drop(g_frame_);
     for (auto &g : g_depth_) drop(g);
+    teardown_tp_exchange();
     tp_comm_.reset();
     for (void *p : allocs_) cudaFree(p);
     for (void *p : {(void *)fin_h_, (void *)z_h_, (void *)logits_h_, (void *)zin_h_, (void *)dlogits_h_,
@@ -617,11 +619,88 @@ static FramePhase gemv_op(const GemvArgs &g, int pro, int epi) {
     return p;
 }
 
+// Maps every rank's exchange block into this process through CUDA IPC (the
+// handles travel over the NCCL communicator).  All ranks agree: if any rank
+// cannot export or map a block, every rank keeps the NCCL path
+// (BMO_TP_P2P=0 forces it).
+void Engine::setup_tp_exchange() {
+    tp_p2p_ = false;
+    if (!tensor_parallel || tp_size < 2) return;
+    int ok = tp_size <= kTpMaxRanks && std::max(n_embd, dep_dim) <= kTpBufDoubles && env_int("BMO_TP_P2P", 1) != 0;
+    cudaIpcMemHandle_t mine{};
+    if (ok) {
+        ok = cudaMalloc(&tp_block_, kTpBlockBytes) == cudaSuccess &&
+             cudaMemset(tp_block_, 0, kTpBlockBytes) == cudaSuccess &&
+             cudaIpcGetMemHandle(&mine, tp_block_) == cudaSuccess;
+        if (!ok) cudaGetLastError();
+    }
+    if (!tp_comm_->all_min(ok)) {
+        teardown_tp_exchange();
+        return;
+    }
+    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(tp_size));
+    tp_comm_->all_gather_bytes(&mine, all.data(), sizeof mine);
+    for (int r = 0; r < tp_size; ++r) {
+        if (r == tp_rank) {
+            tp_peer_[r] = tp_block_;
+        } else if (ok && cudaIpcOpenMemHandle(&tp_peer_[r], all[static_cast<size_t>(r)],
+                                              cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            tp_peer_[r] = nullptr;
+            ok = 0;
+        }
+    }
+    if (!tp_comm_->all_min(ok)) {  // every rank has mapped every block, or none uses them
+        teardown_tp_exchange();
+        return;
+    }
+    void *seq = nullptr;
+    ck(cudaMalloc(&seq, sizeof(unsigned long long)), "cudaMalloc exchange count");
+    allocs_.push_back(seq);
+    ck(cudaMemset(seq, 0, sizeof(unsigned long long)), "cudaMemset exchange count");
+    tp_seq_ = static_cast<unsigned long long *>(seq);
+    tp_p2p_ = true;
+}
+
+// Unmaps the peers' blocks and frees this rank's once every rank is done with
+// them (a barrier when the exchange was live).
+void Engine::teardown_tp_exchange() {
+    if (tp_p2p_ && tp_comm_) {
+        try {
+            tp_comm_->barrier();
+        } catch (...) {
+        }
+    }
+    for (int r = 0; r < kTpMaxRanks; ++r) {
+        if (tp_peer_[r] && tp_peer_[r] != tp_block_) cudaIpcCloseMemHandle(tp_peer_[r]);
+        tp_peer_[r] = nullptr;
+    }
+    if (tp_block_) cudaFree(tp_block_);
+    tp_block_ = nullptr;
+    tp_p2p_ = false;
+}
+
 // Tensor parallel: the split projection g (whose output rows are partial over
 // the ranks) as a GEMV storing double partials, their sum over the ranks, and
-// y = resid + the sum rounded once.
-void Engine::ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n) const {
+// y = resid + the sum rounded once.  Over peer memory (default): the partials
+// go to this rank's exchange buffer `buf` (a layer's two split projections use
+// buffers 0 and 1) and one exchange kernel sums every rank's buffer and adds
+// the residual; else an NCCL all-reduce and a residual kernel.
+void Engine::ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n,
+                           int buf) const {
     GemvArgs p = g;
+    if (tp_p2p_) {
+        p.ypart = tp_buf(tp_rank, buf);
+        v.push_back(gemv_op(p, kProPlain, kEpiPartial));
+        FramePhase ex{};
+        ex.kind = kPhTpExchange;
+        ex.splits = buf;
+        ex.g.resid = resid;
+        ex.g.y = y;
+        ex.count = n;
+        v.push_back(ex);
+        return;
+    }
     p.ypart = tp_part_;
     v.push_back(gemv_op(p, kProPlain, kEpiPartial));
     FramePhase ar{};
@@ -690,7 +769,7 @@ void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     o.x = attn_;
     o.y = xmid_;
     o.resid = x_in;
-    if (tensor_parallel) ops_tp_reduce(v, o, x_in, xmid_, n_embd);
+    if (tensor_parallel) ops_tp_reduce(v, o, x_in, xmid_, n_embd, 0);
     else v.push_back(gemv_op(o, kProPlain, kEpiResid));
 
     GemvArgs fi = gemv_base(L_[l].ffn_in);
@@ -704,7 +783,7 @@ void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     fo.x = act_;
     fo.y = x_out;
     fo.resid = xmid_;
-    if (tensor_parallel) ops_tp_reduce(v, fo, xmid_, x_out, n_embd);
+    if (tensor_parallel) ops_tp_reduce(v, fo, xmid_, x_out, n_embd, 1);
     else v.push_back(gemv_op(fo, kProPlain, kEpiResid));
 }
 
@@ -791,7 +870,7 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
             ap.head_dim = dep_hd;
             ap.splits = 1;
             v.push_back(ap);
-            if (tensor_parallel) ops_tp_reduce(v, o, dxa_, dxb_, dep_dim);
+            if (tensor_parallel) ops_tp_reduce(v, o, dxa_, dxb_, dep_dim, 0);
             else v.push_back(gemv_op(o, kProPlain, kEpiResid));
         }
 
@@ -806,7 +885,7 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
         fo.x = dact_;
         fo.y = dxa_;
         fo.resid = dxb_;
-        if (tensor_parallel) ops_tp_reduce(v, fo, dxb_, dxa_, dep_dim);
+        if (tensor_parallel) ops_tp_reduce(v, fo, dxb_, dxa_, dep_dim, 1);
         else v.push_back(gemv_op(fo, kProPlain, kEpiResid));
     }
     GemvArgs h = gemv_base(dep_head_[cb]);
@@ -857,6 +936,24 @@ void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
             break;
         case kPhAllReduce: tp_comm_->all_reduce_sum(op.g.ypart, static_cast<size_t>(op.count), s); break;
         case kPhResidAdd: ck(launch_tp_resid(op.g.ypart, op.g.resid, op.g.y, op.count, s), "launch tp resid"); break;
+        case kPhTpExchange: {
+            TpExchangeArgs a{};
+            for (int r = 0; r < tp_size; ++r) {
+                a.part[r] = tp_buf(r, op.splits);
+                a.flag_out[r] =
+                    reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(tp_peer_[r]) + kTpFlagOffset) + tp_rank;
+            }
+            a.flag_in = reinterpret_cast<const unsigned long long *>(static_cast<uint8_t *>(tp_block_) + kTpFlagOffset);
+            a.seq = tp_seq_;
+            a.resid = op.g.resid;
+            a.y = op.g.y;
+            a.status = status_;
+            a.rank = tp_rank;
+            a.size = tp_size;
+            a.n = op.count;
+            ck(launch_tp_exchange(a, s, cfg_.pdl), "launch tp exchange");
+            break;
+        }
         default: throw std::runtime_error("internal: unknown op");
         }
     }
@@ -1013,6 +1110,7 @@ void Engine::finish_call() {
         if (st & (1 << 1)) what += " a bulk copy wait timed out;";
         if (st & (1 << 2)) what += " launch arguments inconsistent with the weight layout;";
         if (st & (1 << 3)) what += " a grid barrier timed out;";
+        if (st & (1 << 4)) what += " a tensor-parallel peer's partial sums did not arrive;";
         throw std::runtime_error("device status " + std::to_string(st) + ":" + what);
     }
 }

@@ -99,6 +99,7 @@ public:
     void capture_all();
     bool graphs_captured() const { return graphs_ready_; }
     bool persistent() const { return persistent_; }
+    bool tp_exchange() const { return tp_p2p_; }
 
     // ---- batched sessions: up to kBatchMax independent sessions stepped
     // together, each with its own temporal ring, sharing one weight stream ----
@@ -162,8 +163,20 @@ private:
     void enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal);
     // tensor parallel
     std::unique_ptr<TpComm> tp_comm_;
-    double *tp_part_ = nullptr;  // partial sums of the split projections, summed over the ranks
-    void ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n) const;
+    double *tp_part_ = nullptr;  // partial sums of the split projections, summed over the ranks (NCCL path)
+    // peer-memory exchange (kPhTpExchange): this rank's block and every rank's
+    // block mapped here (tp_peer_[tp_rank] == tp_block_), and the exchange count
+    bool tp_p2p_ = false;
+    void *tp_block_ = nullptr;
+    void *tp_peer_[kTpMaxRanks] = {};
+    unsigned long long *tp_seq_ = nullptr;
+    void setup_tp_exchange();
+    void teardown_tp_exchange();
+    double *tp_buf(int rank, int buf) const {
+        return static_cast<double *>(tp_peer_[rank]) + static_cast<size_t>(buf) * kTpBufDoubles;
+    }
+    void ops_tp_reduce(std::vector<FramePhase> &v, const GemvArgs &g, const float *resid, float *y, int n,
+                       int buf) const;
     // batched sessions (batch_engine.cpp)
     struct BatchState;
     struct BatchDeleter {

@@ -85,6 +85,7 @@ cudaError_t launch_batch_finalize(const float2 *pairs, int pairs_stride, int n_p
 
 // Tensor parallel: y = resid + (float)part (kernels/misc.cu).
 cudaError_t launch_tp_resid(const double *part, const float *resid, float *y, int n, cudaStream_t s);
+cudaError_t launch_tp_exchange(const TpExchangeArgs &a, cudaStream_t s, bool pdl);
 
 // Frame-start embedding sum + RoPE table (kernels/misc.cu).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,

@@ -145,6 +145,31 @@ enum PhaseKind : int {
     kPhTokenOut = 2,  // CTA 0 writes the first maximum over tok.pairs into tok.tok_out
     kPhAllReduce = 3, // tensor parallel: sum g.ypart[0..count) over the ranks (double, in place)
     kPhResidAdd = 4,  // tensor parallel: g.y[i] = g.resid[i] + (float)g.ypart[i], i < count
+    kPhTpExchange = 5,  // tensor parallel over peer memory: g.y[i] = g.resid[i] + (float)(sum over ranks r,
+                        // in rank order, of rank r's partial buffer `splits`)[i], i < count
+};
+
+// ---- tensor parallel exchange over peer memory ----
+// Every rank owns one exchange block (cudaMalloc, mapped into the other ranks
+// through CUDA IPC): two partial-sum buffers of kTpBufDoubles doubles (the
+// split projections of a layer alternate between them), then one 64-bit
+// arrival word per source rank.  A rank signals "my buffer is complete for
+// exchange e" by storing e into its word of every peer's block (release, system
+// scope); a rank sums the buffers once every peer's word in its own block
+// has reached e.  kTpBlockBytes covers both buffers and the words.
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpBufDoubles = 8192;
+constexpr size_t kTpFlagOffset = 2 * kTpBufDoubles * sizeof(double);
+constexpr size_t kTpBlockBytes = kTpFlagOffset + kTpMaxRanks * sizeof(unsigned long long) + 64;
+struct TpExchangeArgs {
+    const double *part[kTpMaxRanks];           // rank r's partial buffer of this exchange (peer memory for r != rank)
+    unsigned long long *flag_out[kTpMaxRanks];  // this rank's arrival word in rank r's block
+    const unsigned long long *flag_in;          // this rank's arrival words, one per source rank
+    unsigned long long *seq;                    // exchanges this rank has completed (device counter)
+    const float *resid;
+    float *y;
+    int *status;
+    int rank, size, n;
 };
 
 struct FramePhase {

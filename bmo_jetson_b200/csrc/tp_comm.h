@@ -22,6 +22,12 @@ public:
     TpComm &operator=(const TpComm &) = delete;
     // In-place sum of n doubles over the ranks, on stream s (capturable).
     void all_reduce_sum(double *buf, size_t n, cudaStream_t s);
+    // Host-side setup collectives (synchronous): every rank's `bytes` bytes of
+    // `send`, rank by rank, into `recv`; the minimum of v over the ranks;
+    // a barrier.
+    void all_gather_bytes(const void *send, void *recv, size_t bytes);
+    int all_min(int v);
+    void barrier() { (void)all_min(1); }
     int rank() const { return rank_; }
     int size() const { return size_; }
 

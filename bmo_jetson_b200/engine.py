@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
     L.bmo_get_tp_size.restype = i
     L.bmo_get_tp_rank.argtypes = [vp]
     L.bmo_get_tp_rank.restype = i
+    L.bmo_get_tp_exchange.argtypes = [vp]
+    L.bmo_get_tp_exchange.restype = i
     L.bmo_batch_init.argtypes = [vp, i]
     L.bmo_batch_init.restype = i
     L.bmo_batch_sessions.argtypes = [vp]
@@ -209,6 +211,7 @@ class BMOEngine:
 
         self.tp_size = L.bmo_get_tp_size(self._h) or 1
         self.tp_rank = L.bmo_get_tp_rank(self._h)
+        self.tp_peer_exchange = bool(L.bmo_get_tp_exchange(self._h))
 
     # ---- reference methods -------------------------------------------------
     def reset(self) -> None:

@@ -106,6 +106,11 @@ BMO_API bmo_handle_t *bmo_init_tp(const char *gguf_path, int n_ctx, int device, 
                                   int tp_size, const void *tp_id);
 BMO_API int bmo_get_tp_size(bmo_handle_t *h);
 BMO_API int bmo_get_tp_rank(bmo_handle_t *h);
+/* 1 when the ranks sum their partial projections over NVLink peer memory
+ * (every rank's exchange buffers mapped through CUDA IPC, one fused sum +
+ * residual kernel per split projection); 0 on the NCCL all-reduce path (one
+ * rank, BMO_TP_P2P=0, or a rank that could not map its peers). */
+BMO_API int bmo_get_tp_exchange(bmo_handle_t *h);
 
 /* ---- batched sessions ----------------------------------------------------
  * Up to 64 independent sessions share the handle's weights; each has its own

@@ -1,6 +1,8 @@
 """Tensor-parallel batch-1 mode (bmo_init_tp): attention heads and FFN
 columns split over ranks, partial sums of the O-projection and FFN-out summed
-over the ranks in double (NCCL) and rounded once.
+over the ranks in double and rounded once -- over NVLink peer memory (one
+exchange kernel reading every rank's partial buffer through CUDA IPC
+mappings; the default) or an NCCL all-reduce (BMO_TP_P2P=0).
 
 Bars: with one rank the frames are bit-identical to the single-GPU handle;
 with two ranks (two GPUs) both ranks hold the same hidden state and the
@@ -64,11 +66,16 @@ def test_tp_one_rank_is_bit_identical_to_single_gpu(tiny_model):
     et.close()
 
 
-def _tp_rank(rank, size, gid, path, q):
+def _tp_rank(rank, size, gid, path, q, exchange):
+    import os
+    os.environ["BMO_TP_P2P"] = "1" if exchange == "p2p" else "0"
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
     torch.cuda.set_device(rank)
     try:
         e = engine.BMOEngine(path, n_ctx=N_CTX, device=rank, tp=(rank, size, gid))
+        if e.tp_peer_exchange != (exchange == "p2p"):
+            raise RuntimeError(f"exchange path: peer memory {e.tp_peer_exchange}, wanted {exchange}")
         # the full model's KV width, for slicing this rank's heads out of the shared history
         w = e.n_kv_heads * e.head_dim
         full = type("G", (), {"n_kv_heads": e.n_kv_heads * size, "head_dim": e.head_dim, "n_layers": e.n_layers})
@@ -81,7 +88,8 @@ def _tp_rank(rank, size, gid, path, q):
         q.put((rank, repr(ex), 0))
 
 
-def test_tp_two_ranks_match_single_gpu_and_oracle(tiny_model):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_tp_two_ranks_match_single_gpu_and_oracle(tiny_model, exchange):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -89,7 +97,7 @@ def test_tp_two_ranks_match_single_gpu_and_oracle(tiny_model):
     gid = engine.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, size, gid, tiny_model, q)) for r in range(size)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, size, gid, tiny_model, q, exchange)) for r in range(size)]
     for p in procs:
         p.start()
     res = {}
