@@ -240,4 +240,27 @@ int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *
     return static_cast<int>(launch_attention(a, head_dim, attn_splits_for(n_ctx), s, false));
 }
 
+int bmo_k_tp_exchange(const double *const *parts, unsigned long long *const *flag_out,
+                      const unsigned long long *flag_in_dev, unsigned long long *seq_dev, const float *resid_dev,
+                      float *y_dev, int *status_dev, int rank, int size, int n, void *stream) {
+    if (!parts || !flag_out || !flag_in_dev || !seq_dev || !resid_dev || !y_dev || !status_dev || size < 2 ||
+        size > kTpMaxRanks || rank < 0 || rank >= size || n <= 0 || n > kTpBufDoubles)
+        return static_cast<int>(cudaErrorInvalidValue);
+    TpExchangeArgs a{};
+    for (int r = 0; r < size; ++r) {
+        if (!parts[r] || (r != rank && !flag_out[r])) return static_cast<int>(cudaErrorInvalidValue);
+        a.part[r] = parts[r];
+        a.flag_out[r] = flag_out[r];
+    }
+    a.flag_in = flag_in_dev;
+    a.seq = seq_dev;
+    a.resid = resid_dev;
+    a.y = y_dev;
+    a.status = status_dev;
+    a.rank = rank;
+    a.size = size;
+    a.n = n;
+    return static_cast<int>(launch_tp_exchange(a, static_cast<cudaStream_t>(stream), false));
+}
+
 }  // extern "C"

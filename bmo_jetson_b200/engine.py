@@ -133,6 +133,9 @@ def lib() -> ctypes.CDLL:
     L.bmo_k_batch_gemm_q4_0.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, i, i, vp, sz, vp]
     L.bmo_k_batch_gemm_q4_0.restype = i
     L.bmo_k_decode_attention.argtypes = [vp] * 8 + [i] * 4 + [vp, i, i, vp]
+    L.bmo_k_tp_exchange.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)] + [vp] * 5 + \
+        [i, i, i, vp]
+    L.bmo_k_tp_exchange.restype = i
     L.bmo_k_decode_attention.restype = i
     _lib = L
     return L

@@ -107,6 +107,22 @@ BMO_API int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const
                                    int head_dim, int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev,
                                    int layer, int kv_type, void *stream);
 
+/* One tensor-parallel exchange over peer memory (the kernel bmo_init_tp
+ * handles run after each split projection): parts[r] is rank r's buffer of n
+ * double partial sums (device or peer-mapped pointers, r < size <= 8),
+ * flag_out[r] this rank's 64-bit arrival word in rank r's block (ignored for
+ * r == rank), flag_in this rank's words (one per source rank), seq a device
+ * counter starting at 0 that the exchanges of a group share, status a device
+ * int.  Publishes exchange number e into flag_out, waits (at most 2 s) for
+ * flag_in[r] >= e from every peer, then y[i] = resid[i] + fl(sum over r in
+ * rank order of parts[r][i]).  A wait that runs out sets bit 4 of *status and
+ * leaves y untouched; while that bit is set, exchanges return at once.
+ * n <= 8192. */
+BMO_API int bmo_k_tp_exchange(const double *const *parts, unsigned long long *const *flag_out,
+                              const unsigned long long *flag_in_dev, unsigned long long *seq_dev,
+                              const float *resid_dev, float *y_dev, int *status_dev, int rank, int size, int n,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif
