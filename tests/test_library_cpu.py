@@ -108,3 +108,24 @@ def test_gguf_writer_round_trip(tiny_model):
     emb = by_name["emb.0.weight"]
     assert emb.tensor_type == GGMLQuantizationType.F16
     assert list(emb.shape) == [cfg.n_embd, cfg.audio_vocab + 1]
+
+
+def test_cli_arguments_follow_the_reference_harness():
+    from bmo_jetson_b200 import cli
+    a = cli.parse_args([])
+    assert (a.model, a.mode, a.n_iterations, a.layer_begin, a.layer_end, a.debug_dumps) == (
+        "bmo_weights.gguf", "depth_cascade", 100, 0, -1, False)
+    a = cli.parse_args(["m.gguf", "--mode", "stress_test", "--n-iterations", "5", "--n-threads", "8",
+                        "--layer_begin", "2", "--layer_end", "4", "--debug-dumps"])
+    assert (a.model, a.mode, a.n_iterations, a.layer_begin, a.layer_end, a.debug_dumps) == (
+        "m.gguf", "stress_test", 5, 2, 4, True)
+    with pytest.raises(SystemExit):
+        cli.parse_args(["--mode", "bogus"])
+    with pytest.raises(SystemExit):
+        cli.parse_args(["--n-iterations", "-1"])
+
+
+def test_cli_reports_a_missing_model_and_exits_1(tmp_path, capsys):
+    from bmo_jetson_b200 import cli
+    assert cli.main([str(tmp_path / "absent.gguf"), "--mode", "depth_cascade"]) == 1
+    assert "[bmo_main] ERROR:" in capsys.readouterr().err
