@@ -119,16 +119,26 @@ def dist_env():
     return rank, world, local
 
 
-def init_dist(world, local):
+def init_dist(world, local, backend=None):
+    """One process group per run: NCCL over the GPUs, or gloo on the host
+    (backend="gloo", or BMO_DIST_BACKEND=gloo) for the host-side logic."""
     if world <= 1:
         return None
     import datetime
 
     import torch
     import torch.distributed as dist
-    torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    backend = backend or os.environ.get("BMO_DIST_BACKEND", "nccl")
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    else:
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     return dist
+
+
+def _dist_device(dist):
+    return "cuda" if dist.get_backend() == "nccl" else "cpu"
 
 
 def barrier(dist):
@@ -137,12 +147,33 @@ def barrier(dist):
 
 
 def reduce_max(dist, v):
+    """The maximum of v over the ranks (every rank gets it)."""
     if dist is None:
         return v
     import torch
-    t = torch.tensor([float(v)], device="cuda")
+    t = torch.tensor([float(v)], device=_dist_device(dist))
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def broadcast_bytes(dist, data, n, src=0):
+    """Rank src's n bytes `data` on every rank (the tensor-parallel group id)."""
+    if dist is None:
+        return bytes(data)
+    import torch
+    t = torch.zeros(n, dtype=torch.uint8)
+    if dist.get_rank() == src:
+        t = torch.frombuffer(bytearray(data), dtype=torch.uint8).clone()
+    t = t.to(_dist_device(dist))
+    dist.broadcast(t, src)
+    return bytes(t.cpu().numpy())
+
+
+def whole_job_rate(dist, world, ms_local):
+    """Frames/s of the whole job: every rank's frames over the slowest rank's
+    time (max over ranks), and that time."""
+    ms = reduce_max(dist, ms_local)
+    return world * 1000.0 / ms, ms
 
 
 def prepare_model(rank, dist):
@@ -328,15 +359,9 @@ def run_tp(args, rank, world, local):
     torch.cuda.set_device(local)
     path = prepare_model(rank, dist)
     from bmo_jetson_b200 import engine
-    gid = torch.zeros(128, dtype=torch.uint8)
-    if rank == 0:
-        gid = torch.frombuffer(bytearray(engine.tp_unique_id()), dtype=torch.uint8)
-    if dist is not None:
-        g = gid.cuda()
-        dist.broadcast(g, 0)
-        gid = g.cpu()
+    gid = broadcast_bytes(dist, engine.tp_unique_id() if rank == 0 else b"", 128)
     kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
-    e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type, tp=(rank, world, bytes(gid.numpy())))
+    e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type, tp=(rank, world, gid))
     rng = np.random.default_rng(7)
     width = e.n_kv_heads * e.head_dim
     for layer in range(e.n_layers):  # the same history on every rank, each keeps its heads
@@ -549,8 +574,7 @@ def main():
         torch.cuda.synchronize(dev)
     barrier(dist)
     ms_local = ev0.elapsed_time(ev1) / args.steps
-    ms = reduce_max(dist, ms_local)
-    value = world * 1000.0 / ms
+    value, ms = whole_job_rate(dist, world, ms_local)
     out_tokens = out_d.cpu().numpy()
     assert (out_tokens[:, 0] >= 0).all() and (out_tokens[:, 0] < e.text_vocab).all()
 
