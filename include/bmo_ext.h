@@ -94,9 +94,11 @@ BMO_API int bmo_enqueue_cascade(bmo_handle_t *h, int32_t text_token);
  * their KV ring and O-projection columns, and FFN columns [r F/T, (r+1) F/T)
  * of every temporal and depformer layer; embeddings, norms and heads are
  * replicated.  After the O-projection and the FFN-out of every layer the
- * ranks sum their partial outputs in double over NCCL (in the frame's CUDA
- * graph) and round once, so every rank holds the same hidden state and the
- * tokens equal the single-GPU handle's.  Every rank must make the same calls
+ * ranks sum their partial outputs in double -- over NVLink peer memory (the
+ * ranks' exchange buffers mapped through CUDA IPC at init), or an NCCL
+ * all-reduce with BMO_TP_P2P=0; both in the frame's CUDA graph -- and round
+ * once, so every rank holds the same hidden state and the tokens equal the
+ * single-GPU handle's.  Every rank must make the same calls
  * in the same order.  The handle's geometry getters report its shard's head
  * and FFN counts; bmo_kv_import_f32 takes the shard's KV heads.  Needs H, the
  * KV heads, the depformer heads and both FFN widths to split into
