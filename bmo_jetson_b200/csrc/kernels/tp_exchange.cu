@@ -50,6 +50,9 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
     __shared__ int ok_s;
     const int tid = threadIdx.x;
     pdl_wait();  // the GEMV that wrote this rank's partial buffer has completed
+    // the next GEMV's CTAs (which fit beside these 8) may launch and stream
+    // their weights while this kernel waits for the peers
+    pdl_launch_dependents();
     if (tid == 0) {
         // exchange number: the CTAs of the k-th launch draw arrival counts [kG, kG + G)
         const unsigned long long old = atomicAdd(a.seq, 1ull);
@@ -107,7 +110,6 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
             if (r < a.size) acc += v[r][k];
         a.y[i] = __fadd_rn(__ldcg(a.resid + i), __double2float_rn(acc));
     }
-    pdl_launch_dependents();
 }
 
 cudaError_t launch_tp_exchange(const TpExchangeArgs &a, cudaStream_t s, bool pdl) {
