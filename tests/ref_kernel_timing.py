@@ -8,7 +8,7 @@ buffer (so weights and caches come from HBM, as in a decode frame); the median
 of 20 launches is reported.  Work per row:
   GEMV  -- reference: launch_gemv_q4_0_q8_1 (its Q8_1 quantiser + GEMV
            kernels); here: bmo_k_gemv_q4_0 (quantiser fused into the GEMV
-           prologue), plain store epilogue; the SURVEY shapes of the temporal
+           prologue), plain store epilogue; the 7B Moshi shapes of the temporal
            layer and the text head.
   ATTN  -- one layer at pos 700 over a 512-slot fp16 ring, 32 heads x 128:
            reference launch_decode_attention vs bmo_k_decode_attention.
