@@ -67,7 +67,6 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
     cfg_.graphs = cfg.graphs && env_int("BMO_GRAPHS", 1) != 0;
     cfg_.pdl = cfg.pdl && env_int("BMO_PDL", 1) != 0;
-    cfg_.persistent = (cfg.persistent || env_int("BMO_PERSISTENT", 0) != 0) && env_int("BMO_PERSISTENT", 1) != 0;
     n_ctx = cfg.n_ctx > 0 ? cfg.n_ctx : 2048;
     if (n_ctx > attn_max_ctx()) throw std::runtime_error("n_ctx exceeds the ring limit of " + std::to_string(attn_max_ctx()));
     if (cfg.kv_type >= 0) {
@@ -81,17 +80,35 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
         tp_size = cfg.tp_size;
         tp_rank = cfg.tp_rank;
         if (tp_rank < 0 || tp_rank >= tp_size) throw std::runtime_error("tensor parallel: rank outside [0, size)");
-        cfg_.persistent = false;  // the frame kernel has no collective step
     }
     load(gguf_path);
+    int want = cfg.semantics;
+    if (const char *sem = std::getenv("BMO_SEMANTICS")) {
+        if (std::strcmp(sem, "exact") == 0) want = 0;
+        else if (std::strcmp(sem, "ref") == 0) want = 1;
+    }
+    choose_semantics(want);
     if (tensor_parallel) tp_comm_.reset(new TpComm(cfg.tp_id, tp_rank, tp_size));
     alloc_state();
     setup_tp_exchange();
-    // BMO_DEP_FOLD=1: the depformer attention runs inside its O-projection GEMV
-    // (measured slower than a separate attention kernel on B200, so off by default)
-    dep_fold_ = !tensor_parallel && dep_hd == gemv_dep_attn_head_dim() && dep_n_ctx <= gemv_dep_attn_max_window() &&
-                dep_heads * dep_hd <= gemv_max_norm_cols() && env_int("BMO_DEP_FOLD", 0) != 0;
-    build_programs();
+}
+
+// The reference kernels' own fp32 order where everything on the path has a
+// reference kernel to follow (fp16 rings, one GPU, shapes those kernels and
+// the fused prologue take); otherwise the exact-reduction order.
+void Engine::choose_semantics(int want) {
+    std::string why;
+    const bool dep = has_dep_tables && dep_dim > 0 && dep_q > 0;
+    if (kv_type != kKvF16) why = "the KV ring is Q4_0 (the reference's rings are fp16)";
+    else if (tensor_parallel) why = "tensor parallel sums partial projections over the ranks";
+    else if (!attn_ref_supported(head_dim, n_ctx, true))
+        why = "temporal head_dim must be 64 or 128 and n_ctx at most " + std::to_string(attn_ref_max_ctx());
+    else if (dep && !attn_ref_supported(dep_hd, dep_n_ctx, dep_n_ctx > 64))
+        why = "depformer head_dim must be 64 or 128";
+    else if (n_embd > gemv_ref_max_norm_cols() || (dep && dep_dim > gemv_ref_max_norm_cols()))
+        why = "normalised widths above " + std::to_string(gemv_ref_max_norm_cols());
+    if (want == 1 && !why.empty()) throw std::runtime_error("reference-order semantics unavailable: " + why);
+    ref_order_ = want != 0 && why.empty();
 }
 
 Engine::~Engine() {
@@ -747,7 +764,7 @@ void Engine::ops_layer(std::vector<FramePhase> &v, int l) const {
     FramePhase at{};
     at.kind = kPhAttn;
     at.head_dim = head_dim;
-    at.splits = attn_splits_;
+    at.splits = ref_order_ ? 8 : attn_splits_;
     at.at.q = q_;
     at.at.v_raw = vraw_;
     at.at.k_cache = k_cache_;
@@ -809,9 +826,7 @@ std::vector<FramePhase> Engine::ops_temporal() const {
 }
 
 // One depformer codebook step (bmo_build_depth_graph, bmo_compute.cpp:2741-3340).
-// fold: the attention of all heads becomes the O-projection's prologue
-// (persistent kernel only).
-void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok, bool fold) const {
+void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok) const {
     GemvArgs w = gemv_base(dep_in_[cb]);
     w.x = z;
     w.y = dxa_;
@@ -857,22 +872,14 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
         o.x = dattn_;
         o.y = dxb_;
         o.resid = dxa_;
-        if (fold) {
-            o.att = at;
-            FramePhase op = gemv_op(o, kProDepAttn, kEpiResid);
-            op.at = at;
-            op.head_dim = dep_hd;
-            v.push_back(op);
-        } else {
-            FramePhase ap{};
-            ap.kind = kPhAttn;
-            ap.at = at;
-            ap.head_dim = dep_hd;
-            ap.splits = 1;
-            v.push_back(ap);
-            if (tensor_parallel) ops_tp_reduce(v, o, dxa_, dxb_, dep_dim, 0);
-            else v.push_back(gemv_op(o, kProPlain, kEpiResid));
-        }
+        FramePhase ap{};
+        ap.kind = kPhAttn;
+        ap.at = at;
+        ap.head_dim = dep_hd;
+        ap.splits = (ref_order_ && dep_n_ctx > 64) ? 8 : 1;
+        v.push_back(ap);
+        if (tensor_parallel) ops_tp_reduce(v, o, dxa_, dxb_, dep_dim, 0);
+        else v.push_back(gemv_op(o, kProPlain, kEpiResid));
 
         GemvArgs fi = gemv_base(D_[i].ffn_in[cb]);
         fi.x = dxb_;
@@ -898,7 +905,7 @@ void Engine::ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, 
 
 // dep_q greedy steps, each step's token the argmax of the previous head,
 // then the last step's token.
-void Engine::ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first, bool fold) const {
+void Engine::ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first) const {
     for (int cb = 0; cb < dep_q; ++cb) {
         TokenSrc t{};
         if (cb == 0) {
@@ -909,7 +916,7 @@ void Engine::ops_cascade(std::vector<FramePhase> &v, const float *z, const Token
             t.n_pairs = dep_head_[cb - 1].n_tiles;
             t.tok_out = tok_out_ + cb;
         }
-        ops_depth_step(v, cb, z, t, fold);
+        ops_depth_step(v, cb, z, t);
     }
     FramePhase f{};
     f.kind = kPhTokenOut;
@@ -924,13 +931,20 @@ void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
     for (const FramePhase &op : ops) {
         switch (op.kind) {
         case kPhGemv: {
+            if (ref_order_) {
+                ck(launch_gemv_ref(op.g, op.pro, op.epi, gemv_ref_grid(op.g.W, sm_count), s, cfg_.pdl), "launch gemv");
+                break;
+            }
             const GemvPlan p = plan_gemv(op.g.W, sm_count);
             GemvArgs b = op.g;
             b.tile_aligned = p.tile_aligned;
             ck(launch_gemv(b, op.pro, op.epi, p.grid, s, cfg_.pdl), "launch gemv");
             break;
         }
-        case kPhAttn: ck(launch_attention(op.at, op.head_dim, op.splits, s, cfg_.pdl), "launch attention"); break;
+        case kPhAttn:
+            if (ref_order_) ck(launch_attention_ref(op.at, op.head_dim, op.splits > 1, s, cfg_.pdl), "launch attention");
+            else ck(launch_attention(op.at, op.head_dim, op.splits, s, cfg_.pdl), "launch attention");
+            break;
         case kPhTokenOut:
             ck(launch_finalize_token(op.tok.pairs, op.tok.n_pairs, op.tok.tok_out, s, cfg_.pdl), "launch finalize");
             break;
@@ -961,7 +975,7 @@ void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
 
 void Engine::enqueue_embed(cudaStream_t s) {
     ck(launch_embed(ttables_d_, n_ttables_, fin_d_->tokens, &fin_d_->n_tok, n_embd, resid_, &fin_d_->pos, rope_theta,
-                    head_dim, rope_, s),
+                    head_dim, rope_, ref_order_, s),
        "launch embed");
 }
 
@@ -978,7 +992,7 @@ void Engine::enqueue_layer(cudaStream_t s, int l) {
 
 void Engine::enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok) {
     std::vector<FramePhase> v;
-    ops_depth_step(v, cb, z, tok, dep_fold_);
+    ops_depth_step(v, cb, z, tok);
     enqueue_ops(s, v);
 }
 
@@ -990,82 +1004,8 @@ void Engine::reset_depth_kv_async(cudaStream_t s) {
 void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
     reset_depth_kv_async(s);
     std::vector<FramePhase> v;
-    ops_cascade(v, z, first, dep_fold_);
+    ops_cascade(v, z, first);
     enqueue_ops(s, v);
-}
-
-// ---------------------------------------------------------------------------
-// persistent frame kernel programs
-// ---------------------------------------------------------------------------
-// Decides whether this model runs under the frame kernel and uploads its
-// programs.  Anything the kernel does not cover keeps the per-op path.
-void Engine::build_programs() {
-    persistent_ = false;
-    if (!cfg_.persistent || kv_type != kKvF16 || tensor_parallel) return;
-    frame_grid_ = frame_max_grid();
-    if (frame_grid_ <= 0) return;
-    if (n_ctx > frame_max_window() || (head_dim != 64 && head_dim != 128) || n_heads > frame_grid_) return;
-    const bool dep = has_dep_tables && dep_dim > 0 && dep_q > 0;
-    if (dep && (dep_n_ctx > frame_dep_max_window() || dep_hd != frame_dep_head_dim() ||
-                dep_heads * dep_hd > frame_max_window()))
-        return;
-    auto fits = [&](const std::vector<FramePhase> &ops) {
-        for (const FramePhase &op : ops) {
-            if (op.kind != kPhGemv) continue;
-            const int tiles_per_cta = (op.g.W.n_tiles + frame_grid_ - 1) / frame_grid_;
-            if (tiles_per_cta > frame_max_tiles_per_cta() || op.g.W.nbx > gemv_max_nbx()) return false;
-            if (op.pro == kProNorm && op.g.W.cols > 8192) return false;
-            if ((reinterpret_cast<uintptr_t>(op.g.x) & 15) != 0) return false;
-        }
-        return true;
-    };
-    auto upload = [&](const std::vector<FramePhase> &ops, DevProgram &p) {
-        const size_t bytes = sizeof(FramePhase) * ops.size();
-        FramePhase *d = nullptr;
-        ck(cudaMalloc(&d, bytes), "program alloc");
-        allocs_.push_back(d);
-        ck(cudaMemcpy(d, ops.data(), bytes, cudaMemcpyHostToDevice), "program upload");
-        p.d = d;
-        p.n = static_cast<int>(ops.size());
-    };
-    const std::vector<FramePhase> temporal = ops_temporal();
-    std::vector<FramePhase> casc_z, casc_dz, frame = temporal;
-    if (dep) {
-        TokenSrc prev{};
-        prev.tok = &fin_d_->prev_token;
-        ops_cascade(casc_z, z_, prev, true);
-        ops_cascade(casc_dz, dz_, prev, true);
-        if (has_text_head) {
-            TokenSrc tp{};
-            tp.pairs = tpairs_;
-            tp.n_pairs = text_head_.n_tiles;
-            ops_cascade(frame, z_, tp, true);
-        }
-    }
-    if (!fits(temporal) || !fits(casc_z) || !fits(casc_dz) || !fits(frame)) return;
-    ck(cudaMalloc(&fbar_, 2 * sizeof(unsigned)), "barrier alloc");
-    allocs_.push_back(fbar_);
-    upload(temporal, prog_temporal_);
-    if (dep) {
-        upload(casc_z, prog_cascade_z_);
-        upload(casc_dz, prog_cascade_dz_);
-        if (has_text_head) upload(frame, prog_frame_);
-    }
-    persistent_ = true;
-}
-
-void Engine::enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal) {
-    if (!p.d) throw std::runtime_error("internal: missing frame program");
-    ck(cudaMemsetAsync(fbar_, 0, 2 * sizeof(unsigned), s), "barrier reset");
-    FrameArgs fa{};
-    fa.prog = p.d;
-    fa.n_phases = p.n;
-    fa.bar = fbar_;
-    fa.abort = reinterpret_cast<int *>(fbar_ + 1);
-    fa.status = status_;
-    fa.rope = temporal ? rope_ : nullptr;
-    fa.rope_pairs = temporal ? head_dim / 2 : 0;
-    ck(launch_frame(fa, frame_grid_, s), "launch frame kernel");
 }
 
 cudaGraphExec_t Engine::capture(const std::function<void(cudaStream_t)> &fn) {
@@ -1125,12 +1065,7 @@ void Engine::run_temporal(const int32_t *tokens, int K, int pos) {
     fin_h_->n_tok = K;
     fin_h_->pos = pos;
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    if (persistent_) {
-        enqueue_embed(stream);
-        enqueue_program(stream, prog_temporal_, true);
-    } else {
-        launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
-    }
+    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
     ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
     if (has_text_head)
         ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
@@ -1161,7 +1096,7 @@ void Engine::run_layers(const float *x_in, int pos, int layer_begin, int layer_e
     launch(g_layers_, [this, layer_begin, layer_end](cudaStream_t s) {
         // RoPE table only (no embedding output)
         ck(launch_embed(ttables_d_, 0, fin_d_->tokens, nullptr, n_embd, nullptr, &fin_d_->pos, rope_theta, head_dim,
-                        rope_, s),
+                        rope_, ref_order_, s),
            "launch rope");
         for (int l = layer_begin; l < layer_end; ++l) enqueue_layer(s, l);
     });
@@ -1196,16 +1131,11 @@ void Engine::run_cascade_greedy(int32_t text_tok, const float *z, int32_t *out_t
     fin_h_->prev_token = text_tok;
     ck(cudaMemcpyAsync(dz_, zin_h_, sizeof(float) * n_embd, cudaMemcpyHostToDevice, stream), "z in copy");
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    if (persistent_) {
-        reset_depth_kv_async(stream);
-        enqueue_program(stream, prog_cascade_dz_, false);
-    } else {
-        launch(g_cascade_, [this](cudaStream_t s) {
-            TokenSrc t{};
-            t.tok = &fin_d_->prev_token;
-            enqueue_cascade(s, dz_, t);
-        });
-    }
+    launch(g_cascade_, [this](cudaStream_t s) {
+        TokenSrc t{};
+        t.tok = &fin_d_->prev_token;
+        enqueue_cascade(s, dz_, t);
+    });
     ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
     finish_call();
     for (int cb = 0; cb < dep_q; ++cb) out_tokens[cb] = tok_h_[1 + cb];
@@ -1218,19 +1148,13 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
     fin_h_->n_tok = K;
     fin_h_->pos = pos;
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    if (persistent_ && prog_frame_.d) {
-        enqueue_embed(stream);
-        reset_depth_kv_async(stream);
-        enqueue_program(stream, prog_frame_, true);
-    } else {
-        launch(g_frame_, [this](cudaStream_t s) {
-            enqueue_temporal(s);
-            TokenSrc t{};
-            t.pairs = tpairs_;
-            t.n_pairs = text_head_.n_tiles;
-            enqueue_cascade(s, z_, t);
-        });
-    }
+    launch(g_frame_, [this](cudaStream_t s) {
+        enqueue_temporal(s);
+        TokenSrc t{};
+        t.pairs = tpairs_;
+        t.n_pairs = text_head_.n_tiles;
+        enqueue_cascade(s, z_, t);
+    });
     ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
     ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
     ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
@@ -1243,19 +1167,13 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
 void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
-    if (persistent_ && prog_frame_.d) {
-        enqueue_embed(stream);
-        reset_depth_kv_async(stream);
-        enqueue_program(stream, prog_frame_, true);
-    } else {
-        launch(g_frame_, [this](cudaStream_t s) {
-            enqueue_temporal(s);
-            TokenSrc t{};
-            t.pairs = tpairs_;
-            t.n_pairs = text_head_.n_tiles;
-            enqueue_cascade(s, z_, t);
-        });
-    }
+    launch(g_frame_, [this](cudaStream_t s) {
+        enqueue_temporal(s);
+        TokenSrc t{};
+        t.pairs = tpairs_;
+        t.n_pairs = text_head_.n_tiles;
+        enqueue_cascade(s, z_, t);
+    });
     if (out_tokens_dev)
         ck(cudaMemcpyAsync(out_tokens_dev, tok_out_, sizeof(int) * (1 + dep_q), cudaMemcpyDeviceToDevice, stream),
            "tokens copy");
@@ -1264,27 +1182,17 @@ void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int
 void Engine::enqueue_temporal_device(const int32_t *tokens_dev, int K, int pos) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
-    if (persistent_) {
-        enqueue_embed(stream);
-        enqueue_program(stream, prog_temporal_, true);
-    } else {
-        launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
-    }
+    launch(g_temporal_, [this](cudaStream_t s) { enqueue_temporal(s); });
 }
 
 void Engine::enqueue_cascade_device(int32_t text_token) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_int(&fin_d_->prev_token, text_token, stream), "set token");
-    if (persistent_) {
-        reset_depth_kv_async(stream);
-        enqueue_program(stream, prog_cascade_z_, false);
-    } else {
-        launch(g_cascade_z_, [this](cudaStream_t s) {
-            TokenSrc t{};
-            t.tok = &fin_d_->prev_token;
-            enqueue_cascade(s, z_, t);
-        });
-    }
+    launch(g_cascade_z_, [this](cudaStream_t s) {
+        TokenSrc t{};
+        t.tok = &fin_d_->prev_token;
+        enqueue_cascade(s, z_, t);
+    });
 }
 
 int Engine::sync_status() {
@@ -1300,7 +1208,7 @@ void Engine::capture_all() {
         return;
     }
     auto temporal = [this](cudaStream_t s) { enqueue_temporal(s); };
-    if (!g_temporal_ && !persistent_) g_temporal_ = capture(temporal);
+    if (!g_temporal_) g_temporal_ = capture(temporal);
     if (has_dep_tables && dep_dim > 0) {
         for (int cb = 0; cb < dep_q; ++cb) {
             if (g_depth_[cb]) continue;
@@ -1311,13 +1219,13 @@ void Engine::capture_all() {
                 enqueue_depth_step(s, cb, dz_, t);
             });
         }
-        if (!g_cascade_ && !persistent_)
+        if (!g_cascade_)
             g_cascade_ = capture([this](cudaStream_t s) {
                 TokenSrc t{};
                 t.tok = &fin_d_->prev_token;
                 enqueue_cascade(s, dz_, t);
             });
-        if (!g_frame_ && has_text_head && !persistent_)
+        if (!g_frame_ && has_text_head)
             g_frame_ = capture([this](cudaStream_t s) {
                 enqueue_temporal(s);
                 TokenSrc t{};

@@ -7,9 +7,12 @@
 //   depth[cb]     one depformer step (reference bmo_forward_depth)
 //   cascade       dep_q depformer steps with greedy argmax chaining on device
 //   frame         temporal + greedy text token + cascade
-// Two execution paths run the same op lists: one kernel per op chained with
-// programmatic dependent launch inside CUDA graphs, or (default where the
-// model fits) the persistent frame kernel running the list as a program.
+// Each op list runs one kernel per op, chained with programmatic dependent
+// launch inside CUDA graphs.  Two summation orders exist for the GEMV and
+// the attention: the reference kernels' own fp32 order (default; bit-identical
+// to the reference's chain of kernels) and the exact-reduction order (double
+// sums rounded once; used by Q4_0 rings, tensor parallel and batched
+// sessions, whose arithmetic has no fp32 counterpart in the reference).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -36,7 +39,10 @@ struct EngineConfig {
     int kv_type = -1;  // < 0: BMO_KV_TYPE or fp16
     bool graphs = true;
     bool pdl = true;
-    bool persistent = false;  // run frames as one persistent kernel where the model allows
+    // -1: the reference kernels' fp32 order where the model and ring allow,
+    // else the exact-reduction order; 0: exact-reduction order; 1: the
+    // reference order or an error
+    int semantics = -1;
     // tensor parallel (batch-1 latency mode): tp_size >= 1 makes this engine
     // rank tp_rank of tp_size, holding the attention heads and FFN columns of
     // its shard; tp_id is the group's NCCL unique id
@@ -98,7 +104,7 @@ public:
     int debug_tap(int which, float *out, int max_floats);
     void capture_all();
     bool graphs_captured() const { return graphs_ready_; }
-    bool persistent() const { return persistent_; }
+    bool ref_order() const { return ref_order_; }
     bool tp_exchange() const { return tp_p2p_; }
 
     // ---- batched sessions: up to kBatchMax independent sessions stepped
@@ -144,8 +150,8 @@ private:
     void ops_layer(std::vector<FramePhase> &v, int l) const;
     void ops_text_head(std::vector<FramePhase> &v) const;
     std::vector<FramePhase> ops_temporal() const;
-    void ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok, bool fold) const;
-    void ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first, bool fold) const;
+    void ops_depth_step(std::vector<FramePhase> &v, int cb, const float *z, const TokenSrc &tok) const;
+    void ops_cascade(std::vector<FramePhase> &v, const float *z, const TokenSrc &first) const;
     // per-op path
     void enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops);
     void enqueue_embed(cudaStream_t s);
@@ -154,13 +160,7 @@ private:
     void enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok);
     void enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first);
     void reset_depth_kv_async(cudaStream_t s);
-    // persistent path
-    struct DevProgram {
-        FramePhase *d = nullptr;
-        int n = 0;
-    };
-    void build_programs();
-    void enqueue_program(cudaStream_t s, const DevProgram &p, bool temporal);
+    void choose_semantics(int want);
     // tensor parallel
     std::unique_ptr<TpComm> tp_comm_;
     double *tp_part_ = nullptr;  // partial sums of the split projections, summed over the ranks (NCCL path)
@@ -250,12 +250,8 @@ private:
     int g_layers_range_[2] = {-1, -1};
     bool graphs_ready_ = false;
 
-    // persistent frame kernel
-    bool persistent_ = false;
-    bool dep_fold_ = false;  // depformer attention fused into the O-projection GEMV
-    int frame_grid_ = 0;
-    unsigned *fbar_ = nullptr;  // [grid barrier counter, abort flag]
-    DevProgram prog_temporal_, prog_cascade_z_, prog_cascade_dz_, prog_frame_;
+    // summation order of the single-session path (see the header comment)
+    bool ref_order_ = false;
 };
 
 }  // namespace bmo

@@ -132,6 +132,36 @@ int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swi
     return static_cast<int>(launch_gemv(a, pro, epi, static_cast<int>(g), static_cast<cudaStream_t>(stream), false));
 }
 
+int bmo_k_gemv_q4_0_ref(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
+                        const float *gamma_dev, float eps, const float *resid_dev, float *y_dev, void *q8_out_dev,
+                        float *xn_out_dev, int *status_dev, void *stream) {
+    if (!tiled_dev || !x_dev || !y_dev || !shape_ok(rows, cols, perm, swiglu_f))
+        return static_cast<int>(cudaErrorInvalidValue);
+    if (cols / 32 > gemv_max_nbx() * kChunkBlocks || (gamma_dev && cols > gemv_ref_max_norm_cols()))
+        return static_cast<int>(cudaErrorInvalidValue);
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (reinterpret_cast<uintptr_t>(xn_out_dev) & 15))
+        return static_cast<int>(cudaErrorInvalidValue);
+    const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
+    GemvArgs a{};
+    a.W = m;
+    a.x = x_dev;
+    a.gamma = gamma_dev;
+    a.eps = eps;
+    a.xn_out = xn_out_dev;
+    a.q8_out = static_cast<uint8_t *>(q8_out_dev);
+    a.y = y_dev;
+    a.resid = resid_dev;
+    a.argmax_limit = INT_MAX;
+    a.status = status_dev;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int pro = gamma_dev ? kProNorm : kProPlain;
+    const int epi = perm == kPermSwiGLU ? kEpiSwiGLU : (resid_dev ? kEpiResid : kEpiStore);
+    return static_cast<int>(
+        launch_gemv_ref(a, pro, epi, gemv_ref_grid(m, sms), static_cast<cudaStream_t>(stream), false));
+}
+
 namespace {
 struct BatchScratch {
     size_t xq, xds, ws, cnt, status, total;
@@ -238,6 +268,37 @@ int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const float *
     a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
     a.out = out_dev;
     return static_cast<int>(launch_attention(a, head_dim, attn_splits_for(n_ctx), s, false));
+}
+
+int bmo_k_decode_attention_ref(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
+                               void *v_cache_dev, float *out_dev, int head_dim, int n_heads, int n_kv_heads, int n_ctx,
+                               const int *pos_dev, int layer, void *stream) {
+    if (!q_dev || !k_dev || !v_dev || !k_cache_dev || !v_cache_dev || !out_dev || !pos_dev)
+        return static_cast<int>(cudaErrorInvalidValue);
+    const bool split = n_ctx > 64;
+    if (!attn_ref_supported(head_dim, n_ctx, split) || n_kv_heads <= 0 || n_heads % n_kv_heads || layer < 0)
+        return static_cast<int>(cudaErrorInvalidValue);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const long long layer_off = static_cast<long long>(layer) * n_kv_heads * n_ctx * head_dim;
+    const int warps = 2 * n_kv_heads * head_dim / 32;
+    kv_append_kernel<<<(warps * 32 + 127) / 128, 128, 0, s>>>(k_dev, v_dev, k_cache_dev, v_cache_dev, nullptr, nullptr,
+                                                             n_kv_heads, head_dim, n_ctx, pos_dev, layer_off, kKvF16);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+    AttnArgs a{};
+    a.q = q_dev;
+    a.v_raw = v_dev;
+    a.k_cache = k_cache_dev;
+    a.v_cache = v_cache_dev;
+    a.kv_layer_off = layer_off;
+    a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.n_ctx = n_ctx;
+    a.kv_type = kKvF16;
+    a.pos = pos_dev;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.out = out_dev;
+    return static_cast<int>(launch_attention_ref(a, head_dim, split, s, false));
 }
 
 int bmo_k_tp_exchange(const double *const *parts, unsigned long long *const *flag_out,

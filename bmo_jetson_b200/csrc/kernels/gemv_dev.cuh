@@ -1,9 +1,9 @@
-// gemv_dev.cuh -- device pieces of the Q4_0 x Q8_1 GEMV shared by the
-// per-op kernel (gemv_q4.cu) and the persistent frame kernel (frame.cu):
-// the reference's per-half-block term, the 8-block chunk dot product, the
-// activation quantiser and the fused tile epilogues.  Activations and
-// residuals written earlier in the same launch by other CTAs are read with
-// L2-only loads (ld.global.cg).
+// gemv_dev.cuh -- device pieces of the Q4_0 x Q8_1 GEMV shared by its two
+// summation orders (gemv_q4.cu: exact double sums; gemv_ref.cu: the
+// reference kernel's own fp32 order): the reference's per-half-block term,
+// the 8-block chunk dot products, the activation quantiser and the fused tile
+// epilogues.  Activations and residuals written earlier in the same launch by
+// other CTAs are read with L2-only loads (ld.global.cg).
 #pragma once
 
 #include "common.cuh"
@@ -39,6 +39,34 @@ __device__ __forceinline__ double chunk_dot(const uint8_t *ch, const int8_t *xq,
         acc += static_cast<double>(half_term(hi, d4, ds));
     }
     return acc;
+}
+
+// The reference's accumulation of one 8-block chunk (32 rows, lane = row):
+// for each block and half block h, with sumi the half block's integer dot
+// product, acc[blk][h] = fma(d4, fma((float)sumi, d8, -4 s8), acc[blk][h]) --
+// bmo_gemv_q4_0_q8_1_kernel's `acc += d4 * ((float) sumi * ds8.x - 4.0f *
+// ds8.y)` (src/bmo_cuda_kernels.cu:648-651) as nvcc contracts it (measured
+// bit-exact against the reference kernel on B200).  xds holds (d8, 4 s8).
+__device__ __forceinline__ void chunk_acc_ref(const uint8_t *ch, const int8_t *xq, const float2 *xds, int lane,
+                                              float (&acc)[kChunkBlocks][2]) {
+#pragma unroll
+    for (int blk = 0; blk < kChunkBlocks; ++blk) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(ch + blk * 512 + lane * 16);
+        const float d4 = __half2float(*reinterpret_cast<const __half *>(ch + kChunkQsBytes + blk * 64 + lane * 2));
+        const int4 xa = *reinterpret_cast<const int4 *>(xq + blk * 32);
+        const int4 xb = *reinterpret_cast<const int4 *>(xq + blk * 32 + 16);
+        const float2 ds = xds[blk];
+        int lo = __dp4a(static_cast<int>(w.x & 0x0F0F0F0Fu), xa.x, 0);
+        lo = __dp4a(static_cast<int>((w.x >> 4) & 0x0F0F0F0Fu), xb.x, lo);
+        lo = __dp4a(static_cast<int>(w.y & 0x0F0F0F0Fu), xa.y, lo);
+        lo = __dp4a(static_cast<int>((w.y >> 4) & 0x0F0F0F0Fu), xb.y, lo);
+        int hi = __dp4a(static_cast<int>(w.z & 0x0F0F0F0Fu), xa.z, 0);
+        hi = __dp4a(static_cast<int>((w.z >> 4) & 0x0F0F0F0Fu), xb.z, hi);
+        hi = __dp4a(static_cast<int>(w.w & 0x0F0F0F0Fu), xa.w, hi);
+        hi = __dp4a(static_cast<int>((w.w >> 4) & 0x0F0F0F0Fu), xb.w, hi);
+        acc[blk][0] = __fmaf_rn(d4, __fmaf_rn(static_cast<float>(lo), ds.x, -ds.y), acc[blk][0]);
+        acc[blk][1] = __fmaf_rn(d4, __fmaf_rn(static_cast<float>(hi), ds.x, -ds.y), acc[blk][1]);
+    }
 }
 
 // ---- embedding element fetch (ggml to_float for the supported types) ----
@@ -165,7 +193,10 @@ __device__ __forceinline__ void quantize_x_block(const GemvArgs &a, int8_t *xq, 
     }
 }
 
-template <int EPI>
+// REF: the reference's own fp32 forms (SwiGLU with __expf, RoPE with the
+// products fused as nvcc fuses rope_interleaved_kernel's); otherwise the
+// exact-reduction forms (transcendentals in double, every product rounded).
+template <int EPI, bool REF = false>
 __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane, float v, int tok,
                                               const float2 *rope_cs) {
     const int r = t * kTileRows + lane;
@@ -174,12 +205,12 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
     } else if constexpr (EPI == kEpiResid) {
         if (r < a.W.rows) a.y[r] = __fadd_rn(__ldcg(a.resid + r), v);
     } else if constexpr (EPI == kEpiSwiGLU) {
-        // silu(gate) * up (swiglu_split_kernel, bmo_cuda_kernels.cu:370-387),
-        // exp evaluated in double and rounded once
+        // silu(gate) * up (swiglu_split_kernel, bmo_cuda_kernels.cu:370-387);
+        // exact form: exp evaluated in double and rounded once
         const float up = __shfl_down_sync(0xffffffffu, v, 16);
         const int h = t * 16 + lane;
         if (lane < 16 && h < a.W.swiglu_f) {
-            const float e = __double2float_rn(exp(-static_cast<double>(v)));
+            const float e = REF ? __expf(-v) : __double2float_rn(exp(-static_cast<double>(v)));
             const float silu = __fdiv_rn(v, __fadd_rn(1.0f, e));
             a.y[h] = __fmul_rn(silu, up);
         }
@@ -210,12 +241,19 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
         const bool is_q = r < a.q_dim;
         const bool is_k = !is_q && r < a.q_dim + a.kv_dim;
         if ((is_q || is_k) && rope_cs) {
-            // interleaved RoPE (rope_interleaved_kernel, :317-368), separately rounded
+            // interleaved RoPE (rope_interleaved_kernel, :317-368): even lane
+            // real part xr, odd lane imaginary part xi.  REF: y_r = fma(xr, c,
+            // -(xi s)), y_i = fma(xr, s, xi c) (the reference's contraction);
+            // exact form: every product rounded
             const int d = (is_q ? r : r - a.q_dim) % hd;
             const float2 cs = rope_cs[d >> 1];
             const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-            out = (lane & 1) ? __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x))
-                             : __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
+            if constexpr (REF)
+                out = (lane & 1) ? __fmaf_rn(partner, cs.y, __fmul_rn(v, cs.x))
+                                 : __fmaf_rn(v, cs.x, -__fmul_rn(partner, cs.y));
+            else
+                out = (lane & 1) ? __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x))
+                                 : __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
         }
         if (is_q) {
             a.y[r] = out;
@@ -234,113 +272,6 @@ __device__ __forceinline__ void tile_epilogue(const GemvArgs &a, int t, int lane
             uint8_t *qs = static_cast<uint8_t *>(cache) + e0 / 2;
             __half *dp = reinterpret_cast<__half *>(is_k ? a.k_scale : a.v_scale) + e0 / 32;
             warp_store_q4_0(out, lane, qs, dp);
-        }
-    }
-}
-
-// ---- depformer attention of every head (kProDepAttn prologue) ----
-// Same semantics as attn_kernel: s = fl(fl(q.k in double) * scale), M = max s,
-// p = fl(exp(s - M) in double), out = fl(sum p v / sum p) with the sums in
-// double; a window of one returns the raw fp32 v.  One warp per head, lanes
-// split head_dim, the window (<= MAXWIN rows) held in registers; warps
-// [0, NWARPS) take part, each taking kHpw heads at a time whose q, K and V
-// loads are all issued before any arithmetic (one memory round trip), and the
-// window's dot products reduced across lanes together (independent shuffle
-// chains); the output goes to xout[n_heads * HD].
-template <int NWARPS, int HD, int MAXWIN>
-__device__ void dep_attention_block(const AttnArgs &at, float *xout) {
-    constexpr int kP = HD / 64;  // half2 pairs per lane per row
-    constexpr int kHpw = 2;      // heads per warp in flight
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = *at.pos;
-    const int window = pos + 1 > at.n_ctx ? at.n_ctx : pos + 1;
-    const int start = pos + 1 - window;
-    const __half2 *kc = static_cast<const __half2 *>(at.k_cache);
-    const __half2 *vc = static_cast<const __half2 *>(at.v_cache);
-    for (int hb = warp; hb < at.n_heads; hb += NWARPS * kHpw) {
-        float2 q[kHpw][kP];
-        __half2 kk[kHpw][MAXWIN][kP], vv[kHpw][MAXWIN][kP];
-        float rawv[kHpw][HD / 32];
-#pragma unroll
-        for (int u = 0; u < kHpw; ++u) {
-            const int h = hb + u * NWARPS;
-            const bool on = h < at.n_heads;
-            const int kh = at.n_kv_heads == at.n_heads ? h : h / (at.n_heads / at.n_kv_heads);
-            if (window == 1) {
-#pragma unroll
-                for (int i = 0; i < HD / 32; ++i) rawv[u][i] = on ? __ldcg(at.v_raw + kh * HD + lane + 32 * i) : 0.0f;
-                continue;
-            }
-            const long long head_row0 = at.kv_layer_off / HD + static_cast<long long>(kh) * at.n_ctx;
-#pragma unroll
-            for (int i = 0; i < kP; ++i)
-                q[u][i] = on ? __ldcg(reinterpret_cast<const float2 *>(at.q + h * HD) + lane + 32 * i) : make_float2(0.0f, 0.0f);
-#pragma unroll
-            for (int j = 0; j < MAXWIN; ++j) {
-                const bool in = on && j < window;
-                const long long row = head_row0 + (start + j) % at.n_ctx;
-#pragma unroll
-                for (int i = 0; i < kP; ++i) {
-                    const long long e2 = (row * HD) / 2 + lane + 32 * i;
-                    kk[u][j][i] = in ? __ldcg(kc + e2) : __floats2half2_rn(0.0f, 0.0f);
-                    vv[u][j][i] = in ? __ldcg(vc + e2) : __floats2half2_rn(0.0f, 0.0f);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kHpw; ++u) {
-            const int h = hb + u * NWARPS;
-            if (h >= at.n_heads) continue;
-            float *x = xout + h * HD;
-            if (window == 1) {
-#pragma unroll
-                for (int i = 0; i < HD / 32; ++i) x[lane + 32 * i] = rawv[u][i];
-                continue;
-            }
-            double dot[MAXWIN];
-#pragma unroll
-            for (int j = 0; j < MAXWIN; ++j) {
-                dot[j] = 0.0;
-#pragma unroll
-                for (int i = 0; i < kP; ++i) {
-                    const float2 kf = __half22float2(kk[u][j][i]);
-                    dot[j] = fma(static_cast<double>(q[u][i].x), static_cast<double>(kf.x), dot[j]);
-                    dot[j] = fma(static_cast<double>(q[u][i].y), static_cast<double>(kf.y), dot[j]);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int j = 0; j < MAXWIN; ++j) dot[j] += __shfl_xor_sync(0xffffffffu, dot[j], o);
-            float my_s = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < MAXWIN; ++j)
-                if (lane == j && j < window) my_s = __fmul_rn(__double2float_rn(dot[j]), at.scale);
-            const float M = warp_max(my_s);
-            const float p = lane < window ? __double2float_rn(exp(static_cast<double>(__fsub_rn(my_s, M)))) : 0.0f;
-            double l = static_cast<double>(p);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            double ox[kP], oy[kP];
-#pragma unroll
-            for (int i = 0; i < kP; ++i) ox[i] = oy[i] = 0.0;
-#pragma unroll
-            for (int j = 0; j < MAXWIN; ++j) {
-                const double pj = static_cast<double>(__shfl_sync(0xffffffffu, p, j));
-                if (j < window) {
-#pragma unroll
-                    for (int i = 0; i < kP; ++i) {
-                        const float2 vf = __half22float2(vv[u][j][i]);
-                        ox[i] = fma(pj, static_cast<double>(vf.x), ox[i]);
-                        oy[i] = fma(pj, static_cast<double>(vf.y), oy[i]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kP; ++i) {
-                x[2 * (lane + 32 * i)] = __double2float_rn(__ddiv_rn(ox[i], l));
-                x[2 * (lane + 32 * i) + 1] = __double2float_rn(__ddiv_rn(oy[i], l));
-            }
         }
     }
 }

@@ -45,9 +45,6 @@ constexpr int kMaxNormCols = kMaxTilesPerCta * kWarps * 32 * 2;  // RMSNorm weig
 // A cross-CTA combine (partial store, release, acquire, reload) costs about as
 // long as one SM streaming this many chunks.
 constexpr int kCombineChunks = 12;
-// kProDepAttn: head size and longest window (the window is held in registers)
-constexpr int kDepAttnHd = 64;
-constexpr int kDepAttnMaxWin = 8;
 
 // Kept under half of an SM's shared memory so that the next kernel's CTA fits
 // beside this one under programmatic dependent launch and prefetches its weights.
@@ -71,8 +68,6 @@ size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
 int gemv_max_tiles_per_cta() { return kMaxTilesPerCta; }
 int gemv_max_nbx() { return kMaxNbx; }
 int gemv_max_norm_cols() { return kMaxNormCols; }
-int gemv_dep_attn_max_window() { return kDepAttnMaxWin; }
-int gemv_dep_attn_head_dim() { return kDepAttnHd; }
 
 __device__ __forceinline__ int cta_of_chunk(long long k, long long nc, int g) {
     return static_cast<int>(((k + 1) * g - 1) / nc);
@@ -128,16 +123,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_kernel(const __grid_const
     // other memory access so that the activation costs one round trip.
     float v0[32], v1[32];
     const bool h0 = tid < nb, h1 = tid + kThreads < nb;
-    if constexpr (PRO == kProDepAttn) {
-        // the depformer attention of every head is the activation (n_heads * 64 <= kMaxNormCols)
-        dep_attention_block<kWarps, kDepAttnHd, kDepAttnMaxWin>(a.att, S.gamma);
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v0[j] = h0 ? S.gamma[tid * 32 + j] : 0.0f;
-    } else {
-        if (h0) load_block32(a.x + tid * 32, v0);
-        if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
-    }
+    if (h0) load_block32(a.x + tid * 32, v0);
+    if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
     int tok = -1;
     if constexpr (EPI == kEpiEmbAdd) {
         tok = resolve_token<kThreads>(a.tok, S.tok_v, S.tok_i, [] { __syncthreads(); });
@@ -280,7 +267,6 @@ static cudaError_t configure_one() {
 
 #define BMO_GEMV_VARIANTS(X)  \
     X(kProNorm, kEpiQKV)      \
-    X(kProDepAttn, kEpiResid) \
     X(kProPlain, kEpiResid)   \
     X(kProNorm, kEpiSwiGLU)   \
     X(kProNorm, kEpiLogits)   \
@@ -323,12 +309,7 @@ GemvPlan plan_gemv(const QMatDesc &m, int sms) {
 cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl) {
     if (a.W.nbx > kMaxNbx || grid <= 0 || a.W.cpt <= 0 || a.W.n_tiles <= 0) return cudaErrorInvalidValue;
     if (prologue == kProNorm && a.W.cols > kMaxNormCols) return cudaErrorInvalidValue;
-    if (prologue == kProDepAttn &&
-        (a.att.n_ctx > kDepAttnMaxWin || a.att.n_ctx <= 0 || a.att.n_heads <= 0 || a.att.n_kv_heads <= 0 ||
-         a.att.n_heads % a.att.n_kv_heads || a.att.n_heads * kDepAttnHd != a.W.cols || a.W.cols > kMaxNormCols ||
-         a.att.kv_type != kKvF16))
-        return cudaErrorInvalidValue;
-    if (prologue != kProDepAttn && (reinterpret_cast<uintptr_t>(a.x) & 15)) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(a.x) & 15) return cudaErrorInvalidValue;
     // every CTA's tile range must fit the shared partial table
     const long long nc = static_cast<long long>(a.W.n_tiles) * a.W.cpt;
     if (a.tile_aligned) {

@@ -1,0 +1,308 @@
+// gemv_ref.cu -- batch-1 Q4_0 x Q8_1 GEMV computing every output row with
+// the reference kernel's own fp32 operations in the reference's own order,
+// so that its results are bit-identical to bmo_gemv_q4_0_q8_1_kernel
+// (src/bmo_cuda_kernels.cu:560-683) on the same weights and activation.
+//
+// The reference's order.  A warp owns a row; lane l takes half block
+// h = l % 2 of the blocks whose index within each group of 16 is m = l / 2.
+// Its accumulator j (0..3) chains, in increasing order, the blocks
+// 64 i + 16 j + m of the main loop; blocks past the last whole group of 64
+// (the tail, in steps of 16) continue accumulator 0.  Each block adds
+// acc = fma(d4, fma((float)sumi, d8, -4 s8), acc).  The lane's value is
+// ((acc0 + acc1) + acc2) + acc3 and the row is the __shfl_down_sync tree of
+// the 32 lane values.  So one row is 128 independent fp32 chains ("keys":
+// block position within 64 x half block) joined by a fixed tree.
+//
+// B200 design.  The weights keep the engine's tiled layout (32 rows x
+// 8-block chunks, one 4608-byte bulk copy each).  A chunk's 8 blocks share
+// one key group G = 2 j + m / 8: main chunk c (tile-local) has G = c % 8 and
+// chain position c / 8; tail chunk c = nm + t has G = t % 2 (j = 0) and
+// position nm / 8 + t / 2.  So warp w of a CTA owns key group w of every
+// tile of the CTA, streams exactly that group's chunks in chain order
+// through a private TMA ring, and keeps the 16 chains of each row (8 blocks
+// x 2 half blocks) in registers -- no chain ever crosses a warp.  After a
+// tile, each warp leaves its 16 chain values per row in shared memory and a
+// combiner warp (rotating with the tile) adds them in the reference's lane
+// order, runs the 32-leaf tree in registers (lane = row) and applies the
+// fused epilogue.  Two named barriers hand the shared buffer over: the
+// combiner waits until all warps have written ("full"); the writers of the
+// next tile wait until the combiner has read ("empty"), which it signals
+// before its tree and epilogue.  Each CTA owns whole tiles (the chains must
+// not be split), one CTA per SM at most, sized (registers <= 128, shared
+// memory < half an SM) so the next kernel's CTA fits beside it.
+//
+// The prologue is the RMSNorm of rmsnorm_kernel (:244-295) in its own order
+// -- thread t of 256 sums x[t + 256 k]^2 with fma, a shfl_down tree per warp,
+// the 8 warp sums by the tree ((w0+w4)+(w2+w6))+((w1+w5)+(w3+w7)), scale =
+// rsqrtf(total / n + eps), y = (x * scale) * gamma -- then the Q8_1
+// quantiser of :529-558, bit-exact.
+#include <algorithm>
+
+#include "gemv_dev.cuh"
+#include "../launch.h"
+
+namespace bmo {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRing = 2;                  // chunks in flight per warp
+constexpr int kMaxNbx = 384;              // activations up to 12288 elements
+constexpr int kMaxNormCols = 4096;        // RMSNorm weight staged in the chain buffer's space
+constexpr int kNormLoads = kMaxNormCols / kThreads;  // strided elements per thread
+constexpr int kBarFull = 1, kBarEmpty = 2;  // named barrier ids (0 is __syncthreads)
+
+struct GemvRefSmem {
+    uint64_t bar[kWarps][kRing];
+    uint64_t gbar;  // RMSNorm weight bulk copy
+    alignas(128) uint8_t ring[kWarps][kRing][kChunkBytes];
+    alignas(16) int8_t xq[kMaxNbx * 32];
+    float2 xds[kMaxNbx];  // (d8, 4 * s8) of each Q8_1 block
+    union {
+        float part[kWarps][2 * kChunkBlocks][32];  // [key group][block * 2 + half][row]: one tile's chains
+        float gamma[kMaxNormCols];                 // prologue only
+    };
+    float red[kWarps];
+    float tok_v[kWarps];
+    int tok_i[kWarps];
+    int err;
+};
+
+// Chunks of a tile in the reference's key order (see the header comment).
+struct KeyChains {
+    int nm;     // main chunks per tile: 8 * (blocks / 64)
+    int nmg;    // main chunks per key group
+    int ntail;  // tail chunks per tile (the last may hold padding blocks)
+    __device__ int len(int g) const { return nmg + ((g < 2 && ntail > g) ? (ntail - g + 1) / 2 : 0); }
+    __device__ int chunk(int g, int p) const { return p < nmg ? g + 8 * p : nm + g + 2 * (p - nmg); }
+};
+
+__device__ __forceinline__ void named_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ float shfl_down_tree(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    GemvRefSmem &S = *reinterpret_cast<GemvRefSmem *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int cpt = a.W.cpt;
+    const int t0 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * c / G);
+    const int t1 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * (c + 1) / G);
+    const int nb = a.W.cols / 32, nbx = a.W.nbx;
+    KeyChains kc;
+    kc.nmg = nb / 64;
+    kc.nm = 8 * kc.nmg;
+    kc.ntail = cpt - kc.nm;
+    const int my_len = kc.len(warp);
+    const int n_mine = my_len * (t1 - t0);
+    const bool gbulk = PRO == kProNorm && (reinterpret_cast<uintptr_t>(a.gamma) & 15) == 0;
+
+    if (tid < kWarps * kRing) mbar_init(&S.bar[tid / kRing][tid % kRing], 1);
+    if (tid == kWarps * kRing) mbar_init(&S.gbar, 1);
+    if (tid == 0) S.err = 0;
+    fence_barrier_init();
+    __syncthreads();
+
+    // Weights never depend on earlier kernels: start streaming them now.
+    const uint64_t pol = l2_evict_first_policy();
+    auto issue = [&](int i) {
+        const int tile = t0 + i / my_len;
+        const long long k = static_cast<long long>(tile) * cpt + kc.chunk(warp, i % my_len);
+        uint64_t *bar = &S.bar[warp][i % kRing];
+        mbar_arrive_expect_tx(bar, kChunkBytes);
+        bulk_load(S.ring[warp][i % kRing], a.W.tiles + k * kChunkBytes, kChunkBytes, bar, pol);
+    };
+    if (lane == 0)
+        for (int i = 0; i < kRing && i < n_mine; ++i) issue(i);
+    if (gbulk && tid == 0) {
+        const uint32_t gb = static_cast<uint32_t>(a.W.cols) * 4u;
+        mbar_arrive_expect_tx(&S.gbar, gb);
+        bulk_load(S.gamma, a.gamma, gb, &S.gbar, l2_evict_last_policy());
+    }
+
+    pdl_wait();
+
+    // ---- prologue: activation -> Q8_1 blocks in shared memory ----
+    // Thread t quantises blocks t and t + kThreads; for the RMSNorm it also
+    // loads x[t + 256 k], its share of the reference's sum of squares.  All
+    // loads are issued before any arithmetic (one memory round trip).
+    float v0[32], v1[32];
+    const bool h0 = tid < nb, h1 = tid + kThreads < nb;
+    if (h0) load_block32(a.x + tid * 32, v0);
+    if (h1) load_block32(a.x + (tid + kThreads) * 32, v1);
+    float xs[kNormLoads];
+    if constexpr (PRO == kProNorm) {
+#pragma unroll
+        for (int k = 0; k < kNormLoads; ++k) {
+            const int i = tid + k * kThreads;
+            xs[k] = i < a.W.cols ? __ldcg(a.x + i) : 0.0f;
+        }
+    }
+    int tok = -1;
+    if constexpr (EPI == kEpiEmbAdd) {
+        tok = resolve_token<kThreads>(a.tok, S.tok_v, S.tok_i, [] { __syncthreads(); });
+        if (c == 0 && tid == 0 && a.tok.tok_out) *a.tok.tok_out = tok;
+    }
+    float scale = 1.0f;
+    const float *gam = a.gamma;
+    if constexpr (PRO == kProNorm) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kNormLoads; ++k)
+            if (tid + k * kThreads < a.W.cols) ss = __fmaf_rn(xs[k], xs[k], ss);
+        ss = shfl_down_tree(ss);
+        if (lane == 0) S.red[warp] = ss;
+        __syncthreads();
+        const float total = __fadd_rn(__fadd_rn(__fadd_rn(S.red[0], S.red[4]), __fadd_rn(S.red[2], S.red[6])),
+                                      __fadd_rn(__fadd_rn(S.red[1], S.red[5]), __fadd_rn(S.red[3], S.red[7])));
+        scale = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(a.W.cols)), a.eps));
+        if (gbulk) {
+            if (!mbar_wait(&S.gbar, 0)) atomicOr(&S.err, 1);
+            gam = S.gamma;
+        }
+    }
+    if (tid < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid, h0, v0, scale, gam, c == 0);
+    if (tid + kThreads < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid + kThreads, h1, v1, scale, gam, c == 0);
+    __syncthreads();  // also ends the prologue's use of S.gamma, which S.part overlays
+
+    // ---- main loop: each tile's key-group chains, then the combine ----
+    int i = 0;           // chunks of this warp passed through
+    int issued = n_mine < kRing ? n_mine : kRing;
+    int first_bad = n_mine;  // first chunk whose wait gave up
+    bool bad = false;
+    for (int tt = 0; tt < t1 - t0; ++tt) {
+        float acc[kChunkBlocks][2];
+#pragma unroll
+        for (int b = 0; b < kChunkBlocks; ++b) acc[b][0] = acc[b][1] = 0.0f;
+        for (int p = 0; p < my_len; ++p, ++i) {
+            if (!bad && !mbar_wait(&S.bar[warp][i % kRing], (i / kRing) & 1)) {
+                bad = true;
+                first_bad = i;
+                if (lane == 0) atomicOr(&S.err, 1);
+            }
+            if (!bad) {
+                const int ch = kc.chunk(warp, p);
+                chunk_acc_ref(S.ring[warp][i % kRing], S.xq + ch * kChunkBlocks * 32, S.xds + ch * kChunkBlocks,
+                              lane, acc);
+            }
+            __syncwarp();
+            if (!bad && i + kRing < n_mine) {
+                if (lane == 0) {
+                    fence_proxy_async();
+                    issue(i + kRing);
+                }
+                ++issued;
+            }
+        }
+        // hand the tile's chains to the combiner warp
+        const int comb = tt % kWarps;
+        if (tt > 0 && warp != (tt - 1) % kWarps) named_sync(kBarEmpty, kThreads);
+#pragma unroll
+        for (int b = 0; b < kChunkBlocks; ++b) {
+            S.part[warp][2 * b][lane] = acc[b][0];
+            S.part[warp][2 * b + 1][lane] = acc[b][1];
+        }
+        if (warp != comb) {
+            named_arrive(kBarFull, kThreads);
+            continue;
+        }
+        named_sync(kBarFull, kThreads);
+        // lane value L[2m + h] = ((A0 + A1) + A2) + A3, A_j from key group 2j + m/8
+        float L[32];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int kk = 2 * (m & 7) + h, mh = m >> 3;
+                float s = __fadd_rn(S.part[mh][kk][lane], S.part[2 + mh][kk][lane]);
+                s = __fadd_rn(s, S.part[4 + mh][kk][lane]);
+                L[2 * m + h] = __fadd_rn(s, S.part[6 + mh][kk][lane]);
+            }
+        }
+        if (tt + 1 < t1 - t0) named_arrive(kBarEmpty, kThreads);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int q = 0; q < o; ++q) L[q] = __fadd_rn(L[q], L[q + o]);
+        if (!bad && !S.err) tile_epilogue<EPI, true>(a, t0 + tt, lane, L[0], tok, a.rope_cs);
+    }
+    // The next kernel may start: its weight prefetch overlaps this kernel's tail.
+    pdl_launch_dependents();
+    if (bad) {  // let this warp's copies in flight land before the CTA exits
+        for (int j = first_bad; j < issued; ++j) mbar_wait(&S.bar[warp][j % kRing], (j / kRing) & 1);
+    }
+    __syncthreads();
+    if (S.err && tid == 0) raise_error(a.status, kErrTmaTimeout);
+}
+
+// ---------------------------------------------------------------------------
+// launch
+// ---------------------------------------------------------------------------
+template <int PRO, int EPI>
+static cudaError_t launch_ref_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = sizeof(GemvRefSmem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_ref_kernel<PRO, EPI>, a);
+}
+
+#define BMO_GEMV_REF_VARIANTS(X) \
+    X(kProNorm, kEpiQKV)         \
+    X(kProPlain, kEpiResid)      \
+    X(kProNorm, kEpiSwiGLU)      \
+    X(kProNorm, kEpiLogits)      \
+    X(kProPlain, kEpiLogits)     \
+    X(kProPlain, kEpiEmbAdd)     \
+    X(kProPlain, kEpiStore)      \
+    X(kProNorm, kEpiStore)       \
+    X(kProPlain, kEpiSwiGLU)     \
+    X(kProNorm, kEpiResid)
+
+cudaError_t configure_gemv_ref() {
+    cudaError_t e = cudaSuccess;
+#define BMO_GEMV_REF_CFG(P, E)                                                                              \
+    if ((e = cudaFuncSetAttribute(gemv_ref_kernel<P, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                  static_cast<int>(sizeof(GemvRefSmem)))) != cudaSuccess)                   \
+        return e;
+    BMO_GEMV_REF_VARIANTS(BMO_GEMV_REF_CFG)
+#undef BMO_GEMV_REF_CFG
+    return e;
+}
+
+size_t gemv_ref_smem_bytes() { return sizeof(GemvRefSmem); }
+int gemv_ref_max_norm_cols() { return kMaxNormCols; }
+
+int gemv_ref_grid(const QMatDesc &m, int sms) { return std::max(1, std::min(m.n_tiles, sms)); }
+
+cudaError_t launch_gemv_ref(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl) {
+    if (a.W.nbx > kMaxNbx || grid <= 0 || grid > a.W.n_tiles || a.W.cpt <= 0 || a.W.n_tiles <= 0 ||
+        a.W.cols % 32 || a.W.nbx != a.W.cpt * kChunkBlocks || a.W.nbx < a.W.cols / 32)
+        return cudaErrorInvalidValue;
+    if (prologue == kProNorm && a.W.cols > kMaxNormCols) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(a.x) & 15) return cudaErrorInvalidValue;
+#define BMO_GEMV_REF_CASE(P, E) \
+    if (prologue == P && epilogue == E) return launch_ref_t<P, E>(a, grid, s, pdl);
+    BMO_GEMV_REF_VARIANTS(BMO_GEMV_REF_CASE)
+#undef BMO_GEMV_REF_CASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace bmo

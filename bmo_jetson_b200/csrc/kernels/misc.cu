@@ -10,9 +10,12 @@ namespace bmo {
 // channels added in order, a channel skipped when its token is negative or
 // out of range or its table has the wrong width.  Block 0 also builds the
 // RoPE (cos, sin) table of this position, inv_freq = theta^(-2i/hd) and
-// angle = pos * inv_freq in fp32 as in rope_interleaved_kernel (:317-368).
+// angle = pos * inv_freq in fp32 as in rope_interleaved_kernel (:317-368);
+// ref: the power and the trigonometry by the reference's own intrinsics
+// (__powf, __sincosf), else evaluated in double and rounded once.
 __global__ void embed_kernel(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev,
-                             int n_embd, float *out, const int *pos, float theta, int head_dim, float2 *rope_cs) {
+                             int n_embd, float *out, const int *pos, float theta, int head_dim, float2 *rope_cs,
+                             int ref) {
     pdl_launch_dependents();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int n_tok = n_tok_dev ? *n_tok_dev : 0;
@@ -48,24 +51,31 @@ __global__ void embed_kernel(const EmbTable *tables, int n_tables, const int *to
         out[i] = acc;
     }
     if (blockIdx.x == 0 && rope_cs && threadIdx.x < head_dim / 2) {
-        // exponent and angle in fp32 as the reference; the power and the
-        // trig evaluated in double and rounded once (exact-reduction semantics)
         const int k = threadIdx.x;
         const float exponent = __fdiv_rn(static_cast<float>(2 * k), static_cast<float>(head_dim));
-        const float inv_freq = __double2float_rn(pow(static_cast<double>(theta), -static_cast<double>(exponent)));
-        const float angle = __fmul_rn(static_cast<float>(*pos), inv_freq);
-        double sn, cs;
-        sincos(static_cast<double>(angle), &sn, &cs);
-        rope_cs[k] = make_float2(__double2float_rn(cs), __double2float_rn(sn));
+        if (ref) {
+            const float inv_freq = __powf(theta, -exponent);
+            const float angle = __fmul_rn(static_cast<float>(*pos), inv_freq);
+            float sn, cs;
+            __sincosf(angle, &sn, &cs);
+            rope_cs[k] = make_float2(cs, sn);
+        } else {
+            const float inv_freq = __double2float_rn(pow(static_cast<double>(theta), -static_cast<double>(exponent)));
+            const float angle = __fmul_rn(static_cast<float>(*pos), inv_freq);
+            double sn, cs;
+            sincos(static_cast<double>(angle), &sn, &cs);
+            rope_cs[k] = make_float2(__double2float_rn(cs), __double2float_rn(sn));
+        }
     }
 }
 
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,
-                         float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, cudaStream_t s) {
+                         float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, bool ref,
+                         cudaStream_t s) {
     const int threads = 256;
     const int blocks = (n_embd + threads - 1) / threads;
     embed_kernel<<<blocks, threads, 0, s>>>(tables, n_tables, tokens, n_tok_dev, n_embd, out, pos, theta, head_dim,
-                                            rope_cs);
+                                            rope_cs, ref ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -134,13 +144,17 @@ cudaError_t launch_tp_resid(const double *part, const float *resid, float *y, in
 }
 
 cudaError_t configure_gemv();
+cudaError_t configure_gemv_ref();
 cudaError_t configure_attention();
+cudaError_t configure_attention_ref();
 cudaError_t configure_batch();
 cudaError_t configure_batch_mma();
 
 cudaError_t configure_kernels() {
     cudaError_t e = configure_gemv();
+    if (e == cudaSuccess) e = configure_gemv_ref();
     if (e == cudaSuccess) e = configure_attention();
+    if (e == cudaSuccess) e = configure_attention_ref();
     if (e == cudaSuccess) e = configure_batch();
     return e != cudaSuccess ? e : configure_batch_mma();
 }

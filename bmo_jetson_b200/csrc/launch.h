@@ -8,16 +8,19 @@
 
 namespace bmo {
 
-// GEMV (kernels/gemv_q4.cu).  `grid` CTAs split the (tile, chunk) units;
-// `pdl` enables programmatic dependent launch on the stream.
+// GEMV, exact-reduction order (kernels/gemv_q4.cu).  `grid` CTAs split the
+// (tile, chunk) units; `pdl` enables programmatic dependent launch on the stream.
 cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl);
 size_t gemv_smem_bytes();
 int gemv_max_tiles_per_cta();
 int gemv_max_nbx();
 int gemv_max_norm_cols();
-// kProDepAttn limits: longest ring window and head size
-int gemv_dep_attn_max_window();
-int gemv_dep_attn_head_dim();
+// GEMV in the reference kernel's fp32 order (kernels/gemv_ref.cu): `grid`
+// CTAs (at most the tile count, gemv_ref_grid) each own whole row tiles.
+cudaError_t launch_gemv_ref(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl);
+int gemv_ref_grid(const QMatDesc &m, int sms);
+size_t gemv_ref_smem_bytes();
+int gemv_ref_max_norm_cols();
 // Grid and split for a matrix on a device with `sms` SMs: whole row tiles per
 // CTA unless that leaves the busiest CTA much more work than an even split.
 struct GemvPlan {
@@ -31,27 +34,12 @@ GemvPlan plan_gemv(const QMatDesc &m, int sms);
 cudaError_t launch_attention(const AttnArgs &a, int head_dim, int splits, cudaStream_t s, bool pdl, int n_sess = 1);
 int attn_splits_for(int n_ctx);
 int attn_max_ctx();
-
-// Persistent frame kernel (kernels/frame.cu): runs `n_phases` FramePhase
-// steps with one CTA per SM (cooperative launch) and a grid barrier between
-// steps.  `bar` and `abort` are zero at launch.
-struct FrameArgs {
-    const FramePhase *prog;  // device
-    int n_phases;
-    unsigned *bar;
-    int *abort;
-    int *status;
-    const float2 *rope;      // this frame's RoPE table (device), copied into shared memory
-    int rope_pairs;
-};
-cudaError_t launch_frame(const FrameArgs &fa, int grid, cudaStream_t s);
-// SMs the frame kernel can cover (0: it cannot be resident on this device).
-int frame_max_grid();
-size_t frame_smem_bytes();
-int frame_max_window();
-int frame_max_tiles_per_cta();
-int frame_dep_max_window();
-int frame_dep_head_dim();
+// Decode attention over an fp16 ring in the reference kernel's fp32 order
+// (kernels/attention_ref.cu): split = a cluster of 8 CTAs per head (rings up
+// to 1024 slots), else one CTA per head (rings up to 64 slots).
+cudaError_t launch_attention_ref(const AttnArgs &a, int head_dim, bool split, cudaStream_t s, bool pdl);
+bool attn_ref_supported(int head_dim, int n_ctx, bool split);
+int attn_ref_max_ctx();
 
 // Batched sessions (kernels/batch.cu).  Stage: per-session RMSNorm + Q8_1
 // into the block-major layout (and the embedding token); GEMM: the skinny
@@ -87,9 +75,11 @@ cudaError_t launch_batch_finalize(const float2 *pairs, int pairs_stride, int n_p
 cudaError_t launch_tp_resid(const double *part, const float *resid, float *y, int n, cudaStream_t s);
 cudaError_t launch_tp_exchange(const TpExchangeArgs &a, cudaStream_t s, bool pdl);
 
-// Frame-start embedding sum + RoPE table (kernels/misc.cu).
+// Frame-start embedding sum + RoPE table (kernels/misc.cu); ref: the table
+// by the reference's intrinsics (__powf, __sincosf).
 cudaError_t launch_embed(const EmbTable *tables, int n_tables, const int *tokens, const int *n_tok_dev, int n_embd,
-                         float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, cudaStream_t s);
+                         float *out, const int *pos, float theta, int head_dim, float2 *rope_cs, bool ref,
+                         cudaStream_t s);
 cudaError_t launch_set_frame(int *fin_tokens, int *fin_n_tok, int *fin_pos, const int *tokens, int K, int pos,
                              cudaStream_t s);
 cudaError_t launch_set_int(int *dst, int v, cudaStream_t s);

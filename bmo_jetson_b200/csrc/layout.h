@@ -29,8 +29,6 @@ enum RowPerm : int {
 enum Prologue : int {
     kProPlain = 0,    // quantise fp32 x
     kProNorm = 1,     // RMSNorm(x) * gamma, then quantise
-    kProDepAttn = 2,  // persistent frame kernel only: x = decode attention of every head
-                      // over a short ring (the depformer), computed in each CTA
 };
 
 // Epilogue: what happens to the finished dot products of a tile.
@@ -124,8 +122,6 @@ struct GemvArgs {
     TokenSrc tok;
     // partial-sum epilogue: [rows] doubles
     double *ypart;
-    // kProDepAttn prologue: the decode attention whose output is the activation
-    AttnArgs att;
     // work split: tile_aligned = 1 gives every CTA whole row tiles (no
     // cross-CTA combine); 0 splits the (tile, chunk) units evenly (stream-K)
     int tile_aligned;
@@ -136,9 +132,8 @@ struct GemvArgs {
 };
 
 
-// One step of a decode frame.  The engine builds a frame as a list of these;
-// the per-op path launches one kernel per entry, the persistent frame kernel
-// runs the list as its program with a grid barrier between entries.
+// One step of a decode frame.  The engine builds a frame as a list of these
+// and launches one kernel per entry.
 enum PhaseKind : int {
     kPhGemv = 0,      // g with prologue `pro`, epilogue `epi`
     kPhAttn = 1,      // decode attention `at` (head_dim, `splits` CTAs per head in the per-op path)
@@ -178,7 +173,7 @@ struct FramePhase {
     int head_dim;
     int splits;
     GemvArgs g;
-    AttnArgs at;   // kPhAttn, and the attention of a kProDepAttn prologue
+    AttnArgs at;   // kPhAttn
     TokenSrc tok;  // kPhTokenOut
     int count;     // kPhAllReduce, kPhResidAdd
 };

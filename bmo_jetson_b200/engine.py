@@ -26,7 +26,10 @@ _c_i32p = ctypes.POINTER(ctypes.c_int32)
 _c_f32p = ctypes.POINTER(ctypes.c_float)
 
 KV_F16, KV_Q4_0 = 0, 1
-FLAG_NO_GRAPHS, FLAG_NO_PDL, FLAG_PERSISTENT = 1, 2, 4
+FLAG_NO_GRAPHS, FLAG_NO_PDL = 1, 2
+# summation order (include/bmo_ext.h): default the reference kernels' own
+# fp32 order where the model allows; EXACT: double sums rounded once
+FLAG_EXACT, FLAG_REF_ORDER = 8, 16
 
 
 def lib() -> ctypes.CDLL:
@@ -50,7 +53,7 @@ def lib() -> ctypes.CDLL:
     for name in ("bmo_get_n_layers", "bmo_get_n_embd", "bmo_get_n_codebooks", "bmo_get_dep_q", "bmo_get_text_vocab",
                  "bmo_get_audio_vocab", "bmo_get_n_attn_heads", "bmo_get_head_dim", "bmo_capture_graphs",
                  "bmo_has_cuda_graphs", "bmo_get_kv_type", "bmo_get_n_ctx", "bmo_get_n_kv_heads", "bmo_get_device",
-                 "bmo_get_pos", "bmo_sync", "bmo_get_persistent"):
+                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order"):
         fn = getattr(L, name)
         fn.argtypes = [vp]
         fn.restype = i
@@ -128,6 +131,10 @@ def lib() -> ctypes.CDLL:
     L.bmo_k_gemv_q4_0.restype = i
     L.bmo_k_gemv_q4_0_static.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, vp, vp, i, vp]
     L.bmo_k_gemv_q4_0_static.restype = i
+    L.bmo_k_gemv_q4_0_ref.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, vp, vp, vp, vp]
+    L.bmo_k_gemv_q4_0_ref.restype = i
+    L.bmo_k_decode_attention_ref.argtypes = [vp] * 6 + [i] * 4 + [vp, i, vp]
+    L.bmo_k_decode_attention_ref.restype = i
     L.bmo_k_batch_gemm_scratch_bytes.argtypes = [i, i, i, i, i]
     L.bmo_k_batch_gemm_scratch_bytes.restype = sz
     L.bmo_k_batch_gemm_q4_0.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, i, i, vp, sz, vp]
@@ -236,9 +243,10 @@ class BMOEngine:
         return bool(lib().bmo_has_cuda_graphs(self._h))
 
     @property
-    def persistent(self) -> bool:
-        """True when frames run as the persistent frame kernel."""
-        return bool(lib().bmo_get_persistent(self._h))
+    def ref_order(self) -> bool:
+        """True when the handle computes in the reference kernels' fp32 order
+        (bit-identical to the reference's chain), False for the exact order."""
+        return bool(lib().bmo_get_ref_order(self._h))
 
     def forward_temporal(self, tokens: np.ndarray, copy: bool = False) -> Tuple[np.ndarray, np.ndarray]:
         assert tokens.dtype == np.int32 and tokens.shape == (self.n_codebooks,), (

@@ -22,7 +22,15 @@ enum { BMO_KV_F16 = 0, BMO_KV_Q4_0 = 1 };
 enum {
     BMO_FLAG_NO_GRAPHS = 1, /* launch kernels eagerly instead of replaying CUDA graphs */
     BMO_FLAG_NO_PDL = 2,    /* no programmatic dependent launch between kernels */
-    BMO_FLAG_PERSISTENT = 4, /* run frames as the persistent frame kernel (default: one kernel per op) */
+    /* Summation order of the decode step.  Default: the reference kernels'
+     * own fp32 operations in their own order (RMSNorm, Q4_0 x Q8_1 GEMV,
+     * RoPE, decode attention, SwiGLU, residual adds), so that hidden states,
+     * logits and tokens are bit-identical to the reference's chain of
+     * kernels; used where it applies (fp16 ring of at most 1024 slots, head
+     * sizes 64 or 128, one GPU), else the exact-reduction order.  The
+     * environment variable BMO_SEMANTICS=exact|ref overrides the flags. */
+    BMO_FLAG_EXACT = 8,      /* exact-reduction order: every sum in double, rounded once */
+    BMO_FLAG_REF_ORDER = 16, /* the reference order, or fail when the model or ring does not allow it */
 };
 
 /* bmo_init with an explicit CUDA device, KV ring format and flags.
@@ -38,8 +46,9 @@ BMO_API int bmo_get_pos(bmo_handle_t *h);
 BMO_API void *bmo_get_stream(bmo_handle_t *h);
 /* Bytes of device memory the handle holds (weights, KV, buffers). */
 BMO_API size_t bmo_get_device_bytes(bmo_handle_t *h);
-/* 1 when frames run as the persistent frame kernel, 0 for one kernel per op. */
-BMO_API int bmo_get_persistent(bmo_handle_t *h);
+/* 1 when the handle computes in the reference kernels' fp32 order, 0 for
+ * the exact-reduction order (see BMO_FLAG_EXACT). */
+BMO_API int bmo_get_ref_order(bmo_handle_t *h);
 
 /* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
  * slots [slot0, slot0+n) of temporal layer `layer`; rows are

@@ -53,6 +53,19 @@ BMO_API int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm,
                             float *y_dev, void *q8_out_dev, float *xn_out_dev, void *scratch_dev,
                             size_t scratch_bytes, int grid, void *stream);
 
+/* y = W x computed in the reference kernel's own fp32 order: every row is
+ * bit-identical to launch_gemv_q4_0_q8_1 (bmo.h:405-412, kernel
+ * bmo_cuda_kernels.cu:560-683) on the same ggml weights and x, and with
+ * gamma_dev the RMSNorm is launch_rmsnorm's (bmo.h:358-364) in its own
+ * order, the SwiGLU (perm SWIGLU) launch_swiglu_split's with __expf and the
+ * residual (resid_dev) launch_residual_add's.  Arguments as in
+ * bmo_k_gemv_q4_0; no scratch (each CTA owns whole row tiles); with
+ * gamma_dev, cols <= 4096.  status_dev (optional, device int) receives bit
+ * 1 if a weight copy did not land within the wait bound. */
+BMO_API int bmo_k_gemv_q4_0_ref(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
+                                const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
+                                float *y_dev, void *q8_out_dev, float *xn_out_dev, int *status_dev, void *stream);
+
 /* Size of the fixed scratch buffer behind bmo_k_gemv_q4_0_static (4 MiB: every
  * temporal and depformer layer matrix of the 7B Moshi shapes fits; the
  * 32000-row text head does not). */
@@ -106,6 +119,15 @@ BMO_API int bmo_k_decode_attention(const float *q_dev, const float *k_dev, const
                                    void *v_cache_dev, void *k_scale_dev, void *v_scale_dev, float *out_dev,
                                    int head_dim, int n_heads, int n_kv_heads, int n_ctx, const int *pos_dev,
                                    int layer, int kv_type, void *stream);
+
+/* bmo_k_decode_attention over an fp16 ring, computed in the reference
+ * kernel's own fp32 order: bit-identical to launch_decode_attention
+ * (bmo.h:414-428, kernel bmo_cuda_kernels.cu:713-848) on the same ring,
+ * q, k and v, including the appended slot.  head_dim 64 or 128; n_ctx <= 1024
+ * (the reference kernel's own score buffer).  No scratch. */
+BMO_API int bmo_k_decode_attention_ref(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
+                                       void *v_cache_dev, float *out_dev, int head_dim, int n_heads, int n_kv_heads,
+                                       int n_ctx, const int *pos_dev, int layer, void *stream);
 
 /* One tensor-parallel exchange over peer memory (the kernel bmo_init_tp
  * handles run after each split projection): parts[r] is rank r's buffer of n

@@ -200,6 +200,144 @@ void orc_gemv_q4_0_q8_1(const orc_block_q4_0 *W, const orc_block_q8_1 *x,
     for (int r = 0; r < rows; ++r) y[r] = gemv_row(W + (size_t)r * nb, x, nb);
 }
 
+/* ---- the reference kernels' own fp32 order ------------------------------
+ * bmo_gemv_q4_0_q8_1_kernel (bmo_cuda_kernels.cu:560-683) exactly: a warp per
+ * row, lane l takes half block l % 2 of blocks m = l / 2 (mod 16); its
+ * accumulator j chains blocks 64 i + 16 j + m in order, the tail (blocks past
+ * the last whole 64) continues accumulator 0 in steps of 16; each block adds
+ * acc = fmaf(d4, fmaf((float)sumi, d8, -4 s8), acc) (the kernel's
+ * `acc += d4 * ((float) sumi * ds8.x - 4.0f * ds8.y)` as nvcc contracts it);
+ * lane value ((acc0 + acc1) + acc2) + acc3; row = the __shfl_down_sync tree
+ * (offsets 16, 8, 4, 2, 1) of the 32 lane values.  Pure fp32 arithmetic, so
+ * this restatement is bit-exact against the kernel (pinned to its outputs on
+ * B200 in tests/golden/ref_kernels.npz). */
+static float ref_half_term(const orc_block_q4_0 *b4, const orc_block_q8_1 *b8, int half, float acc) {
+    const float d4 = orc_fp16_to_fp32(b4->d);
+    const float d8 = orc_fp16_to_fp32(b8->d);
+    const float s8 = orc_fp16_to_fp32(b8->s);
+    int sumi = 0;
+    for (int j = 8 * half; j < 8 * half + 8; ++j) {
+        sumi += (int)(b4->qs[j] & 0x0f) * (int)b8->qs[j];
+        sumi += (int)(b4->qs[j] >> 4) * (int)b8->qs[j + 16];
+    }
+    return fmaf(d4, fmaf((float)sumi, d8, -4.0f * s8), acc);
+}
+
+static float gemv_row_reforder(const orc_block_q4_0 *row, const orc_block_q8_1 *x, int nb) {
+    float lane_val[32];
+    for (int l = 0; l < 32; ++l) {
+        const int m = l / 2, half = l % 2;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int base = 0;
+        for (; base + 64 <= nb; base += 64)
+            for (int j = 0; j < 4; ++j) acc[j] = ref_half_term(row + base + 16 * j + m, x + base + 16 * j + m, half, acc[j]);
+        for (; base < nb; base += 16)
+            if (base + m < nb) acc[0] = ref_half_term(row + base + m, x + base + m, half, acc[0]);
+        lane_val[l] = ((acc[0] + acc[1]) + acc[2]) + acc[3];
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        for (int i = 0; i < o; ++i) lane_val[i] = lane_val[i] + lane_val[i + o];
+    return lane_val[0];
+}
+
+void orc_gemv_q4_0_q8_1_reforder(const orc_block_q4_0 *W, const orc_block_q8_1 *x, float *y, int rows, int cols) {
+    const int nb = cols / 32;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) y[r] = gemv_row_reforder(W + (size_t)r * nb, x, nb);
+}
+
+/* rmsnorm_kernel (bmo_cuda_kernels.cu:244-295) in its own order: thread t of
+ * 256 sums x[t + 256 k]^2 with fmaf; each warp's shfl_down tree; the 8 warp
+ * sums as ((w0+w4)+(w2+w6))+((w1+w5)+(w3+w7)); y = (x * scale) * w.  The
+ * kernel's scale is rsqrtf (an approximate instruction); here it is the
+ * correctly rounded 1/sqrt, so results agree to about an ulp of the scale. */
+void orc_rmsnorm_reforder(const float *x, const float *w, float eps, int n, float *y) {
+    float t[256], ws[8];
+    for (int i = 0; i < 256; ++i) {
+        t[i] = 0.0f;
+        for (int k = i; k < n; k += 256) t[i] = fmaf(x[k], x[k], t[i]);
+    }
+    for (int wp = 0; wp < 8; ++wp) {
+        float *v = t + 32 * wp;
+        for (int o = 16; o > 0; o >>= 1)
+            for (int i = 0; i < o; ++i) v[i] = v[i] + v[i + o];
+        ws[wp] = v[0];
+    }
+    const float total = ((ws[0] + ws[4]) + (ws[2] + ws[6])) + ((ws[1] + ws[5]) + (ws[3] + ws[7]));
+    const float scale = (float)(1.0 / sqrt((double)(total / (float)n + eps)));
+    for (int i = 0; i < n; ++i) y[i] = (x[i] * scale) * w[i];
+}
+
+/* bmo_decode_attention_kernel (bmo_cuda_kernels.cu:713-848) in its own order
+ * over an fp16 ring [layer][head][slot][hd] (head_dim threads, thread = dim):
+ * s_i = fl(T_i * scale), T_i = in warp order from 0, the shfl_down tree of
+ * each 32-dim group's products fl(q_d k_d); M = max(-1e20, s_i);
+ * e_i = expf(s_i - M); thread t sums e_{t + hd k} in order, warp trees, warp
+ * sums in order; inv = 1 / sum; p_i = fl(e_i inv); out_d = fmaf chain over i
+ * of p_i v_{i,d}.  expf here is libm's, the kernel's is CUDA's (both within a
+ * couple of ulp of exp), so results agree to a few ulp. */
+void orc_decode_attention_f16_reforder(const float *q, const float *k, const float *v, uint16_t *k_cache,
+                                       uint16_t *v_cache, float *out, int head_dim, int n_heads, int n_kv_heads,
+                                       int n_ctx, int pos, int layer) {
+    const int total = pos + 1, W = total > n_ctx ? n_ctx : total, start = total - W, cur = pos % n_ctx;
+    const size_t per_layer = (size_t)head_dim * n_ctx * n_heads, per_head = (size_t)head_dim * n_ctx;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    float *s = (float *)malloc(sizeof(float) * (size_t)(W > 0 ? W : 1));
+    float p[1024], tsum[1024], red[32];
+    for (int h = 0; h < n_kv_heads; ++h)
+        for (int d = 0; d < head_dim; ++d) {
+            const size_t off = (size_t)layer * per_layer + (size_t)h * per_head + (size_t)cur * head_dim + d;
+            k_cache[off] = orc_fp32_to_fp16(k[h * head_dim + d]);
+            v_cache[off] = orc_fp32_to_fp16(v[h * head_dim + d]);
+        }
+    const int q_per_kv = n_heads / n_kv_heads, nw = (head_dim + 31) / 32;
+    for (int h = 0; h < n_heads; ++h) {
+        const int kh = (n_kv_heads == n_heads) ? h : h / q_per_kv;
+        const size_t base = (size_t)layer * per_layer + (size_t)kh * per_head;
+        if (W == 1) {
+            for (int d = 0; d < head_dim; ++d) out[h * head_dim + d] = v[kh * head_dim + d];
+            continue;
+        }
+        for (int i = 0; i < W; ++i) {
+            const uint16_t *kr = k_cache + base + (size_t)((start + i) % n_ctx) * head_dim;
+            float tot = 0.0f;
+            for (int w = 0; w < nw; ++w) {
+                for (int d = 0; d < 32; ++d) p[d] = q[h * head_dim + 32 * w + d] * orc_fp16_to_fp32(kr[32 * w + d]);
+                for (int o = 16; o > 0; o >>= 1)
+                    for (int d = 0; d < o; ++d) p[d] = p[d] + p[d + o];
+                tot = tot + p[0];
+            }
+            s[i] = tot * scale;
+        }
+        float M = -1e20f;
+        for (int i = 0; i < W; ++i) M = s[i] > M ? s[i] : M;
+        for (int t = 0; t < head_dim; ++t) {
+            tsum[t] = 0.0f;
+            for (int i = t; i < W; i += head_dim) {
+                s[i] = expf(s[i] - M);
+                tsum[t] = tsum[t] + s[i];
+            }
+        }
+        for (int w = 0; w < nw; ++w) {
+            float *tv = tsum + 32 * w;
+            for (int o = 16; o > 0; o >>= 1)
+                for (int d = 0; d < o; ++d) tv[d] = tv[d] + tv[d + o];
+            red[w] = tv[0];
+        }
+        float se = 0.0f;
+        for (int w = 0; w < nw; ++w) se = se + red[w];
+        const float inv = se > 0.0f ? 1.0f / se : 0.0f;
+        for (int i = 0; i < W; ++i) s[i] = s[i] * inv;
+        for (int d = 0; d < head_dim; ++d) {
+            float acc = 0.0f;
+            for (int i = 0; i < W; ++i)
+                acc = fmaf(s[i], orc_fp16_to_fp32(v_cache[base + (size_t)((start + i) % n_ctx) * head_dim + d]), acc);
+            out[h * head_dim + d] = acc;
+        }
+    }
+    free(s);
+}
+
 /* apply_dense_q4_0_linear_gpu (bmo_compute.cpp:674-755) = launch_gemv_q4_0_q8_1:
  * quantise the activation to Q8_1, then the integer GEMV. */
 static void linear_q4_0(const orc_block_q4_0 *W, const float *x, float *y,

@@ -56,6 +56,14 @@ void orc_decode_attention_q4(const float *q, const float *k, const float *v,
                              float *out, int head_dim, int n_heads,
                              int n_kv_heads, int n_ctx, int pos, int layer);
 int  orc_argmax(const float *x, int n);
+/* The same three kernels restated in the reference kernels' own fp32 order
+ * (the GEMV bit-exact; the RMSNorm and attention up to the reference's
+ * approximate rsqrtf / CUDA's expf). */
+void orc_gemv_q4_0_q8_1_reforder(const orc_block_q4_0 *W, const orc_block_q8_1 *x, float *y, int rows, int cols);
+void orc_rmsnorm_reforder(const float *x, const float *w, float eps, int n, float *y);
+void orc_decode_attention_f16_reforder(const float *q, const float *k, const float *v, uint16_t *k_cache,
+                                       uint16_t *v_cache, float *out, int head_dim, int n_heads, int n_kv_heads,
+                                       int n_ctx, int pos, int layer);
 
 /* ---- model-level restatement --------------------------------------------- */
 typedef struct orc_model orc_model;

@@ -46,6 +46,9 @@ def lib() -> ctypes.CDLL:
         L.orc_swiglu.argtypes = [_f32p, ctypes.c_int, _f32p]
         L.orc_decode_attention_f16.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 6
         L.orc_decode_attention_q4.argtypes = [_f32p, _f32p, _f32p, _u8p, _u8p, _f32p] + [ctypes.c_int] * 6
+        L.orc_gemv_q4_0_q8_1_reforder.argtypes = [_u8p, _u8p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.orc_rmsnorm_reforder.argtypes = [_f32p, _f32p, ctypes.c_float, ctypes.c_int, _f32p]
+        L.orc_decode_attention_f16_reforder.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 6
         L.orc_argmax.argtypes = [_f32p, ctypes.c_int]
         L.orc_fp32_to_fp16.argtypes = [ctypes.c_float]
         L.orc_fp32_to_fp16.restype = ctypes.c_uint16
@@ -104,6 +107,30 @@ def gemv_q4_0(W: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
     y = np.zeros(rows, np.float32)
     lib().orc_gemv_q4_0_q8_1(np.ascontiguousarray(W, np.uint8).reshape(-1), xq.reshape(-1), y, rows, cols)
     return y
+
+
+def gemv_q4_0_reforder(W: np.ndarray, xq: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """y = W (Q4_0 bytes) @ Q8_1 blocks xq in the reference kernel's own fp32 order (bit-exact)."""
+    y = np.zeros(rows, np.float32)
+    lib().orc_gemv_q4_0_q8_1_reforder(np.ascontiguousarray(W, np.uint8).reshape(-1),
+                                      np.ascontiguousarray(xq, np.uint8).reshape(-1), y, rows, cols)
+    return y
+
+
+def rmsnorm_reforder(x, w, eps=1e-8):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros_like(x)
+    lib().orc_rmsnorm_reforder(x, np.ascontiguousarray(w, np.float32), eps, x.size, y)
+    return y
+
+
+def attention_f16_reforder(q, k, v, k_cache, v_cache, head_dim, n_heads, n_kv_heads, n_ctx, pos, layer):
+    """Ring attention in the reference kernel's order; caches (uint16 fp16 bits) updated in place."""
+    out = np.zeros(n_heads * head_dim, np.float32)
+    lib().orc_decode_attention_f16_reforder(np.ascontiguousarray(q, np.float32), np.ascontiguousarray(k, np.float32),
+                                            np.ascontiguousarray(v, np.float32), k_cache, v_cache, out,
+                                            head_dim, n_heads, n_kv_heads, n_ctx, pos, layer)
+    return out
 
 
 def rmsnorm(x, w, eps=1e-8):

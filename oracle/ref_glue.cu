@@ -1,10 +1,12 @@
-// ref_glue.cu -- host-buffer C entry points around the reference's own CUDA
-// launchers (utkarshyadav009/bmo_jetson src/bmo_cuda_kernels.cu, compiled
-// unmodified next to this file). TEST INFRASTRUCTURE: used only to produce
-// golden vectors on a B200 that pin the CPU oracle, and to time the
-// reference kernels as a baseline. Each wrapper copies its inputs to the
-// device, calls one reference launcher on the default stream, and copies the
-// results back.
+// ref_glue.cu -- C entry points around the reference's own CUDA launchers
+// (utkarshyadav009/bmo_jetson src/bmo_cuda_kernels.cu, compiled unmodified
+// next to this file). TEST INFRASTRUCTURE: used only to produce golden
+// vectors on a B200 that pin the CPU oracle, to chain the reference's kernels
+// into its own decode step (oracle/ref_chain.py) as the parity oracle of the
+// engine, and to time the reference kernels as a baseline.  The ref_*
+// wrappers copy their inputs to the device, call one reference launcher on
+// the default stream, and copy the results back; the refd_* wrappers take
+// device pointers and only launch.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstring>
@@ -196,5 +198,41 @@ float ref_time_attention_cold(int head_dim, int n_heads, int n_ctx, int pos, voi
     cudaEventDestroy(b);
     return finish() == 0 ? median_us(ts, iters) : -1.0f;
 }
+
+// ---- device-pointer launchers (default stream), for chaining ----
+int refd_rmsnorm(const float *x, const float *w, float eps, int n, float *y) {
+    launch_rmsnorm(x, w, eps, n, y, nullptr);
+    return (int)cudaGetLastError();
+}
+
+int refd_residual(const float *a, const float *b, int n, float *y) {
+    launch_residual_add(a, b, n, y, nullptr);
+    return (int)cudaGetLastError();
+}
+
+int refd_rope(const float *x, int n_heads, int head_dim, const int *pos_dev, float theta, float *y) {
+    launch_rope_interleaved(x, n_heads, head_dim, 1, 0, theta, y, nullptr, pos_dev);
+    return (int)cudaGetLastError();
+}
+
+int refd_swiglu(const float *h, int d_ff, float *y) {
+    launch_swiglu_split(h, d_ff, y, nullptr);
+    return (int)cudaGetLastError();
+}
+
+int refd_gemv(const void *W, const float *x, float *y, int rows, int cols, void *q8_scratch) {
+    launch_gemv_q4_0_q8_1(W, x, y, rows, cols, q8_scratch, nullptr);
+    return (int)cudaGetLastError();
+}
+
+// pos_dev may be null (the depformer passes its step as n_past).
+int refd_attention(const float *q, const float *k, const float *v, void *k_cache, void *v_cache, float *out,
+                   int head_dim, int n_heads, int n_kv_heads, int n_ctx, int n_past, int layer, const int *pos_dev) {
+    launch_decode_attention(q, k, v, k_cache, v_cache, out, head_dim, n_heads, n_kv_heads, n_ctx, n_past, layer,
+                            nullptr, pos_dev);
+    return (int)cudaGetLastError();
+}
+
+int refd_sync() { return finish(); }
 
 }  // extern "C"

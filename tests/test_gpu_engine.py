@@ -20,7 +20,11 @@ TOL_LOGITS = 1e-5   # logits (1e-3)
 # to the last bit except for rare double-rounding ties; without them a single
 # Q8_1 code rounding the other way (a last-bit difference at a .5 boundary)
 # moves a 256-wide activation's logits by ~1.5e-3 and the drift compounds
-# through every requantisation.  Greedy tokens must be identical.
+# through every requantisation.  Greedy tokens must be identical.  These
+# tests run the engine in its exact-reduction order (FLAG_EXACT), the order
+# of the CPU oracle; the default reference order is checked bit for bit
+# against the reference's own kernels in test_gpu_ref_chain.py.
+EXACT = engine.FLAG_EXACT
 
 
 def head_weights(path):
@@ -50,7 +54,7 @@ def tokens_for(step, K, text_vocab, audio_vocab, seed=42):
 
 @pytest.fixture(scope="module")
 def pair(tiny_model):
-    e = engine.BMOEngine(tiny_model, n_ctx=16)
+    e = engine.BMOEngine(tiny_model, n_ctx=16, flags=EXACT)
     o = orc.OracleModel(tiny_model, n_ctx=16)
     yield e, o
     e.close()
@@ -178,36 +182,10 @@ def test_frame_greedy_equals_steps(pair):
         np.testing.assert_array_equal(audio, o.depth_cascade_greedy(text_tok, zo))
 
 
-@pytest.mark.parametrize("mode", ["dep_fold", "persistent"])
-def test_alternative_paths_match_oracle(tiny_model, mode, monkeypatch):
-    """The depformer attention fused into its O-projection GEMV (BMO_DEP_FOLD=1),
-    and whole frames as the persistent frame kernel: same tokens as the oracle."""
-    flags = 0
-    if mode == "dep_fold":
-        monkeypatch.setenv("BMO_DEP_FOLD", "1")
-    else:
-        flags = engine.FLAG_PERSISTENT
-    e = engine.BMOEngine(tiny_model, n_ctx=32, flags=flags)
-    o = orc.OracleModel(tiny_model, n_ctx=32)
-    assert e.persistent == (mode == "persistent")
-    rng = np.random.default_rng(21)
-    for step in range(4):
-        t = tokens_for(step + 3, e.n_codebooks, e.text_vocab, e.audio_vocab)
-        e.pos = step
-        z, lg = e.forward_temporal(t, copy=True)
-        zo, lo, _ = o.forward_temporal(t, step)
-        assert rel_l2(z, zo) < TOL and rel_l2(lg, lo) < TOL_LOGITS
-        text = int(np.argmax(lo))
-        np.testing.assert_array_equal(e.forward_depth_cascade(text, z, 0.0, 0), o.depth_cascade_greedy(text, zo))
-    zr = rng.normal(0, 1, e.n_embd).astype(np.float32)
-    np.testing.assert_array_equal(e.forward_depth_cascade(9, zr, 0.0, 0), o.depth_cascade_greedy(9, zr))
-    e.close()
-    o.close()
-
-
 def test_graphs_and_eager_agree_bitwise(tiny_model):
     eg = engine.BMOEngine(tiny_model, n_ctx=32)
     ee = engine.BMOEngine(tiny_model, n_ctx=32, flags=engine.FLAG_NO_GRAPHS | engine.FLAG_NO_PDL)
+    assert eg.ref_order and ee.ref_order
     assert eg.capture_graphs() == 0 and eg.has_cuda_graphs()
     for step in range(5):
         t = tokens_for(step, eg.n_codebooks, eg.text_vocab, eg.audio_vocab)
@@ -223,7 +201,7 @@ def test_graphs_and_eager_agree_bitwise(tiny_model):
 @pytest.mark.parametrize("kv_type", [0, 1])
 def test_wrapped_ring_from_imported_history(tiny_model, kv_type):
     n_ctx = 64
-    e = engine.BMOEngine(tiny_model, n_ctx=n_ctx, kv_type=kv_type)
+    e = engine.BMOEngine(tiny_model, n_ctx=n_ctx, kv_type=kv_type, flags=EXACT)
     o = orc.OracleModel(tiny_model, n_ctx=n_ctx, kv_type=kv_type)
     rng = np.random.default_rng(kv_type)
     width = e.n_kv_heads * e.head_dim
@@ -266,7 +244,7 @@ def test_reset_clears_ring(pair):
 
 
 def test_reference_shaped_model_17_channels(tiny17_model):
-    e = engine.BMOEngine(tiny17_model, n_ctx=16)
+    e = engine.BMOEngine(tiny17_model, n_ctx=16, flags=EXACT)
     o = orc.OracleModel(tiny17_model, n_ctx=16)
     assert e.n_codebooks == 17
     for step in range(4):
@@ -285,7 +263,7 @@ def test_full_width_block_at_wrapped_position(model_dir):
     path = synth.ensure_model("config1", model_dir)
     n_ctx = 512
     for kv_type in (0, 1):
-        e = engine.BMOEngine(path, n_ctx=n_ctx, kv_type=kv_type)
+        e = engine.BMOEngine(path, n_ctx=n_ctx, kv_type=kv_type, flags=EXACT)
         o = orc.OracleModel(path, n_ctx=n_ctx, kv_type=kv_type)
         rng = np.random.default_rng(700)
         width = e.n_kv_heads * e.head_dim

@@ -1,8 +1,10 @@
 """Full-size parity: the BASELINE config-2/3 model (32-layer d4096 temporal
 transformer, 32000 text head, 8-step depformer) on a 512-slot ring of seeded
 history, decoding frames at positions 700.. (wrapped ring), through the
-reference C ABI and the fused frame graph, against the CPU oracle -- once
-with one kernel per op and once through the persistent frame kernel."""
+reference C ABI and the fused frame graph, in the exact-reduction order
+(FLAG_EXACT) against the CPU oracle, with fp16 and Q4_0 rings.  The default
+reference order is checked bit for bit against the reference's own kernels
+on the same model in test_gpu_ref_chain.py."""
 import numpy as np
 import pytest
 
@@ -30,11 +32,10 @@ def model(model_dir):
     return synth.ensure_model("config2", model_dir)
 
 
-@pytest.mark.parametrize("kv_type,persistent", [(0, False), (1, False), (0, True)])
-def test_full_model_frames_match_oracle(model, kv_type, persistent):
-    flags = engine.FLAG_PERSISTENT if persistent else 0
-    e = engine.BMOEngine(model, n_ctx=N_CTX, kv_type=kv_type, flags=flags)
-    assert e.persistent == persistent
+@pytest.mark.parametrize("kv_type", [0, 1])
+def test_full_model_frames_match_oracle(model, kv_type):
+    e = engine.BMOEngine(model, n_ctx=N_CTX, kv_type=kv_type, flags=engine.FLAG_EXACT)
+    assert not e.ref_order
     o = orc.OracleModel(model, n_ctx=N_CTX, kv_type=kv_type)
     assert (e.n_layers, e.n_embd, e.text_vocab, e.audio_vocab, e.dep_q) == (32, 4096, 32000, 2048, 8)
     fill(e, o, 11 + kv_type)

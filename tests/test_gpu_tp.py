@@ -51,7 +51,7 @@ def run_frames(e, hist, toks, kv_slice=None):
 
 
 def test_tp_one_rank_is_bit_identical_to_single_gpu(tiny_model):
-    e1 = engine.BMOEngine(tiny_model, n_ctx=N_CTX)
+    e1 = engine.BMOEngine(tiny_model, n_ctx=N_CTX, flags=engine.FLAG_EXACT)  # tensor parallel runs the exact order
     et = engine.BMOEngine(tiny_model, n_ctx=N_CTX, tp=(0, 1, engine.tp_unique_id()))
     assert et.tp_size == 1 and e1.tp_size == 1
     hist = history(e1)

@@ -231,3 +231,52 @@ def test_golden_attention():
         idx = np.array([base + (hh * n_ctx + slot) * hd + d for hh in range(nh) for d in range(hd)])
         np.testing.assert_array_equal(kc[idx], g[f"attn{i}_kslot"])
         np.testing.assert_array_equal(vc[idx], g[f"attn{i}_vslot"])
+
+
+# ---- the reference kernels' own fp32 order ---------------------------------
+
+def ulps(a, b):
+    """Distance in units in the last place between two float32 arrays."""
+    ia = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    ib = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    ia = np.where(ia < 0, -(ia & 0x7FFFFFFF), ia)
+    ib = np.where(ib < 0, -(ib & 0x7FFFFFFF), ib)
+    return np.abs(ia - ib)
+
+
+@golden
+def test_golden_gemv_reforder_bit_exact():
+    """The reference-order restatement reproduces the reference GEMV kernel's
+    output bit for bit on all five shapes (main-loop only, tail only, both,
+    and a padded 2816-column case)."""
+    g = np.load(GOLDEN)
+    from tests.golden.make_ref_golden import GEMV_SHAPES, gemv_inputs
+    for i, (r, c) in enumerate(GEMV_SHAPES):
+        W, _ = gemv_inputs(r, c, 200 + i)
+        y = orc.gemv_q4_0_reforder(W, g[f"gemv{i}_q8"], r, c)
+        np.testing.assert_array_equal(y.view(np.uint32), g[f"gemv{i}_y"].view(np.uint32), err_msg=f"shape {r}x{c}")
+
+
+@golden
+def test_golden_rmsnorm_reforder():
+    """Reference order up to rsqrtf: within 4 ulp of the kernel's output."""
+    g = np.load(GOLDEN)
+    for i, n in enumerate((4096, 1024)):
+        rng = np.random.default_rng(300 + i)
+        x = rng.normal(0, 1, n).astype(np.float32)
+        w = (1 + 0.1 * rng.normal(0, 1, n)).astype(np.float32)
+        assert int(ulps(orc.rmsnorm_reforder(x, w, 1e-8), g[f"rms{i}_y"]).max()) <= 4
+
+
+@golden
+def test_golden_attention_reforder():
+    """Reference order up to CUDA's expf: within 1e-6 relative L2 of the
+    kernel's output, appended fp16 slots bit-exact."""
+    g = np.load(GOLDEN)
+    from tests.golden.make_ref_golden import ATTN_CASES, attn_inputs
+    for i, (hd, nh, n_ctx, n_layers, layer, pos) in enumerate(ATTN_CASES):
+        q, k, v, kc, vc = attn_inputs(hd, nh, n_ctx, n_layers, 600 + i)
+        out = orc.attention_f16_reforder(q, k, v, kc, vc, hd, nh, nh, n_ctx, pos, layer)
+        assert rel_l2(out, g[f"attn{i}_out"]) < 1e-6, (i, pos)
+        if pos == 0:
+            np.testing.assert_array_equal(out, g[f"attn{i}_out"])
