@@ -57,6 +57,19 @@ __global__ void kv_append_kernel(const float *k, const float *v, void *k_cache, 
 }  // namespace
 }  // namespace bmo
 
+namespace bmo {
+// The argument rules of bmo_k_gemv_q4_0 other than the scratch: pointers,
+// shape, activation length and alignment (shared with the fixed-scratch entry
+// point, which must reject a call before it touches its shared buffer).
+bool gemv_kernel_args_ok(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
+                         const float *gamma_dev, const float *y_dev, const float *xn_out_dev) {
+    if (!tiled_dev || !x_dev || !y_dev || !shape_ok(rows, cols, perm, swiglu_f)) return false;
+    const QMatDesc m = make_desc(nullptr, rows, cols, perm, swiglu_f);
+    if (m.nbx > gemv_max_nbx() || (gamma_dev && cols > gemv_max_norm_cols())) return false;
+    return !(reinterpret_cast<uintptr_t>(x_dev) & 15) && !(reinterpret_cast<uintptr_t>(xn_out_dev) & 15);
+}
+}  // namespace bmo
+
 using namespace bmo;
 
 extern "C" {
@@ -86,15 +99,13 @@ size_t bmo_k_gemv_scratch_bytes(int rows, int cols, int perm, int swiglu_f) {
            align256(static_cast<size_t>(m.n_tiles) * sizeof(int)) + 256;
 }
 
+
 int bmo_k_gemv_q4_0(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
                     const float *gamma_dev, float eps, const float *resid_dev, float *y_dev, void *q8_out_dev,
                     float *xn_out_dev, void *scratch_dev, size_t scratch_bytes, int grid, void *stream) {
-    if (!tiled_dev || !x_dev || !y_dev || !scratch_dev || !shape_ok(rows, cols, perm, swiglu_f))
+    if (!scratch_dev || !gemv_kernel_args_ok(tiled_dev, rows, cols, perm, swiglu_f, x_dev, gamma_dev, y_dev, xn_out_dev))
         return static_cast<int>(cudaErrorInvalidValue);
     if (scratch_bytes < bmo_k_gemv_scratch_bytes(rows, cols, perm, swiglu_f)) return static_cast<int>(cudaErrorInvalidValue);
-    if (cols / 32 > gemv_max_nbx() * kChunkBlocks) return static_cast<int>(cudaErrorInvalidValue);
-    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (reinterpret_cast<uintptr_t>(xn_out_dev) & 15))
-        return static_cast<int>(cudaErrorInvalidValue);
     const QMatDesc m = make_desc(tiled_dev, rows, cols, perm, swiglu_f);
     GemvArgs a{};
     a.W = m;

@@ -20,7 +20,11 @@
 //     issue them on one stream or order them with events.
 //   * The first call on each device looks up the buffer's device address
 //     (cudaGetSymbolAddress with that device current); make that first call
-//     before any stream capture on that device.
+//     before any stream capture on that device.  The address is kept for the
+//     life of the process: after cudaDeviceReset on a device it is stale, so
+//     do not use this entry point on that device again.
+//   * A call that breaks an argument rule is rejected before it touches the
+//     shared buffer.
 //   * Matrices whose scratch need exceeds BMO_K_GEMV_STATIC_SCRATCH_BYTES
 //     are rejected with BMO_K_ERR_SCRATCH_TOO_SMALL; no memory is allocated
 //     or freed by this entry point.
@@ -71,7 +75,8 @@ int bmo_k_gemv_q4_0_static(const void *tiled_dev, int rows, int cols, int perm, 
                            const float *gamma_dev, float eps, const float *resid_dev, float *y_dev, void *q8_out_dev,
                            float *xn_out_dev, int grid, void *stream) {
     const size_t need = bmo_k_gemv_scratch_bytes(rows, cols, perm, swiglu_f);
-    if (need == 0 || !tiled_dev || !x_dev || !y_dev) return static_cast<int>(cudaErrorInvalidValue);
+    if (need == 0 || !gemv_kernel_args_ok(tiled_dev, rows, cols, perm, swiglu_f, x_dev, gamma_dev, y_dev, xn_out_dev))
+        return static_cast<int>(cudaErrorInvalidValue);
     if (need > BMO_K_GEMV_STATIC_SCRATCH_BYTES) return BMO_K_ERR_SCRATCH_TOO_SMALL;
     unsigned char *scratch = nullptr;
     cudaError_t e = scratch_for_current_device(&scratch);

@@ -223,8 +223,19 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 // launch
 // ---------------------------------------------------------------------------
+cudaError_t configure_attention_ref();
+
 template <int HD, int NSPLIT>
 static cudaError_t launch_ref_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
+    // The shared-memory opt-in is per device; the first launch on a device sets it.
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !(configured & (1ull << dev))) {
+        const cudaError_t e = configure_attention_ref();
+        if (e != cudaSuccess) return e;
+        configured |= 1ull << dev;
+    }
     const RefAttnLayout<HD, NSPLIT> lay(a.n_ctx);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(NSPLIT, a.n_heads);

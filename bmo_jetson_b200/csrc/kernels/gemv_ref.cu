@@ -249,8 +249,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 // launch
 // ---------------------------------------------------------------------------
+cudaError_t configure_gemv_ref();
+
 template <int PRO, int EPI>
 static cudaError_t launch_ref_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
+    // The shared-memory opt-in is per device; the first launch on a device sets it.
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !(configured & (1ull << dev))) {
+        const cudaError_t e = configure_gemv_ref();
+        if (e != cudaSuccess) return e;
+        configured |= 1ull << dev;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

@@ -12,6 +12,9 @@ namespace bmo {
 // (tile, chunk) units; `pdl` enables programmatic dependent launch on the stream.
 cudaError_t launch_gemv(const GemvArgs &a, int prologue, int epilogue, int grid, cudaStream_t s, bool pdl);
 size_t gemv_smem_bytes();
+// Argument rules of the kernel-layer GEMV (kernel_api.cu) other than its scratch.
+bool gemv_kernel_args_ok(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f, const float *x_dev,
+                         const float *gamma_dev, const float *y_dev, const float *xn_out_dev);
 int gemv_max_tiles_per_cta();
 int gemv_max_nbx();
 int gemv_max_norm_cols();

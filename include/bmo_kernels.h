@@ -85,7 +85,10 @@ BMO_API int bmo_k_gemv_q4_0_ref(const void *tiled_dev, int rows, int cols, int p
  * cleared on `stream` before each launch), so calls that can overlap on the
  * GPU race: keep them on one stream or order them.  The first call on a
  * device looks up the buffer's address; make it before any stream capture.
- * Returns BMO_K_ERR_SCRATCH_TOO_SMALL for matrices beyond the buffer. */
+ * That address is kept for the life of the process, so after cudaDeviceReset
+ * on a device this entry point must not be used on it again.  Arguments are
+ * checked before the shared buffer is touched.  Returns
+ * BMO_K_ERR_SCRATCH_TOO_SMALL for matrices beyond the buffer. */
 BMO_API int bmo_k_gemv_q4_0_static(const void *tiled_dev, int rows, int cols, int perm, int swiglu_f,
                                    const float *x_dev, const float *gamma_dev, float eps, const float *resid_dev,
                                    float *y_dev, void *q8_out_dev, float *xn_out_dev, int grid, void *stream);

@@ -6,8 +6,9 @@ CUDA kernels (src/bmo_cuda_kernels.cu, compiled unmodified by
 ``make -C oracle ref``) are chained in its own order by oracle/ref_chain.py on
 seeded synthetic models, and the outputs kept here, so the parity tests can
 run where that library is not built.  The cases (models, rings, positions,
-tokens) are defined by the functions below and regenerated from their seeds;
-a digest of each case's inputs is stored to catch drift.
+tokens) are defined below and regenerated from their seeds; the tokens and
+the block's input vector are stored with the outputs, and logit vectors as a
+digest of their bytes plus their largest entries.
 
     python tests/golden/make_ref_chain_golden.py OUT.npz     # on a GPU box
 """
@@ -114,21 +115,30 @@ def run_chain_block(model_dir: str | None = None) -> dict:
     return {"x": x, "y": y, "kslot": kslot, "vslot": vslot}
 
 
-def main(out_path: str) -> None:
+def compact(raw: dict) -> dict:
+    """Logit vectors become a digest of their bytes plus their 8 largest
+    entries (index, value); everything else is kept as it is."""
     res = {}
+    for key, val in raw.items():
+        tail = key.split("_", 1)[1] if "_" in key else key
+        if tail.startswith(("logits", "dlogits")) and not tail.endswith(("_digest", "_top")):
+            res[f"{key}_digest"] = np.array(digest(val))
+            flat = np.asarray(val, np.float32).reshape(-1)
+            top = np.argsort(-flat, kind="stable")[:8]
+            res[f"{key}_top"] = np.stack([top.astype(np.float32), flat[top]])
+        else:
+            res[key] = val
+    return res
+
+
+def main(out_path: str) -> None:
+    raw = {}
     for name in FRAME_CASES:
-        r = run_chain_frames(name)
-        for key, val in r.items():
-            if name == "config2" and key.startswith(("logits", "dlogits")):
-                # keep the large logit vectors as digests plus their top entries
-                res[f"{name}_{key}_digest"] = np.array(digest(val))
-                flat = val.reshape(-1)
-                top = np.argsort(-flat, kind="stable")[:8]
-                res[f"{name}_{key}_top"] = np.stack([top.astype(np.float32), flat[top]])
-            else:
-                res[f"{name}_{key}"] = val
+        for key, val in run_chain_frames(name).items():
+            raw[f"{name}_{key}"] = val
     for key, val in run_chain_block().items():
-        res[f"block_{key}"] = val
+        raw[f"block_{key}"] = val
+    res = compact(raw)
     np.savez_compressed(out_path, **res)
     print(f"wrote {out_path} ({len(res)} arrays)")
 

@@ -64,9 +64,9 @@ def attention_ref(q, k, v, kc, vc, hd, nh, nkv, n_ctx, pos, layer):
     kcd, vcd = to_dev(kc.view(np.float16)), to_dev(vc.view(np.float16))
     out = torch.full((nh * hd,), float("nan"), device=DEV)
     posd = torch.tensor([pos], dtype=torch.int32, device=DEV)
-    rc = L.bmo_k_decode_attention_ref(to_dev(q).data_ptr(), to_dev(k).data_ptr(), to_dev(v).data_ptr(), kcd.data_ptr(),
-                                      vcd.data_ptr(), out.data_ptr(), hd, nh, nkv, n_ctx, posd.data_ptr(), layer,
-                                      stream())
+    qd, kd, vd = to_dev(q), to_dev(k), to_dev(v)  # held until the kernels are done
+    rc = L.bmo_k_decode_attention_ref(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kcd.data_ptr(), vcd.data_ptr(),
+                                      out.data_ptr(), hd, nh, nkv, n_ctx, posd.data_ptr(), layer, stream())
     torch.cuda.synchronize()
     assert rc == 0
     return out.cpu().numpy(), kcd.cpu().numpy().view(np.uint16), vcd.cpu().numpy().view(np.uint16)
