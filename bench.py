@@ -1,4 +1,4 @@
-"""Benchmark: Moshi decode frames/s at batch 1 on B200 (BASELINE configs 2 + 3).
+"""Benchmark: Moshi decode frames/s at batch 1 on B200 (workload configs 2 + 3).
 
 One step = one decode frame: the 32-layer temporal transformer (d 4096,
 32x128 heads, FFN 11264, Q4_0) at the next position, its 32000-way text head
@@ -220,8 +220,8 @@ def frame_bytes(e):
 
 
 def gemv_roofline(local, peak_gbs, iters=40):
-    """Times the dominant kernel (Q4_0 GEMV, FFN-in shape 22528x4096 with the
-    fused RMSNorm + SwiGLU) on resident buffers: 8 distinct weight copies
+    """Times the dominant kernel of the default path (the reference-order Q4_0
+    GEMV, FFN-in shape 22528x4096 with the fused RMSNorm + SwiGLU) on resident buffers: 8 distinct weight copies
     (415 MB > L2) rotated per launch, `iters` back-to-back launches captured in
     one CUDA graph (as the decode frame runs them), CUDA events on the
     replaying stream.  The same launches issued one by one from the host are
@@ -239,12 +239,10 @@ def gemv_roofline(local, peak_gbs, iters=40):
     x = torch.randn(cols, device=dev)
     g = torch.ones(cols, device=dev)
     y = torch.empty(F, device=dev)
-    sb = L.bmo_k_gemv_scratch_bytes(rows, cols, 1, F)
-    scratch = torch.zeros(sb, dtype=torch.uint8, device=dev)
 
     def launch(i, st):
-        rc = L.bmo_k_gemv_q4_0(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8, None,
-                               y.data_ptr(), None, None, scratch.data_ptr(), sb, 0, st.cuda_stream)
+        rc = L.bmo_k_gemv_q4_0_ref(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8, None,
+                                   y.data_ptr(), None, None, None, st.cuda_stream)
         assert rc == 0, rc
 
     for i in range(8):
@@ -272,7 +270,8 @@ def gemv_roofline(local, peak_gbs, iters=40):
     del graph
     alg = rows * cols // 32 * 18 + cols * 4 * 2 + F * 4
     achieved = alg / (ms * 1e-3) / 1e9
-    return {"kernel": "gemv_q4_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0, fused RMSNorm+Q8_1, SwiGLU)",
+    return {"kernel": "gemv_ref_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0 in the reference's fp32 order, "
+                      "fused RMSNorm+Q8_1, SwiGLU)",
             "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": achieved,
             "eager_us_per_launch": eager_ms * 1e3, "timing": f"{iters} launches in one CUDA graph, weights rotated "
                                                            "over 8 copies (415 MB > L2)"}
@@ -335,7 +334,10 @@ def bench_batch(path, local, dist, sessions, steps, warmup, rank):
     kv = 2 * e.n_layers * e.n_kv_heads * e.head_dim * 18 / 32 * win
     frame_b = w + kv
     launches = 1 + e.n_layers * 9 + 2 + e.dep_q * (2 + 6 * 9 + 2) + 1
-    h2d = 4 * (64 + 64 + 64 * 64 + 4)
+    # bytes bmo_forward_frame_batch moves per frame: its fixed input block (session ids, positions and
+    # tokens of up to 64 rows x 64 channels, the channel count; one copy) in, the tokens and status out
+    batch_max, max_tokens = 64, 64
+    h2d = 4 * (batch_max + batch_max + batch_max * max_tokens + 4)
     d2h = sessions * (1 + e.dep_q) * 4 + 4
     e.close()
     return {"sessions_per_gpu": sessions, "value": world * sessions * 1000.0 / ms, "unit": "frames/s",
@@ -348,66 +350,96 @@ def bench_batch(path, local, dist, sessions, steps, warmup, rank):
                       "greedy frame (temporal + text head + 8-step depformer) per session per step"}
 
 
-def run_tp(args, rank, world, local):
+def tp_measure(path, dist, rank, world, local, kv, frames, warmup, check_frames=64):
     """Config 5: one session split over the world's GPUs (attention heads and
     FFN columns per rank, the double partial sums of each O-projection and
     FFN-out summed over the ranks -- over peer memory by default, NCCL with
-    BMO_TP_P2P=0).  Every rank decodes the same frames; rank 0 prints frames/s of
-    the single stream and p50/p99 frame times (device events, max over ranks)."""
+    BMO_TP_P2P=0).  Every rank decodes the same `frames` frames; returns (on
+    every rank) frames/s of the single stream, mean/p50/p99 frame times (device
+    events per frame, max over ranks) and whether the first `check_frames`
+    tokens equal a one-GPU handle's (rank 0 re-decodes them alone; tensor
+    parallel computes in the exact-reduction order, so the one-GPU handle does too)."""
     import torch
-    dist = init_dist(world, local)
-    torch.cuda.set_device(local)
-    path = prepare_model(rank, dist)
     from bmo_jetson_b200 import engine
     gid = broadcast_bytes(dist, engine.tp_unique_id() if rank == 0 else b"", 128)
-    kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
+    kv_type = engine.KV_F16 if kv == "f16" else engine.KV_Q4_0
     e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type, tp=(rank, world, gid))
     rng = np.random.default_rng(7)
     width = e.n_kv_heads * e.head_dim
+    hist = []
     for layer in range(e.n_layers):  # the same history on every rank, each keeps its heads
         k = rng.standard_normal((N_CTX, width * world), dtype=np.float32)
         v = rng.standard_normal((N_CTX, width * world), dtype=np.float32)
         e.kv_import(layer, 0, k[:, rank * width:(rank + 1) * width], v[:, rank * width:(rank + 1) * width])
+        if rank == 0:
+            hist.append((k[:, :], v[:, :]))
     assert e.capture_graphs() == 0
     K = e.n_codebooks
     dev = torch.device("cuda", local)
-    toks_d = torch.from_numpy(frame_tokens(args.warmup + args.steps, K, e.text_vocab, e.audio_vocab)).to(dev)
-    out_d = torch.zeros((args.warmup + args.steps, 1 + e.dep_q), dtype=torch.int32, device=dev)
+    toks = frame_tokens(warmup + frames, K, e.text_vocab, e.audio_vocab)
+    toks_d = torch.from_numpy(toks).to(dev)
+    out_d = torch.zeros((warmup + frames, 1 + e.dep_q), dtype=torch.int32, device=dev)
     stream = torch.cuda.ExternalStream(e.stream, device=dev)
     pos = START_POS
-    for i in range(args.warmup):
+    for i in range(warmup):
         e.enqueue_frame(toks_d[i].data_ptr(), K, pos, out_d[i].data_ptr())
         pos += 1
     e.sync()
     barrier(dist)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(frames + 1)]
     evs[0].record(stream)
-    for i in range(args.steps):
-        e.enqueue_frame(toks_d[args.warmup + i].data_ptr(), K, pos, out_d[args.warmup + i].data_ptr())
+    for i in range(frames):
+        e.enqueue_frame(toks_d[warmup + i].data_ptr(), K, pos, out_d[warmup + i].data_ptr())
         evs[i + 1].record(stream)
         pos += 1
     e.sync()
     torch.cuda.synchronize(dev)
-    per = np.array([evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)])
+    per = np.array([evs[i].elapsed_time(evs[i + 1]) for i in range(frames)])
     ms = reduce_max(dist, float(per.mean()))
     p50, p99 = reduce_max(dist, float(np.percentile(per, 50))), reduce_max(dist, float(np.percentile(per, 99)))
-    toks = out_d.cpu().numpy()
+    tp_tokens = out_d.cpu().numpy()
+    exchange = "NVLink peer memory (IPC-mapped partial buffers, fused sum + residual kernel)" \
+        if e.tp_peer_exchange else "NCCL all-reduce"
+    e.close()
     barrier(dist)
+    equal = None
+    if rank == 0 and check_frames > 0:
+        n = min(check_frames, warmup + frames)
+        one = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type, flags=engine.FLAG_EXACT)
+        for layer, (k, v) in enumerate(hist):
+            one.kv_import(layer, 0, k, v)
+        ones = np.zeros((n, 1 + one.dep_q), np.int32)
+        for i in range(n):
+            one.pos = START_POS + i
+            _, _, text, audio = one.forward_frame_greedy(toks[i])
+            ones[i, 0], ones[i, 1:] = text, audio
+        one.close()
+        equal = bool((ones == tp_tokens[:n]).all())
+    barrier(dist)
+    return {"value": 1000.0 / ms, "unit": "frames/s", "n_gpus": world, "frames": frames, "ms_per_step": ms,
+            "p50_ms": p50, "p99_ms": p99, "exchange": exchange, "parallelism": f"tp{world}",
+            "tokens_equal_1gpu": equal, "tokens_checked": check_frames,
+            "config": "config5: one session, 32-layer temporal + text head + 8-step depformer per frame, heads and "
+                      "FFN columns split over the GPUs, one exchange after each O-projection and FFN-out"}
+
+
+def run_tp(args, rank, world, local):
+    """--tp: only the tensor-parallel measurement, as its own JSON line."""
+    import torch
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    path = prepare_model(rank, dist)
+    r = tp_measure(path, dist, rank, world, local, args.kv, args.steps, args.warmup)
     if rank == 0:
-        print(json.dumps({"metric": "Moshi decode frames/s (B=1, tensor parallel)", "value": 1000.0 / ms,
+        print(json.dumps({"metric": "Moshi decode frames/s (B=1, tensor parallel)", "value": r["value"],
                           "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                          "ms_per_step": ms, "p50_ms": p50, "p99_ms": p99, "higher_is_better": True,
-                          "scaling": "strong", "vs_baseline": None, "impl": "ours",
+                          "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "p99_ms": r["p99_ms"],
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "impl": "ours",
                           "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales), double partial sums over ranks",
                           "data": "synthetic: seeded weights, tokens and KV history",
-                          "config": {"workload": "config5: one session, 32-layer temporal + text head + 8-step "
-                                                 "depformer per frame, heads and FFN columns split over the GPUs",
-                                     "parallelism": f"tp{world}", "n_ctx": N_CTX, "start_pos": START_POS,
-                                     "kv": args.kv,
-                                     "exchange": "NVLink peer memory (IPC-mapped partial buffers, fused sum + "
-                                                 "residual kernel)" if e.tp_peer_exchange else "NCCL all-reduce"},
-                          "text_tokens_head": toks[args.warmup:args.warmup + 4, 0].tolist()}), flush=True)
-    e.close()
+                          "config": {"workload": r["config"], "parallelism": r["parallelism"], "n_ctx": N_CTX,
+                                     "start_pos": START_POS, "kv": args.kv, "exchange": r["exchange"]},
+                          "tokens_equal_1gpu": r["tokens_equal_1gpu"]}), flush=True)
     if dist is not None:
         dist.destroy_process_group()
     return 0
@@ -446,13 +478,114 @@ def cpu_baseline(model_path, n_frames=2):
                       f"model at pos {START_POS + 1}.., oracle in C with OpenMP"}
 
 
+def ref_kernel_timing(peak_gbs, iters=20, flush_bytes=256 << 20):
+    """--ref-kernels: the reference's own CUDA kernels (src/bmo_cuda_kernels.cu,
+    compiled unmodified into oracle/_ref) against the kernels of the default
+    path, which compute the same results bit for bit, on the temporal layer's
+    GEMV shapes, the text head and one layer's decode attention at pos 700 of a
+    512-slot fp16 ring.  Each launch alone after a rewrite of a flush buffer
+    larger than L2 (weights and caches come from HBM), median of `iters`, CUDA
+    events on the launching stream.  Reference GEMV = its Q8_1 quantiser +
+    GEMV kernels (launch_gemv_q4_0_q8_1); ours = bmo_k_gemv_q4_0_ref (quantiser
+    in the prologue).  Attention: reference launch_decode_attention; ours
+    bmo_k_decode_attention_ref (K/V append + attention)."""
+    import ctypes
+    import torch
+    from bmo_jetson_b200 import engine
+    from oracle import oracle as orc
+    dev = torch.device("cuda:0")
+    L, R = engine.lib(), orc.ref_lib()
+    s = torch.cuda.current_stream(dev)
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device=dev)
+    rng = np.random.default_rng(0)
+
+    def median_us(fn):
+        ts = []
+        for i in range(iters):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            fn()
+            b.record(s)
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return float(np.median(ts))
+
+    out = {"mode": "ref_kernels", "gpu": torch.cuda.get_device_name(dev), "iters": iters,
+           "l2_flush_bytes": flush_bytes, "peak_gbs": peak_gbs, "gemv": {}, "attention": {}}
+    shapes = {"qkv": (12288, 4096), "o_proj": (4096, 4096), "ffn_in": (22528, 4096), "ffn_out": (4096, 11264),
+              "text_head": (32000, 4096)}
+    for name, (rows, cols) in shapes.items():
+        w = rng.integers(0, 256, (rows, cols // 32, 18), dtype=np.uint8)
+        w[:, :, 0], w[:, :, 1] = 0x00, 0x20  # fp16 scale 2^-7
+        W = np.ascontiguousarray(w.reshape(-1))
+        x = rng.standard_normal(cols, dtype=np.float32)
+        ref_us = R.ref_time_gemv_cold(W, x, rows, cols, ctypes.c_void_p(flush.data_ptr()), flush_bytes, iters)
+        assert ref_us > 0, "reference GEMV failed"
+        src = torch.from_numpy(W).to(dev)
+        tiled = torch.empty(L.bmo_k_q4_0_tiled_bytes(rows, cols, 0, 0), dtype=torch.uint8, device=dev)
+        assert L.bmo_k_repack_q4_0(src.data_ptr(), tiled.data_ptr(), rows, cols, 0, 0, s.cuda_stream) == 0
+        del src
+        xd = torch.from_numpy(x).to(dev)
+        y = torch.empty(rows, device=dev)
+
+        def ours():
+            rc = L.bmo_k_gemv_q4_0_ref(tiled.data_ptr(), rows, cols, 0, 0, xd.data_ptr(), None, 1e-8, None,
+                                       y.data_ptr(), None, None, None, s.cuda_stream)
+            assert rc == 0, rc
+        for _ in range(3):
+            ours()
+        our_us = median_us(ours)
+        alg = rows * cols // 32 * 18 + cols * 4 + rows * 4
+        out["gemv"][name] = {"rows": rows, "cols": cols, "bytes": alg, "reference_us": ref_us,
+                             "reference_gbs": alg / ref_us / 1e3, "ours_us": our_us, "ours_gbs": alg / our_us / 1e3,
+                             "speedup": ref_us / our_us, "ours_frac": alg / our_us / 1e3 / peak_gbs}
+        del tiled
+    hd, nh, n_ctx, pos = 128, 32, 512, 700
+    ref_us = R.ref_time_attention_cold(hd, nh, n_ctx, pos, ctypes.c_void_p(flush.data_ptr()), flush_bytes, iters)
+    assert ref_us > 0, "reference attention failed"
+    q = torch.zeros(nh * hd, device=dev)
+    kc = torch.zeros(nh * n_ctx * hd, dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    o = torch.empty(nh * hd, device=dev)
+    pos_d = torch.tensor([pos], dtype=torch.int32, device=dev)
+
+    def ours_attn():
+        rc = L.bmo_k_decode_attention_ref(q.data_ptr(), q.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                          o.data_ptr(), hd, nh, nh, n_ctx, pos_d.data_ptr(), 0, s.cuda_stream)
+        assert rc == 0, rc
+    for _ in range(3):
+        ours_attn()
+    our_us = median_us(ours_attn)
+    out["attention"] = {"head_dim": hd, "heads": nh, "n_ctx": n_ctx, "pos": pos, "kv_bytes": 2 * nh * n_ctx * hd * 2,
+                        "reference_us": ref_us, "ours_us": our_us, "speedup": ref_us / our_us}
+    return out
+
+
+def workload_config(kv, world):
+    """The `config` object both arms print (the same workload, same keys)."""
+    return {"workload": "config2+3: 32-layer temporal (d4096, 32x128, FFN 11264) + 32000 text head + greedy 8-step "
+                        "depformer (6x d1024) per frame, B=1, one session per GPU",
+            "n_ctx": N_CTX, "start_pos": START_POS, "kv": kv,
+            "l2": "weights 4.1 GB per frame > 126 MB L2 (no flush needed)",
+            "parallelism": f"dp{world} (independent sessions)"}
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU arithmetic (oracle port) on the host cores."""
+    """--impl reference: the reference's CPU arithmetic (the oracle port, C with
+    OpenMP on every host core) on full frames of the same workload.  The model
+    file is written with the oracle's copy of the synthetic generator, so this
+    process loads no library of the engine."""
     if rank != 0:
         return 0
-    path = prepare_model(0, None)
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)  # torchrun gives its workers 1
+    from bmo_jetson_b200 import synth
     from oracle import oracle as orc
-    o = orc.OracleModel(path, n_ctx=N_CTX)
+    synth.use_generator(orc.lib(), "orc_synth_")
+    d = os.environ.get("BMO_MODEL_DIR") or os.path.join(os.environ.get("TMPDIR", "/tmp"), "bmo_models")
+    path = synth.ensure_model("config2", d)
+    o = orc.OracleModel(path, n_ctx=N_CTX, threads=cores)
     rng = np.random.default_rng(7)
     width = o.n_kv_heads * o.head_dim
     for layer in range(o.n_layers):
@@ -471,18 +604,17 @@ def run_reference(args, rank, world):
         pos += 1
     dt = time.perf_counter() - t0
     v = args.steps / dt
-    cores = os.cpu_count() or 1
     line = {"metric": "Moshi decode frames/s (B=1)", "value": v, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
             "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales)",
             "data": "synthetic: seeded N(0,0.02) Q4_0 weights, N(0,1) f16 embeddings, seeded tokens and KV history",
-            "config": {"workload": "config2+3: 32-layer temporal (d4096) + text head + 8-step depformer frame, B=1",
-                       "n_ctx": N_CTX, "start_pos": START_POS, "kv": "f16"},
+            "config": workload_config("f16", world),
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} full frames after {args.warmup} warm-up frames; the reference's "
-                                       "ggml CPU path cannot be built here (llama.cpp not vendored), so this is the "
-                                       "C restatement of its arithmetic (oracle/) with OpenMP"},
+                             "sample": f"{args.steps} full frames after {args.warmup} warm-up frames on rank 0 only; "
+                                       "the reference's ggml CPU path cannot be built here (llama.cpp not vendored), "
+                                       "so this is the C restatement of its arithmetic (oracle/) with OpenMP on "
+                                       f"{cores} threads"},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     o.close()
@@ -501,8 +633,12 @@ def main():
     ap.add_argument("--sessions", type=int, default=64,
                     help="config 4: sessions per GPU of the batched measurement (0: skip it)")
     ap.add_argument("--batch-only", action="store_true", help="only the batched-sessions measurement")
+    ap.add_argument("--ref-kernels", action="store_true",
+                    help="only the per-kernel timing of the reference's CUDA kernels against ours (one GPU)")
     ap.add_argument("--tp", action="store_true",
                     help="config 5: one session tensor-parallel over the --gpus ranks (prints its own line)")
+    ap.add_argument("--tp-frames", type=int, default=3000,
+                    help="N > 1: frames of the tensor-parallel session measured after the data-parallel one (0: skip)")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="profiling: run --warmup frames then this many device-resident frames, print nothing else")
     args = ap.parse_args()
@@ -515,6 +651,10 @@ def main():
 
     import torch
     peak, peak_kind = measured_peaks()
+    if args.ref_kernels:
+        torch.cuda.set_device(local)
+        print(json.dumps(ref_kernel_timing(peak, iters=max(args.steps, 5))), flush=True)
+        return 0
     if args.kernel_only:
         torch.cuda.set_device(local)
         r = gemv_roofline(local, peak, iters=max(args.steps, 1))
@@ -534,6 +674,7 @@ def main():
     from bmo_jetson_b200 import engine
     kv_type = engine.KV_F16 if args.kv == "f16" else engine.KV_Q4_0
     e = engine.BMOEngine(path, n_ctx=N_CTX, device=local, kv_type=kv_type)
+    ref_order = e.ref_order
     fill_history(e)
     assert e.capture_graphs() == 0
     K = e.n_codebooks
@@ -624,6 +765,14 @@ def main():
     if args.sessions > 0:
         batch = bench_batch(path, local, dist, args.sessions, max(5, min(args.steps, 20)), max(3, min(args.warmup, 3)),
                             rank)
+    # N > 1: config 4 as written (64 sessions in total, split over the GPUs)
+    # and config 5 (one session tensor-parallel over the GPUs)
+    batch_split = tp = None
+    if world > 1 and args.sessions > 0 and 64 % world == 0:
+        batch_split = bench_batch(path, local, dist, 64 // world, max(5, min(args.steps, 20)),
+                                  max(3, min(args.warmup, 3)), rank)
+    if world > 1 and args.tp_frames > 0:
+        tp = tp_measure(path, dist, rank, world, local, "f16", args.tp_frames, max(args.warmup, 3))
 
     line = None
     if rank == 0:
@@ -640,16 +789,14 @@ def main():
             "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 (Q4_0 x Q8_1 integer dot, fp32 scales)",
             "data": "synthetic: seeded N(0,0.02) Q4_0 weights, N(0,1) f16 embeddings, seeded tokens and KV history",
-            "config": {"workload": "config2+3: 32-layer temporal (d4096, 32x128, FFN 11264) + 32000 text head + "
-                                   "greedy 8-step depformer (6x d1024) per frame, B=1, one session per GPU",
-                       "n_ctx": N_CTX, "start_pos": START_POS, "kv": args.kv,
-                       "l2": "weights 4.1 GB per frame > 126 MB L2 (no flush needed)",
-                       "parallelism": f"dp{world} (independent sessions)",
-                       "frame_hbm_bytes": total_b, "temporal_bytes": temporal_b, "depformer_bytes": dep_b,
-                       "kv_bytes": kv_b, "frame_hbm_gbs": total_b / (ms * 1e-3) / 1e9,
-                       "frame_hbm_frac": total_b / (ms * 1e-3) / 1e9 / peak,
-                       "temporal_ms": temporal_ms, "depformer_ms": depth_ms,
-                       "temporal_hbm_gbs": (temporal_b + kv_b) / (temporal_ms * 1e-3) / 1e9},
+            "config": workload_config(args.kv, world),
+            "frame": {"semantics": "reference order" if ref_order else "exact order",
+                      "frame_hbm_bytes": total_b, "temporal_bytes": temporal_b, "depformer_bytes": dep_b,
+                      "kv_bytes": kv_b, "frame_hbm_gbs": total_b / (ms * 1e-3) / 1e9,
+                      "frame_hbm_frac": total_b / (ms * 1e-3) / 1e9 / peak,
+                      "temporal_ms": temporal_ms, "depformer_ms": depth_ms,
+                      "temporal_hbm_gbs": (temporal_b + kv_b) / (temporal_ms * 1e-3) / 1e9,
+                      "temporal_hbm_frac": (temporal_b + kv_b) / (temporal_ms * 1e-3) / 1e9 / peak},
             "roofline": {"bound": "hbm", "achieved": rl["achieved_gbs"], "peak": peak, "unit": "GB/s",
                          "frac": rl["achieved_gbs"] / peak, "traffic": traffic_from_profile(),
                          "kernel": rl["kernel"], "bytes_per_launch": rl["bytes_per_launch"],
@@ -661,6 +808,8 @@ def main():
             "gpu_launches": launches_per_frame * args.steps,
             "clocks": clocks.summary(),
             "batch": batch,
+            "batch_split": batch_split,
+            "tp": tp,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -62,10 +62,10 @@ PRESETS = {
     "tiny": SynthConfig(),
     # tiny with the reference's 17-channel input (n_q = 16) and Q4_0 embeddings
     "tiny17": SynthConfig(n_q=16, emb_type="q4_0", text_bias=False, seed=3),
-    # one full-width temporal block (no heads, no depformer)
+    # one full-width temporal block (no heads, no depformer), the benchmark's config 1
     "config1": SynthConfig(n_layers=1, n_embd=4096, n_heads=32, head_dim=128, ffn_hidden=11264,
                            text_vocab=0, n_q=8, dep_q=0, seed=1),
-    # BASELINE config 2 + 3: 32-layer 7B-class temporal transformer, 32000 text head,
+    # configs 2 + 3: 32-layer 7B-class temporal transformer, 32000 text head,
     # 8 audio codebook inputs, depformer 6 x 1024 with 16 heads, FFN 2816, dep_q 8
     "config2": SynthConfig(n_layers=32, n_embd=4096, n_heads=32, head_dim=128, ffn_hidden=11264,
                            text_vocab=32000, audio_vocab=2048, n_q=8, dep_q=8, dep_dim=1024, dep_heads=16,
@@ -73,34 +73,52 @@ PRESETS = {
 }
 
 
-def _lib():
-    L = _eng.lib()
-    L.bmo_synth_normal_f32.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong, ctypes.c_float,
-                                       ctypes.c_float, ctypes.c_void_p]
-    L.bmo_synth_f16.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong, ctypes.c_float,
-                                ctypes.c_float, ctypes.c_void_p]
-    L.bmo_synth_q4_0.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong, ctypes.c_longlong,
-                                 ctypes.c_float, ctypes.c_void_p]
-    L.bmo_quantize_q4_0_ref.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
-    return L
+_GEN = None  # (library, symbol prefix) of the tensor generator
+
+
+def use_generator(cdll, prefix: str) -> None:
+    """Generates tensors with `cdll`'s <prefix>normal_f32, <prefix>f16 and
+    <prefix>q4_0 (the same counter-based generator, bit for bit) instead of
+    libbmo's bmo_synth_* -- for processes that must not load the engine."""
+    global _GEN
+    for name in ("normal_f32", "f16"):
+        getattr(cdll, prefix + name).argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong, ctypes.c_float,
+                                                 ctypes.c_float, ctypes.c_void_p]
+    getattr(cdll, prefix + "q4_0").argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong,
+                                               ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p]
+    _GEN = (cdll, prefix)
+
+
+def _gen(name: str):
+    if _GEN is None:
+        use_generator(_eng.lib(), "bmo_synth_")
+    return getattr(_GEN[0], _GEN[1] + name)
 
 
 def normal_f32(seed: int, stream: int, n: int, mean: float = 0.0, sigma: float = 1.0) -> np.ndarray:
     out = np.empty(n, np.float32)
-    _lib().bmo_synth_normal_f32(seed, stream, n, mean, sigma, out.ctypes.data)
+    _gen("normal_f32")(seed, stream, n, mean, sigma, out.ctypes.data)
+    return out
+
+
+def f16_normal(seed: int, stream: int, n: int, mean: float = 0.0, sigma: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.uint16)
+    _gen("f16")(seed, stream, n, mean, sigma, out.ctypes.data)
     return out
 
 
 def q4_0_normal(seed: int, stream: int, rows: int, cols: int, sigma: float) -> np.ndarray:
     out = np.empty((rows, cols // 32 * 18), np.uint8)
-    _lib().bmo_synth_q4_0(seed, stream, rows, cols, sigma, out.ctypes.data)
+    _gen("q4_0")(seed, stream, rows, cols, sigma, out.ctypes.data)
     return out
 
 
 def quantize_q4_0(x: np.ndarray) -> np.ndarray:
+    L = _eng.lib()
+    L.bmo_quantize_q4_0_ref.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
     x = np.ascontiguousarray(x, np.float32)
     out = np.empty(x.shape[:-1] + (x.shape[-1] // 32 * 18,), np.uint8)
-    _lib().bmo_quantize_q4_0_ref(x.ctypes.data, x.size, out.ctypes.data)
+    L.bmo_quantize_q4_0_ref(x.ctypes.data, x.size, out.ctypes.data)
     return out
 
 
@@ -137,9 +155,7 @@ def tensor_specs(cfg: SynthConfig):
     def emb(name, rows, dim):
         if cfg.emb_type == "f16":
             def make(nm=name):
-                out = np.empty(rows * dim, np.uint16)
-                _lib().bmo_synth_f16(s, _stream_id(nm), rows * dim, 0.0, 1.0, out.ctypes.data)
-                return out
+                return f16_normal(s, _stream_id(nm), rows * dim)
             specs.append(_Spec(name, [dim, rows], GGML_F16, make))
         elif cfg.emb_type == "f32":
             specs.append(_Spec(name, [dim, rows], GGML_F32, lambda nm=name: normal_f32(s, _stream_id(nm), rows * dim)))

@@ -1139,3 +1139,71 @@ int orc_kv_export(orc_model *m, int which, int layer, int slot0, int n, float *o
         }
     return 0;
 }
+
+/* ---- synthetic model data ------------------------------------------------
+ * The counter-based generator of the benchmark models (splitmix64 finaliser
+ * over (seed, stream, index), Box-Muller pairs), restated here so that the
+ * CPU-only benchmark arm can write the same GGUF bit for bit without loading
+ * the CUDA engine library.  Element i of a (seed, stream) tensor is the
+ * cosine (even i) or sine (odd i) branch of pair i / 2. */
+static uint64_t syn_mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+static uint64_t syn_key(uint64_t seed, uint64_t stream) {
+    return syn_mix64(seed) ^ syn_mix64(stream + 0x632be59bd9b4e019ull);
+}
+
+static double syn_uniform(uint64_t key, uint64_t i) {
+    return ((double)(syn_mix64(key ^ syn_mix64(i)) >> 11) + 1.0) * 0x1.0p-53;
+}
+
+static void syn_pair(uint64_t key, uint64_t p, double *z0, double *z1) {
+    const double r = sqrt(-2.0 * log(syn_uniform(key, 2 * p)));
+    const double t = 6.283185307179586 * syn_uniform(key, 2 * p + 1);
+    *z0 = r * cos(t);
+    *z1 = r * sin(t);
+}
+
+void orc_synth_normal_f32(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, float *out) {
+    const uint64_t key = syn_key(seed, stream);
+#pragma omp parallel for schedule(static)
+    for (long long p = 0; p < (n + 1) / 2; ++p) {
+        double z[2];
+        syn_pair(key, (uint64_t)p, &z[0], &z[1]);
+        for (int k = 0; k < 2 && 2 * p + k < n; ++k) out[2 * p + k] = (float)((double)mean + (double)sigma * z[k]);
+    }
+}
+
+void orc_synth_f16(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, uint16_t *out) {
+    const uint64_t key = syn_key(seed, stream);
+#pragma omp parallel for schedule(static)
+    for (long long p = 0; p < (n + 1) / 2; ++p) {
+        double z[2];
+        syn_pair(key, (uint64_t)p, &z[0], &z[1]);
+        for (int k = 0; k < 2 && 2 * p + k < n; ++k)
+            out[2 * p + k] = orc_fp32_to_fp16((float)((double)mean + (double)sigma * z[k]));
+    }
+}
+
+void orc_synth_q4_0(uint64_t seed, uint64_t stream, long long rows, long long cols, float sigma, uint8_t *out) {
+    const uint64_t key = syn_key(seed, stream);
+    const long long nb = cols / 32;
+#pragma omp parallel for schedule(static)
+    for (long long r = 0; r < rows; ++r) {
+        float blk[32];
+        for (long long b = 0; b < nb; ++b) {
+            const uint64_t base = (uint64_t)(r * cols + b * 32);
+            for (int j = 0; j < 32; j += 2) {
+                double z0, z1;
+                syn_pair(key, (base + (uint64_t)j) >> 1, &z0, &z1);
+                blk[j] = (float)((double)sigma * z0);
+                blk[j + 1] = (float)((double)sigma * z1);
+            }
+            orc_quantize_row_q4_0(blk, (orc_block_q4_0 *)(out + (size_t)(r * nb + b) * 18), 32);
+        }
+    }
+}

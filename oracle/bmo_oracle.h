@@ -105,6 +105,11 @@ int orc_select_session(orc_model *m, int s);
 int orc_kv_export(orc_model *m, int which, int layer, int slot0, int n,
                   float *out);
 
+/* ---- synthetic model data (the benchmark models' generator, bit for bit) - */
+void orc_synth_normal_f32(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, float *out);
+void orc_synth_f16(uint64_t seed, uint64_t stream, long long n, float mean, float sigma, uint16_t *out);
+void orc_synth_q4_0(uint64_t seed, uint64_t stream, long long rows, long long cols, float sigma, uint8_t *out);
+
 #ifdef __cplusplus
 }
 #endif

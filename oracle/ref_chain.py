@@ -33,7 +33,8 @@ from . import oracle as _orc
 _vp, _i, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 
 
-def _ref_dev_lib() -> ctypes.CDLL:
+def ref_dev_lib() -> ctypes.CDLL:
+    """The device-pointer launchers of the reference's kernels (refd_*)."""
     L = ctypes.CDLL(_orc.REF_SO)
     L.refd_rmsnorm.argtypes = [_vp, _vp, _f, _i, _vp]
     L.refd_residual.argtypes = [_vp, _vp, _i, _vp]
@@ -41,8 +42,10 @@ def _ref_dev_lib() -> ctypes.CDLL:
     L.refd_swiglu.argtypes = [_vp, _i, _vp]
     L.refd_gemv.argtypes = [_vp, _vp, _vp, _i, _i, _vp]
     L.refd_attention.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp] + [_i] * 6 + [_vp]
+    L.refd_rvq_decode.argtypes = [_vp, _vp, _vp]
+    L.refd_rvq_encode.argtypes = [_vp] * 9
     for n in ("refd_rmsnorm", "refd_residual", "refd_rope", "refd_swiglu", "refd_gemv", "refd_attention",
-              "refd_sync"):
+              "refd_rvq_decode", "refd_rvq_encode", "refd_sync"):
         getattr(L, n).restype = _i
     return L
 
@@ -76,7 +79,7 @@ class RefChain:
         self.torch = torch
         self.dev = torch.device(f"cuda:{device}")
         torch.cuda.set_device(self.dev)
-        self.L = _ref_dev_lib()
+        self.L = ref_dev_lib()
         rd = GGUFReader(gguf_path)
         self._t = {t.name: t for t in rd.tensors}
 

@@ -22,6 +22,10 @@ void launch_gemv_q4_0_q8_1(const void *W_dev, const float *x_dev, float *y_dev, 
 void launch_decode_attention(const float *q_dev, const float *k_dev, const float *v_dev, void *k_cache_dev,
                              void *v_cache_dev, float *out_dev, int head_dim, int n_heads, int n_kv_heads,
                              int n_ctx, int n_past, int layer, void *stream, const int *pos_dev);
+void launch_rvq_decode(const int32_t *codes_dev, const float *proj_tables_dev, float *out_dev, void *stream);
+void launch_rvq_encode(const float *in_vec_dev, const float *w_in0_dev, const float *e0_dev, const float *norm0_dev,
+                       const float *w_in_rest_dev, const float *e_rest_dev, const float *norm_rest_dev,
+                       int32_t *out_codes_dev, float *scratch_dev, void *stream);
 
 namespace {
 struct dbuf {
@@ -230,6 +234,18 @@ int refd_attention(const float *q, const float *k, const float *v, void *k_cache
                    int head_dim, int n_heads, int n_kv_heads, int n_ctx, int n_past, int layer, const int *pos_dev) {
     launch_decode_attention(q, k, v, k_cache, v_cache, out, head_dim, n_heads, n_kv_heads, n_ctx, n_past, layer,
                             nullptr, pos_dev);
+    return (int)cudaGetLastError();
+}
+
+int refd_rvq_decode(const int32_t *codes, const float *proj_tables, float *out) {
+    launch_rvq_decode(codes, proj_tables, out, nullptr);
+    return (int)cudaGetLastError();
+}
+
+int refd_rvq_encode(const float *in_vec, const float *w_in0, const float *e0, const float *norm0,
+                    const float *w_in_rest, const float *e_rest, const float *norm_rest, int32_t *out_codes,
+                    float *scratch) {
+    launch_rvq_encode(in_vec, w_in0, e0, norm0, w_in_rest, e_rest, norm_rest, out_codes, scratch, nullptr);
     return (int)cudaGetLastError();
 }
 

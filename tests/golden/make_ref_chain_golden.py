@@ -63,7 +63,7 @@ FRAME_CASES = {
     "tiny17": ("tiny17", 64, 70, 2, 13, 14),
     "config2": ("config2", 512, 700, 3, 7, 1),
 }
-# One full-width temporal block at a wrapped position.
+# One full-width temporal block at a wrapped position (config 1).
 BLOCK_CASE = ("config1", 512, 700, 5, 6)   # preset, ring slots, pos, history seed, input seed
 
 

@@ -259,7 +259,7 @@ def test_reference_shaped_model_17_channels(tiny17_model):
 
 
 def test_full_width_block_at_wrapped_position(model_dir):
-    """one d=4096 block, 512-slot ring of N(0,1) history, pos 700."""
+    """Config 1: one d=4096 block, 512-slot ring of N(0,1) history, pos 700."""
     path = synth.ensure_model("config1", model_dir)
     n_ctx = 512
     for kv_type in (0, 1):
@@ -282,6 +282,9 @@ def test_full_width_block_at_wrapped_position(model_dir):
 
 
 def test_rvq_decode_and_encode():
+    """bmo_rvq_decode / bmo_rvq_encode (src/bmo_cuda_kernels.cu:886-1063):
+    against a float64 restatement of the search, and against the reference's
+    own RVQ kernels (decode bit for bit, encode the same codes)."""
     import torch
     L = engine.lib()
     dev = torch.device("cuda:0")
@@ -320,3 +323,48 @@ def test_rvq_decode_and_encode():
         expect.append(c)
         r = r - er[s, c]
     assert out_codes.cpu().numpy().tolist() == expect
+    # against the reference's own RVQ kernels, where they are built
+    from oracle import ref_chain
+    if ref_chain.available():
+        R = ref_chain.ref_dev_lib()
+        ref_out = torch.zeros(512, device=dev)
+        ref_codes = torch.zeros(8, dtype=torch.int32, device=dev)
+        ref_scratch = torch.zeros(384, device=dev)
+        assert R.refd_rvq_decode(codes_d.data_ptr(), proj_d.data_ptr(), ref_out.data_ptr()) == 0
+        assert R.refd_rvq_encode(d["x"].data_ptr(), d["w0"].data_ptr(), d["e0"].data_ptr(), d["n0"].data_ptr(),
+                                 d["wr"].data_ptr(), d["er"].data_ptr(), d["nr"].data_ptr(), ref_codes.data_ptr(),
+                                 ref_scratch.data_ptr()) == 0
+        assert R.refd_sync() == 0
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), ref_out.cpu().numpy().view(np.uint32))
+        assert out_codes.cpu().numpy().tolist() == ref_codes.cpu().numpy().tolist()
+
+
+def test_topk_cascade_tokens_equal_reference_sampler(tiny_model):
+    """bmo_forward_depth_cascade with top_k=50, temp=0.8 draws the same tokens
+    as the reference's sampler (tests/sampler.py: partial_sort, expf,
+    discrete_distribution, a per-thread std::mt19937(42)) on the same step
+    logits.  Two cascades run in a fresh thread (a fresh generator); the
+    second continues the first's stream, as the reference's thread_local does."""
+    import threading
+
+    from tests import sampler
+    e = engine.BMOEngine(tiny_model, n_ctx=16)
+    rng = np.random.default_rng(8)
+    cases = [(5, rng.normal(0, 1, e.n_embd).astype(np.float32)), (77, rng.normal(0, 2, e.n_embd).astype(np.float32))]
+    got = []
+    th = threading.Thread(target=lambda: got.extend(e.forward_depth_cascade(t, z, 0.8, 50) for t, z in cases))
+    th.start()
+    th.join()
+    assert len(got) == 2
+    g = sampler.MT19937(42)
+    draws = 0
+    for (text, z), toks in zip(cases, got):
+        prev = text
+        for cb in range(e.dep_q):
+            lg = e.forward_depth(cb, prev, z, copy=True)
+            tok = sampler.sample(lg[:min(e.audio_vocab, 2048)], 0.8, 50, g)
+            assert tok == int(toks[cb]), (cb, tok, toks.tolist())
+            draws += int(tok != int(np.argmax(lg[:2048])))
+            prev = tok
+    assert draws > 0  # the sampler did not reduce to greedy on these logits
+    e.close()

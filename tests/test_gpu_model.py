@@ -1,4 +1,4 @@
-"""Full-size parity: the BASELINE config-2/3 model (32-layer d4096 temporal
+"""Full-size parity: the config-2/3 model (32-layer d4096 temporal
 transformer, 32000 text head, 8-step depformer) on a 512-slot ring of seeded
 history, decoding frames at positions 700.. (wrapped ring), through the
 reference C ABI and the fused frame graph, in the exact-reduction order

@@ -129,3 +129,20 @@ def test_cli_reports_a_missing_model_and_exits_1(tmp_path, capsys):
     from bmo_jetson_b200 import cli
     assert cli.main([str(tmp_path / "absent.gguf"), "--mode", "depth_cascade"]) == 1
     assert "[bmo_main] ERROR:" in capsys.readouterr().err
+
+
+def test_oracle_synth_generator_matches_library():
+    """The oracle's restatement of the synthetic generator writes the same
+    tensors as libbmo's, bit for bit (the CPU-only benchmark arm uses it)."""
+    from bmo_jetson_b200 import engine, synth
+    from oracle import oracle as orc
+    L, O = engine.lib(), orc.lib()
+    synth.use_generator(L, "bmo_synth_")
+    a = (synth.normal_f32(3, 77, 1001, 0.5, 2.0), synth.f16_normal(3, 78, 999), synth.q4_0_normal(3, 79, 5, 256, 0.02))
+    synth.use_generator(O, "orc_synth_")
+    try:
+        b = (synth.normal_f32(3, 77, 1001, 0.5, 2.0), synth.f16_normal(3, 78, 999), synth.q4_0_normal(3, 79, 5, 256, 0.02))
+    finally:
+        synth.use_generator(L, "bmo_synth_")
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x.view(np.uint8), y.view(np.uint8))
