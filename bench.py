@@ -516,12 +516,16 @@ def ref_kernel_timing(peak_gbs, iters=20, flush_bytes=256 << 20):
     shapes = {"qkv": (12288, 4096), "o_proj": (4096, 4096), "ffn_in": (22528, 4096), "ffn_out": (4096, 11264),
               "text_head": (32000, 4096)}
     for name, (rows, cols) in shapes.items():
+        sys.stderr.write(f"[ref-kernels] {name} {rows}x{cols}\n")
+        sys.stderr.flush()
         w = rng.integers(0, 256, (rows, cols // 32, 18), dtype=np.uint8)
         w[:, :, 0], w[:, :, 1] = 0x00, 0x20  # fp16 scale 2^-7
         W = np.ascontiguousarray(w.reshape(-1))
         x = rng.standard_normal(cols, dtype=np.float32)
         ref_us = R.ref_time_gemv_cold(W, x, rows, cols, ctypes.c_void_p(flush.data_ptr()), flush_bytes, iters)
         assert ref_us > 0, "reference GEMV failed"
+        sys.stderr.write(f"[ref-kernels]   reference {ref_us:.1f} us\n")
+        sys.stderr.flush()
         src = torch.from_numpy(W).to(dev)
         tiled = torch.empty(L.bmo_k_q4_0_tiled_bytes(rows, cols, 0, 0), dtype=torch.uint8, device=dev)
         assert L.bmo_k_repack_q4_0(src.data_ptr(), tiled.data_ptr(), rows, cols, 0, 0, s.cuda_stream) == 0
@@ -536,12 +540,16 @@ def ref_kernel_timing(peak_gbs, iters=20, flush_bytes=256 << 20):
         for _ in range(3):
             ours()
         our_us = median_us(ours)
+        sys.stderr.write(f"[ref-kernels]   ours {our_us:.1f} us\n")
+        sys.stderr.flush()
         alg = rows * cols // 32 * 18 + cols * 4 + rows * 4
         out["gemv"][name] = {"rows": rows, "cols": cols, "bytes": alg, "reference_us": ref_us,
                              "reference_gbs": alg / ref_us / 1e3, "ours_us": our_us, "ours_gbs": alg / our_us / 1e3,
                              "speedup": ref_us / our_us, "ours_frac": alg / our_us / 1e3 / peak_gbs}
         del tiled
     hd, nh, n_ctx, pos = 128, 32, 512, 700
+    sys.stderr.write("[ref-kernels] attention\n")
+    sys.stderr.flush()
     ref_us = R.ref_time_attention_cold(hd, nh, n_ctx, pos, ctypes.c_void_p(flush.data_ptr()), flush_bytes, iters)
     assert ref_us > 0, "reference attention failed"
     q = torch.zeros(nh * hd, device=dev)

@@ -24,10 +24,10 @@
 // tile, each warp leaves its 16 chain values per row in shared memory and a
 // combiner warp (rotating with the tile) adds them in the reference's lane
 // order, runs the 32-leaf tree in registers (lane = row) and applies the
-// fused epilogue.  Two named barriers hand the shared buffer over: the
-// combiner waits until all warps have written ("full"); the writers of the
-// next tile wait until the combiner has read ("empty"), which it signals
-// before its tree and epilogue.  Each CTA owns whole tiles (the chains must
+// fused epilogue.  Named barriers hand the shared buffer over: the combiner
+// waits until all warps have written ("full"); the writers of the next tile
+// wait until the combiner has read ("empty"), which it signals before its
+// tree and epilogue; each tile parity has its own pair.  Each CTA owns whole tiles (the chains must
 // not be split), one CTA per SM at most, sized (registers <= 128, shared
 // memory < half an SM) so the next kernel's CTA fits beside it.
 //
@@ -51,7 +51,18 @@ constexpr int kRing = 2;                  // chunks in flight per warp
 constexpr int kMaxNbx = 384;              // activations up to 12288 elements
 constexpr int kMaxNormCols = 4096;        // RMSNorm weight staged in the chain buffer's space
 constexpr int kNormLoads = kMaxNormCols / kThreads;  // strided elements per thread
-constexpr int kBarFull = 1, kBarEmpty = 2;  // named barrier ids (0 is __syncthreads)
+// Named barrier ids (0 is __syncthreads), one pair per tile parity: tile t
+// hands over through FULL[t % 2] and EMPTY[t % 2].  With one pair, the
+// combiner of tile t (which arrives at EMPTY without waiting and skips the
+// next tile's EMPTY wait) could reach EMPTY again while a warp two tiles
+// behind had not yet completed the earlier instance, and be counted into it.
+// With the parity split the next use of an id cannot start before its
+// previous instance completed (every path to it passes the other parity's
+// barrier, which completes only after this one).
+constexpr int kBarFull0 = 1, kBarEmpty0 = 3;
+#ifndef BMO_GEMV_REF_L2_PREFETCH
+#define BMO_GEMV_REF_L2_PREFETCH 0
+#endif
 
 struct GemvRefSmem {
     uint64_t bar[kWarps][kRing];
@@ -125,6 +136,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
     };
     if (lane == 0)
         for (int i = 0; i < kRing && i < n_mine; ++i) issue(i);
+#if BMO_GEMV_REF_L2_PREFETCH
+    // The rest of this CTA's weights (a contiguous run of whole tiles) go to
+    // L2 now, so HBM keeps streaming through the previous kernel's tail and
+    // this kernel's prologue; the ring then reads them from L2.
+    if (warp == kWarps - 1 && t1 > t0) {
+        const uint8_t *base = a.W.tiles + static_cast<long long>(t0) * cpt * kChunkBytes;
+        const long long total = static_cast<long long>(t1 - t0) * cpt * kChunkBytes;
+        constexpr long long kPiece = 32 * kChunkBytes;  // 147 KB per request
+        for (long long off = lane * kPiece; off < total; off += 32 * kPiece)
+            bulk_prefetch_l2(base + off, static_cast<uint32_t>(total - off < kPiece ? total - off : kPiece));
+    }
+#endif
     if (gbulk && tid == 0) {
         const uint32_t gb = static_cast<uint32_t>(a.W.cols) * 4u;
         mbar_arrive_expect_tx(&S.gbar, gb);
@@ -207,17 +230,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
         }
         // hand the tile's chains to the combiner warp
         const int comb = tt % kWarps;
-        if (tt > 0 && warp != (tt - 1) % kWarps) named_sync(kBarEmpty, kThreads);
+        const int bar_full = kBarFull0 + (tt & 1), bar_empty = kBarEmpty0 + (tt & 1);
+        if (tt > 0 && warp != (tt - 1) % kWarps) named_sync(kBarEmpty0 + ((tt - 1) & 1), kThreads);
 #pragma unroll
         for (int b = 0; b < kChunkBlocks; ++b) {
             S.part[warp][2 * b][lane] = acc[b][0];
             S.part[warp][2 * b + 1][lane] = acc[b][1];
         }
         if (warp != comb) {
-            named_arrive(kBarFull, kThreads);
+            named_arrive(bar_full, kThreads);
             continue;
         }
-        named_sync(kBarFull, kThreads);
+        named_sync(bar_full, kThreads);
         // lane value L[2m + h] = ((A0 + A1) + A2) + A3, A_j from key group 2j + m/8
         float L[32];
 #pragma unroll
@@ -230,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
                 L[2 * m + h] = __fadd_rn(s, S.part[6 + mh][kk][lane]);
             }
         }
-        if (tt + 1 < t1 - t0) named_arrive(kBarEmpty, kThreads);
+        if (tt + 1 < t1 - t0) named_arrive(bar_empty, kThreads);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
