@@ -60,8 +60,15 @@ constexpr int kNormLoads = kMaxNormCols / kThreads;  // strided elements per thr
 // previous instance completed (every path to it passes the other parity's
 // barrier, which completes only after this one).
 constexpr int kBarFull0 = 1, kBarEmpty0 = 3;
-#ifndef BMO_GEMV_REF_L2_PREFETCH
-#define BMO_GEMV_REF_L2_PREFETCH 0
+// Ring chunks each warp issues before griddepcontrol.wait; the rest of the
+// ring is issued after the prologue.  Measured on B200 (frames/s of the
+// decode frame, same box, alternating runs): 1 chunk 328-335, 2 chunks
+// 317-325, none 316 -- with the whole ring in flight the activation load of
+// the prologue queues behind the weight copies, with none the weight stream
+// starts late.  A look-ahead of 3 or 6 more chunks into L2
+// (cp.async.bulk.prefetch.L2) measured 308-310.
+#ifndef BMO_GEMV_REF_PRE_WAIT
+#define BMO_GEMV_REF_PRE_WAIT 1
 #endif
 
 struct GemvRefSmem {
@@ -135,19 +142,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
         bulk_load(S.ring[warp][i % kRing], a.W.tiles + k * kChunkBytes, kChunkBytes, bar, pol);
     };
     if (lane == 0)
-        for (int i = 0; i < kRing && i < n_mine; ++i) issue(i);
-#if BMO_GEMV_REF_L2_PREFETCH
-    // The rest of this CTA's weights (a contiguous run of whole tiles) go to
-    // L2 now, so HBM keeps streaming through the previous kernel's tail and
-    // this kernel's prologue; the ring then reads them from L2.
-    if (warp == kWarps - 1 && t1 > t0) {
-        const uint8_t *base = a.W.tiles + static_cast<long long>(t0) * cpt * kChunkBytes;
-        const long long total = static_cast<long long>(t1 - t0) * cpt * kChunkBytes;
-        constexpr long long kPiece = 32 * kChunkBytes;  // 147 KB per request
-        for (long long off = lane * kPiece; off < total; off += 32 * kPiece)
-            bulk_prefetch_l2(base + off, static_cast<uint32_t>(total - off < kPiece ? total - off : kPiece));
-    }
-#endif
+        for (int i = 0; i < BMO_GEMV_REF_PRE_WAIT && i < n_mine; ++i) issue(i);
     if (gbulk && tid == 0) {
         const uint32_t gb = static_cast<uint32_t>(a.W.cols) * 4u;
         mbar_arrive_expect_tx(&S.gbar, gb);
@@ -198,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
     if (tid < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid, h0, v0, scale, gam, c == 0);
     if (tid + kThreads < nbx) quantize_x_block<PRO>(a, S.xq, S.xds, tid + kThreads, h1, v1, scale, gam, c == 0);
     __syncthreads();  // also ends the prologue's use of S.gamma, which S.part overlays
+    if (lane == 0)  // the rest of the ring (its slots were untouched by the prologue)
+        for (int i = BMO_GEMV_REF_PRE_WAIT; i < kRing && i < n_mine; ++i) issue(i);
 
     // ---- main loop: each tile's key-group chains, then the combine ----
     int i = 0;           // chunks of this warp passed through
