@@ -1049,7 +1049,6 @@ void Engine::finish_call() {
         std::string what;
         if (st & (1 << 1)) what += " a bulk copy wait timed out;";
         if (st & (1 << 2)) what += " launch arguments inconsistent with the weight layout;";
-        if (st & (1 << 3)) what += " a grid barrier timed out;";
         if (st & (1 << 4)) what += " a tensor-parallel peer's partial sums did not arrive;";
         throw std::runtime_error("device status " + std::to_string(st) + ":" + what);
     }

@@ -19,8 +19,8 @@ enum : int {
     kErrNone = 0,
     kErrTmaTimeout = 1,    // a bulk copy did not land within the wait bound
     kErrBadShape = 2,      // launch arguments inconsistent with the weight layout
-    kErrBarrierTimeout = 3,  // a grid barrier of the persistent frame kernel did not complete
-    kErrPeerTimeout = 4,     // a tensor-parallel peer's partial sums did not arrive within the wait bound
+    kErrReserved3 = 3,     // unused (no kernel raises it); kept so the other codes keep their bits
+    kErrPeerTimeout = 4,   // a tensor-parallel peer's partial sums did not arrive within the wait bound
 };
 
 // Upper bound on mbarrier polls before a wait gives up (~1-2 s with back-off).
