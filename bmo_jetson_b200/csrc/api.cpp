@@ -103,6 +103,7 @@ bmo_handle_t *bmo_init_ex(const char *gguf_path, int n_ctx, int device, int kv_t
     c.pdl = !(flags & BMO_FLAG_NO_PDL);
     if (flags & BMO_FLAG_EXACT) c.semantics = 0;
     else if (flags & BMO_FLAG_REF_ORDER) c.semantics = 1;
+    c.dep_cluster = (flags & BMO_FLAG_DEP_CLUSTER) != 0;
     return create(gguf_path, n_ctx, c);
 }
 
@@ -232,6 +233,8 @@ int bmo_capture_graphs(bmo_handle_t *h) {
 int bmo_has_cuda_graphs(bmo_handle_t *h) { return (h && h->eng->graphs_captured()) ? 1 : 0; }
 
 int bmo_get_ref_order(bmo_handle_t *h) { return (h && h->eng->ref_order()) ? 1 : 0; }
+
+int bmo_get_dep_cluster(bmo_handle_t *h) { return (h && h->eng->dep_cluster()) ? 1 : 0; }
 
 const char *bmo_last_error(bmo_handle_t *h) { return (!h || h->last_error.empty()) ? nullptr : h->last_error.c_str(); }
 

@@ -6,6 +6,7 @@
 //   temporal      embed -> 32 x {QKV, attention, O, FFN-in, FFN-out} -> head
 //   depth[cb]     one depformer step (reference bmo_forward_depth)
 //   cascade       dep_q depformer steps with greedy argmax chaining on device
+//                 (opt-in: one cluster kernel, kernels/dep_cascade.cu)
 //   frame         temporal + greedy text token + cascade
 // Each op list runs one kernel per op, chained with programmatic dependent
 // launch inside CUDA graphs.  Two summation orders exist for the GEMV and
@@ -43,6 +44,10 @@ struct EngineConfig {
     // else the exact-reduction order; 0: exact-reduction order; 1: the
     // reference order or an error
     int semantics = -1;
+    // reference order: run the greedy depformer cascade as one launch on a
+    // thread-block cluster instead of one kernel per op (same results; opt-in:
+    // measured slower on B200, its 16 SMs are compute-bound)
+    bool dep_cluster = false;
     // tensor parallel (batch-1 latency mode): tp_size >= 1 makes this engine
     // rank tp_rank of tp_size, holding the attention heads and FFN columns of
     // its shard; tp_id is the group's NCCL unique id
@@ -105,6 +110,7 @@ public:
     void capture_all();
     bool graphs_captured() const { return graphs_ready_; }
     bool ref_order() const { return ref_order_; }
+    bool dep_cluster() const { return dep_cluster_; }
     bool tp_exchange() const { return tp_p2p_; }
 
     // ---- batched sessions: up to kBatchMax independent sessions stepped
@@ -252,6 +258,13 @@ private:
 
     // summation order of the single-session path (see the header comment)
     bool ref_order_ = false;
+
+    // the greedy cascade on one thread-block cluster (reference order)
+    bool dep_cluster_ = false;
+    DepOp *dep_ops_d_ = nullptr;
+    DepCascadeArgs dep_args_{};
+    size_t dep_smem_ = 0;
+    void setup_dep_cascade();
 };
 
 }  // namespace bmo

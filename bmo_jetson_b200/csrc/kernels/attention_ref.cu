@@ -28,7 +28,7 @@
 // dimensions.  The depformer (window <= 8) runs with NSPLIT = 1.
 #include <cooperative_groups.h>
 
-#include "common.cuh"
+#include "attention_ref_dev.cuh"
 #include "../launch.h"
 
 namespace cg = cooperative_groups;
@@ -66,7 +66,6 @@ template <int HD, int NSPLIT>
 __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constant__ AttnArgs a) {
     using Lay = RefAttnLayout<HD, NSPLIT>;
     constexpr int kDims = Lay::kDims;
-    constexpr int kGroups = HD / 32;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Lay lay(a.n_ctx);
     float *sq = reinterpret_cast<float *>(smem_raw);
@@ -74,7 +73,7 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constan
     __half *kb = reinterpret_cast<__half *>(smem_raw + lay.off_k);
     __half *vb = reinterpret_cast<__half *>(smem_raw + lay.off_v);
     float *red = reinterpret_cast<float *>(smem_raw + lay.off_red);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int r = blockIdx.x, h = blockIdx.y;
 
     const int pos = *a.pos;  // copied to the device before this graph's first kernel
@@ -123,101 +122,23 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constan
     __syncthreads();
 
     // ---- scores of positions [i0, i1): thread = (position, 32-dim group) ----
-    const float scale = a.scale;
-    {
-        const int g = tid % kGroups;  // kGroups divides 32: a position's groups are adjacent lanes
-        float qg[32];
+    attn_ref_scores<HD, kThreads>(sq, kb, i0, i1, a.scale, tid, [&](int i, float s) {
+        if constexpr (NSPLIT == 1) {
+            ss[i] = s;
+        } else {
+            cg::cluster_group cl = cg::this_cluster();
 #pragma unroll
-        for (int d = 0; d < 32; ++d) qg[d] = sq[32 * g + d];
-        const int tasks = (i1 - i0) * kGroups;
-        for (int u0 = 0; u0 < tasks; u0 += kThreads) {
-            const int u = u0 + tid;
-            const int i = i0 + u / kGroups;
-            const bool on = u < tasks;
-            float p[32];
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (on ? (i - i0) : 0) * HD + 32 * g);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint4 w = kr[j];
-                const __half2 *hp = reinterpret_cast<const __half2 *>(&w);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 kf = __half22float2(hp[e]);
-                    p[8 * j + 2 * e] = __fmul_rn(qg[8 * j + 2 * e], kf.x);
-                    p[8 * j + 2 * e + 1] = __fmul_rn(qg[8 * j + 2 * e + 1], kf.y);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int d = 0; d < o; ++d) p[d] = __fadd_rn(p[d], p[d + o]);
-            // ((0 + W0) + W1) + ... over the groups, in group order
-            const int base = lane & ~(kGroups - 1);
-            float tot = 0.0f;
-#pragma unroll
-            for (int k = 0; k < kGroups; ++k) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, p[0], base + k));
-            if (on && g == 0) {
-                const float s = __fmul_rn(tot, scale);
-                if constexpr (NSPLIT == 1) {
-                    ss[i] = s;
-                } else {
-                    cg::cluster_group cl = cg::this_cluster();
-#pragma unroll
-                    for (int rr = 0; rr < NSPLIT; ++rr) *cl.map_shared_rank(ss + i, rr) = s;
-                }
-            }
+            for (int rr = 0; rr < NSPLIT; ++rr) *cl.map_shared_rank(ss + i, rr) = s;
         }
-    }
+    });
     if constexpr (NSPLIT == 1) __syncthreads();
     else cg::this_cluster().sync();
 
     // ---- softmax over the whole window, the reference's thread pattern ----
-    float m = -1e20f;
-    for (int i = tid; i < W; i += kThreads) m = ss[i] > m ? ss[i] : m;
-    m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    float M = red[0];
-#pragma unroll
-    for (int w = 1; w < kThreads / 32; ++w) M = red[w] > M ? red[w] : M;
-    __syncthreads();
-    if (tid < HD) {  // the reference runs head_dim threads
-        float ls = 0.0f;
-        for (int i = tid; i < W; i += HD) {
-            const float e = expf(__fsub_rn(ss[i], M));
-            ss[i] = e;
-            ls = __fadd_rn(ls, e);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ls = __fadd_rn(ls, __shfl_down_sync(0xffffffffu, ls, o));
-        if (lane == 0) red[8 + warp] = ls;
-    }
-    __syncthreads();
-    float se = 0.0f;
-#pragma unroll
-    for (int w = 0; w < HD / 32; ++w) se = __fadd_rn(se, red[8 + w]);
-    const float inv = se > 0.0f ? __fdiv_rn(1.0f, se) : 0.0f;
-    for (int i = tid; i < W; i += kThreads) ss[i] = __fmul_rn(ss[i], inv);
-    __syncthreads();
+    attn_ref_softmax<HD, kThreads>(ss, W, red, tid, [] { __syncthreads(); });
 
     // ---- weighted sum of V: one sequential chain per dimension ----
-    if (tid < kDims) {
-        float acc = 0.0f;
-        const __half *vcol = vb + tid;
-        int i = 0;
-        for (; i + 8 <= W; i += 8) {
-            float pv[8], vv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                pv[j] = ss[i + j];
-                vv[j] = __half2float(vcol[(i + j) * kDims]);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc = __fmaf_rn(pv[j], vv[j], acc);
-        }
-        for (; i < W; ++i) acc = __fmaf_rn(ss[i], __half2float(vcol[i * kDims]), acc);
-        out[r * kDims + tid] = acc;
-    }
+    if (tid < kDims) out[r * kDims + tid] = attn_ref_vchain(ss, vb + tid, W, kDims);
 }
 
 // ---------------------------------------------------------------------------

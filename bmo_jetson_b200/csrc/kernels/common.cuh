@@ -119,8 +119,12 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 __device__ __forceinline__ void prefetch_l1(const void *p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
-// Named barrier over the first `n` threads of the CTA (n a multiple of 32).
+// Named barrier over `n` threads of the CTA (n a multiple of 32): wait, or
+// arrive without waiting.
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
 // Split thread-block-cluster barrier (all threads of every CTA take part).
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -140,6 +144,14 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// The reference's warp reduction: v += __shfl_down_sync(v, o) for o = 16 .. 1
+// (lane 0 holds the sum), each add rounded.
+__device__ __forceinline__ float shfl_down_tree(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
     return v;
 }
 

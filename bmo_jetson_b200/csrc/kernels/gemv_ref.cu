@@ -87,25 +87,6 @@ struct GemvRefSmem {
     int err;
 };
 
-// Chunks of a tile in the reference's key order (see the header comment).
-struct KeyChains {
-    int nm;     // main chunks per tile: 8 * (blocks / 64)
-    int nmg;    // main chunks per key group
-    int ntail;  // tail chunks per tile (the last may hold padding blocks)
-    __device__ int len(int g) const { return nmg + ((g < 2 && ntail > g) ? (ntail - g + 1) / 2 : 0); }
-    __device__ int chunk(int g, int p) const { return p < nmg ? g + 8 * p : nm + g + 2 * (p - nmg); }
-};
-
-__device__ __forceinline__ void named_arrive(int id, int n) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ float shfl_down_tree(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
-    return v;
-}
-
 }  // namespace
 
 template <int PRO, int EPI>
@@ -118,10 +99,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
     const int t0 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * c / G);
     const int t1 = static_cast<int>(static_cast<long long>(a.W.n_tiles) * (c + 1) / G);
     const int nb = a.W.cols / 32, nbx = a.W.nbx;
-    KeyChains kc;
-    kc.nmg = nb / 64;
-    kc.nm = 8 * kc.nmg;
-    kc.ntail = cpt - kc.nm;
+    const KeyChains kc = KeyChains::of(nb, cpt);
     const int my_len = kc.len(warp);
     const int n_mine = my_len * (t1 - t0);
     const bool gbulk = PRO == kProNorm && (reinterpret_cast<uintptr_t>(a.gamma) & 15) == 0;

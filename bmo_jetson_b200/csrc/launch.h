@@ -44,6 +44,16 @@ cudaError_t launch_attention_ref(const AttnArgs &a, int head_dim, bool split, cu
 bool attn_ref_supported(int head_dim, int n_ctx, bool split);
 int attn_ref_max_ctx();
 
+// The depformer's greedy cascade as one launch on a cluster of `heads` CTAs
+// (kernels/dep_cascade.cu), reference fp32 order.
+cudaError_t launch_dep_cascade(const DepCascadeArgs &a, size_t smem_bytes, cudaStream_t s, bool pdl);
+size_t dep_cascade_smem_bytes(int dim, int ffn, int n_embd, int n_layers, int n_ctx);
+int dep_cascade_configure(int heads, size_t smem_bytes);  // resident clusters on the current device (0: cannot run)
+int dep_cascade_part_slots();
+int dep_cascade_max_cluster();
+int dep_cascade_max_local_tiles();
+int dep_cascade_head_dim();
+
 // Batched sessions (kernels/batch.cu).  Stage: per-session RMSNorm + Q8_1
 // into the block-major layout (and the embedding token); GEMM: the skinny
 // Q4_0 x Q8_1 product of all sessions with a fused epilogue, `grid` CTAs

@@ -12,12 +12,43 @@
 
 #include <stdint.h>
 
+#if defined(__CUDACC__)
+#define BMO_HD __host__ __device__
+#else
+#define BMO_HD
+#endif
+
 namespace bmo {
 
 constexpr int kTileRows = 32;
 constexpr int kChunkBlocks = 8;
 constexpr int kChunkQsBytes = kChunkBlocks * kTileRows * 16;   // 4096
 constexpr int kChunkBytes = kChunkQsBytes + kChunkBlocks * kTileRows * 2;  // 4608
+
+// The chunks of one row tile in the reference GEMV's chain order.  The
+// reference (bmo_cuda_kernels.cu:560-683) gives lane l = 2m + h of a row's
+// warp half block h of the blocks m (mod 16); its accumulator j chains blocks
+// 64 i + 16 j + m, and blocks past the last whole group of 64 (the tail, in
+// steps of 16) continue accumulator 0.  A chunk's 8 blocks therefore share one
+// key group G = 2 j + m / 8: main chunk c (tile-local) has G = c % 8 and chain
+// position c / 8, tail chunk nm + t has G = t % 2 and position nmg + t / 2.
+struct KeyChains {
+    int nm;     // main chunks per tile: 8 * (blocks / 64)
+    int nmg;    // main chunks per key group
+    int ntail;  // tail chunks per tile (the last may hold padding blocks)
+    BMO_HD static KeyChains of(int nb, int cpt) {
+        KeyChains k;
+        k.nmg = nb / 64;
+        k.nm = 8 * k.nmg;
+        k.ntail = cpt - k.nm;
+        return k;
+    }
+    // chunks of key group g, and the tile-local index of its p-th chunk
+    BMO_HD int len(int g) const { return nmg + ((g < 2 && ntail > g) ? (ntail - g + 1) / 2 : 0); }
+    BMO_HD int chunk(int g, int p) const { return p < nmg ? g + 8 * p : nm + g + 2 * (p - nmg); }
+    // key groups that hold chunks (the others contribute +0 to every lane)
+    BMO_HD int groups() const { return nmg > 0 ? 8 : (ntail < 2 ? ntail : 2); }
+};
 
 // Row order inside a tile.
 enum RowPerm : int {
@@ -178,6 +209,38 @@ struct FramePhase {
     int count;     // kPhAllReduce, kPhResidAdd
 };
 
+// ---- the depformer cascade as one launch on one thread-block cluster ----
+// One entry per weight matrix in execution order: per codebook step, the
+// input projection, then per layer QKV, O, FFN-in and FFN-out, then the head.
+enum DepOpKind : int { kDepIn = 0, kDepQKV = 1, kDepO = 2, kDepFfnIn = 3, kDepFfnOut = 4, kDepHead = 5 };
+constexpr int kDepMaxSteps = 8;
+struct DepOp {
+    QMatDesc W;
+    const float *gamma;        // RMSNorm weight of the input (QKV, FFN-in), else null
+    const float *gamma_ahead;  // the RMSNorm weight two normalised ops later (prefetched into this one's buffer)
+    int kind;                  // DepOpKind
+    int layer, step;
+    int norm_idx;              // ordinal among the normalised ops (selects the weight buffer and its phase)
+};
+struct DepCascadeArgs {
+    const DepOp *ops;          // device table of n_ops entries
+    int n_ops;
+    const float *gamma0[2];    // RMSNorm weights of the first two normalised ops
+    EmbTable emb[kDepMaxSteps];  // token table of step cb's input (cb 0: the text-token table)
+    const float *z;            // [n_embd] the temporal transformer's normalised output
+    int n_embd;
+    TokenSrc first;            // step 0's input token (the text token)
+    int *tok_out;              // [1 + dep_q]: the text token, then each step's argmax
+    float *logits;             // [dep_q][logits_stride]
+    int logits_stride;
+    float2 *pairs;             // optional [dep_q][pairs_stride] per-tile (max, argmax)
+    int pairs_stride;
+    __half *k_cache, *v_cache; // [n_layers][heads][n_ctx][hd] fp16 (written for the per-step API)
+    int dep_q, n_layers, dim, ffn, heads, hd, n_ctx, argmax_limit;
+    float eps, scale;
+    int *status;
+};
+
 // ---- batched sessions (config 4) ----
 // Q8_1 activations of S sessions, block-major, padded to P = S rounded up to
 // 16 sessions, laid out as the tensor core's B operand with the two half
@@ -193,10 +256,7 @@ struct FramePhase {
 // (M = 1.5 * 2^23), then P / 2 float2 {-4 s8[2p], -4 s8[2p+1]}.  The 8 blocks of
 // chunk kc are one contiguous run of 512 P bytes (and 96 P bytes of scales).
 constexpr int kBatchMax = 64;  // sessions per launch
-#if defined(__CUDACC__)
-__host__ __device__
-#endif
-constexpr int batch_pad(int n_sess) { return (n_sess + 15) & ~15; }
+BMO_HD constexpr int batch_pad(int n_sess) { return (n_sess + 15) & ~15; }
 constexpr int kBatchMaxTokens = 64;
 
 // Per-call inputs of a batched frame (one host->device copy): row s runs

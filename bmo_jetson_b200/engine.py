@@ -29,7 +29,7 @@ KV_F16, KV_Q4_0 = 0, 1
 FLAG_NO_GRAPHS, FLAG_NO_PDL = 1, 2
 # summation order (include/bmo_ext.h): default the reference kernels' own
 # fp32 order where the model allows; EXACT: double sums rounded once
-FLAG_EXACT, FLAG_REF_ORDER = 8, 16
+FLAG_EXACT, FLAG_REF_ORDER, FLAG_DEP_CLUSTER = 8, 16, 32
 
 
 def lib() -> ctypes.CDLL:
@@ -53,7 +53,7 @@ def lib() -> ctypes.CDLL:
     for name in ("bmo_get_n_layers", "bmo_get_n_embd", "bmo_get_n_codebooks", "bmo_get_dep_q", "bmo_get_text_vocab",
                  "bmo_get_audio_vocab", "bmo_get_n_attn_heads", "bmo_get_head_dim", "bmo_capture_graphs",
                  "bmo_has_cuda_graphs", "bmo_get_kv_type", "bmo_get_n_ctx", "bmo_get_n_kv_heads", "bmo_get_device",
-                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order"):
+                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order", "bmo_get_dep_cluster"):
         fn = getattr(L, name)
         fn.argtypes = [vp]
         fn.restype = i
@@ -248,6 +248,11 @@ class BMOEngine:
         (bit-identical to the reference's chain), False for the exact order."""
         return bool(lib().bmo_get_ref_order(self._h))
 
+    @property
+    def dep_cluster(self) -> bool:
+        """True when greedy depformer cascades run as one cluster launch."""
+        return bool(lib().bmo_get_dep_cluster(self._h))
+
     def forward_temporal(self, tokens: np.ndarray, copy: bool = False) -> Tuple[np.ndarray, np.ndarray]:
         assert tokens.dtype == np.int32 and tokens.shape == (self.n_codebooks,), (
             f"Expected int32 array of shape ({self.n_codebooks},), got {tokens.dtype} shape {tokens.shape}")
@@ -361,7 +366,7 @@ class BMOEngine:
             raise RuntimeError(f"bmo_forward_layers rc={rc}: {_err(self._h)}")
         return out
 
-    TAPS = {"q": 0, "v": 1, "attn": 2, "xmid": 3, "act": 4, "z": 5, "rope": 6}
+    TAPS = {"q": 0, "v": 1, "attn": 2, "xmid": 3, "act": 4, "z": 5, "rope": 6, "dlogits": 7}
 
     def debug_tap(self, name: str) -> np.ndarray:
         """An activation buffer as left by the last call (see bmo_debug_tap)."""

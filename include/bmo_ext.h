@@ -31,6 +31,11 @@ enum {
      * environment variable BMO_SEMANTICS=exact|ref overrides the flags. */
     BMO_FLAG_EXACT = 8,      /* exact-reduction order: every sum in double, rounded once */
     BMO_FLAG_REF_ORDER = 16, /* the reference order, or fail when the model or ring does not allow it */
+    /* Reference order: run the greedy depformer cascade as one launch on a
+     * thread-block cluster (one CTA per depformer head) instead of one kernel
+     * per op, when the model fits it.  Same results; slower on B200 for the
+     * 7B depformer (its 16 SMs are compute-bound), so off by default. */
+    BMO_FLAG_DEP_CLUSTER = 32,
 };
 
 /* bmo_init with an explicit CUDA device, KV ring format and flags.
@@ -49,6 +54,9 @@ BMO_API size_t bmo_get_device_bytes(bmo_handle_t *h);
 /* 1 when the handle computes in the reference kernels' fp32 order, 0 for
  * the exact-reduction order (see BMO_FLAG_EXACT). */
 BMO_API int bmo_get_ref_order(bmo_handle_t *h);
+/* 1 when greedy depformer cascades run as one cluster launch (see
+ * BMO_FLAG_DEP_CLUSTER), 0 when they run one kernel per op. */
+BMO_API int bmo_get_dep_cluster(bmo_handle_t *h);
 
 /* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
  * slots [slot0, slot0+n) of temporal layer `layer`; rows are
@@ -81,7 +89,9 @@ BMO_API int bmo_forward_layers(bmo_handle_t *h, const float *x_in, int pos, int 
  * engine's activation buffer `which` as left by the last call into out
  * (max_floats).  which: 0 rotated q, 1 raw v, 2 attention output, 3
  * post-attention residual, 4 SwiGLU activation, 5 normed hidden z, 6 RoPE
- * (cos, sin) table.  Returns floats copied or -1. */
+ * (cos, sin) table, 7 the audio logits of every depformer step [dep_q][audio
+ * vocabulary] (the last cascade's, or of the steps run since).  Returns
+ * floats copied or -1. */
 BMO_API int bmo_debug_tap(bmo_handle_t *h, int which, float *out, int max_floats);
 
 /* Asynchronous device-resident frame: tokens_dev (device int32[num_codebooks])

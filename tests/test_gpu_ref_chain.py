@@ -81,6 +81,9 @@ def test_frames_bit_identical_to_reference_chain(name, model_dir):
             assert text == int(exp[f"text{f}"])
             audio = e.forward_depth_cascade(text, z, temp=0.0, top_k=0)
             np.testing.assert_array_equal(audio, exp[f"audio{f}"], err_msg=f"{name} frame {f} audio tokens")
+            # the greedy cascade's own logits (one cluster launch where the model allows it)
+            _same_or_digest(e.debug_tap("dlogits").reshape(e.dep_q, -1), exp, f"dlogits{f}",
+                            f"{name} frame {f} cascade logits")
             prev, dl = text, []
             for cb in range(e.dep_q):
                 dl.append(e.forward_depth(cb, prev, z, copy=True))
