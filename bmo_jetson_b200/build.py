@@ -67,6 +67,10 @@ def _compile(cmd):
 def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
     cu, cpp = _sources()
+    live = {_obj_path(s) for s in cu + cpp}
+    for o in glob.glob(os.path.join(OBJ, "*.o")):  # objects of sources that no longer exist
+        if o not in live:
+            os.remove(o)
     newest = max((os.path.getmtime(h) for h in _headers()), default=0.0)
     cmds = []
     objs = []

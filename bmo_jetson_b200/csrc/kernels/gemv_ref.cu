@@ -178,12 +178,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
                 if (!mbar_wait(&S.gbar, 0)) atomicOr(&S.err, 1);
                 gam = S.gamma;
             }
+#pragma unroll 4
             for (int mm = 0; mm < nr; ++mm) {
                 float *e = scr + mm * 33 + lane;
                 *e = __fmul_rn(__fmul_rn(*e, scale), gam[(warp + kWarps * mm) * 32 + lane]);
             }
         }
         if (c == 0 && a.xn_out)
+#pragma unroll 4
             for (int mm = 0; mm < nr; ++mm) a.xn_out[(warp + kWarps * (m0 + mm)) * 32 + lane] = scr[mm * 33 + lane];
         __syncwarp();
         if (lane < nr) {
@@ -203,12 +205,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
             sid[lane] = id;
         }
         __syncwarp();
+        const bool q8o = c == 0 && a.q8_out;
+#pragma unroll 4
         for (int mm = 0; mm < nr; ++mm) {
             int qi = __float2int_rz(roundf(__fmul_rn(scr[mm * 33 + lane], sid[mm])));
             qi = max(-128, min(127, qi));
             const int b = warp + kWarps * (m0 + mm);
             S.xq[b * 32 + lane] = static_cast<int8_t>(qi);
-            if (c == 0 && a.q8_out) a.q8_out[static_cast<size_t>(b) * 36 + 4 + lane] = static_cast<uint8_t>(qi);
+            if (q8o) a.q8_out[static_cast<size_t>(b) * 36 + 4 + lane] = static_cast<uint8_t>(qi);
         }
         __syncwarp();
     }
