@@ -93,7 +93,8 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
     lib_time = os.path.getmtime(LIB) if os.path.exists(LIB) else -1.0
     if cmds or force or lib_time < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        _compile([NVCC] + ARCH + ["-shared", "-ccbin", CXX, "-o", tmp] + objs + ["-cudart", "static", "-lpthread", "-ldl"])
+        _compile([NVCC] + ARCH + ["-shared", "-ccbin", CXX, "-o", tmp] + objs +
+                 ["-cudart", "static", "-lpthread", "-ldl", "-Xlinker", "--no-undefined"])
         os.replace(tmp, LIB)
     return LIB
 

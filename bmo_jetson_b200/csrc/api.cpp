@@ -234,7 +234,10 @@ int bmo_has_cuda_graphs(bmo_handle_t *h) { return (h && h->eng->graphs_captured(
 
 int bmo_get_ref_order(bmo_handle_t *h) { return (h && h->eng->ref_order()) ? 1 : 0; }
 
-int bmo_get_dep_cluster(bmo_handle_t *h) { return (h && h->eng->dep_cluster()) ? 1 : 0; }
+int bmo_get_dep_mode(bmo_handle_t *h) {
+    if (!h) return 0;
+    return h->eng->dep_grid() ? 2 : h->eng->dep_cluster() ? 1 : 0;
+}
 
 const char *bmo_last_error(bmo_handle_t *h) { return (!h || h->last_error.empty()) ? nullptr : h->last_error.c_str(); }
 

@@ -94,23 +94,26 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     setup_dep_cascade();
 }
 
-// On request (BMO_FLAG_DEP_CLUSTER or BMO_DEP_CLUSTER=1), the greedy cascade
-// as one cluster kernel when the depformer fits its design (reference order,
-// one GPU, 64-dimension heads, one CTA per head, at most 16 heads, the
-// shared-memory and per-op tile limits) and the device can co-schedule the
-// cluster; otherwise the per-op chain.  Measured on B200 for the 7B
-// depformer: 1.59-1.67 ms per cascade against 1.19 ms for the per-op chain --
-// on 16 SMs the reference-order dot products are compute- and
-// latency-bound (~700 us), so the per-op chain, which spreads every op over
-// all SMs, stays the default.
+// The greedy cascade as one launch when the depformer fits the kernels'
+// design (reference order, one GPU, 64-dimension heads, the shared-memory
+// and per-op tile limits) and the device can run it; otherwise the per-op
+// chain.  Two forms: over every SM with epoch-tagged exchanges in global
+// memory (BMO_DEP_GRID=1), or on one thread-block cluster of one CTA per head
+// (BMO_FLAG_DEP_CLUSTER / BMO_DEP_CLUSTER=1; measured on B200 for the 7B
+// depformer at 1.59-1.67 ms per cascade against 1.19 ms for the per-op
+// chain -- on 16 SMs the reference-order dot products are compute- and
+// latency-bound).
 void Engine::setup_dep_cascade() {
-    dep_cluster_ = false;
-    if (!cfg_.dep_cluster && env_int("BMO_DEP_CLUSTER", 0) == 0) return;
+    dep_cluster_ = dep_grid_ = false;
+    const bool want_cluster = cfg_.dep_cluster || env_int("BMO_DEP_CLUSTER", 0) != 0;
+    const bool want_grid = !want_cluster && env_int("BMO_DEP_GRID", 0) != 0;
+    if (!want_cluster && !want_grid) return;
     if (!ref_order_ || tensor_parallel || !has_dep_tables || dep_q <= 0 || dep_q > kDepMaxSteps) return;
-    if (dep_hd != dep_cascade_head_dim() || dep_heads < 1 || dep_heads > dep_cascade_max_cluster() ||
-        dep_heads * dep_hd != dep_dim || dep_n_ctx != dep_q)
+    if (dep_hd != dep_cascade_head_dim() || dep_heads < 1 || dep_heads * dep_hd != dep_dim || dep_n_ctx != dep_q)
         return;
-    const int cs = dep_heads;
+    const int grid = want_cluster ? dep_heads : std::min(sm_count, dep_cascade_ll_max_grid());
+    if (want_cluster && dep_heads > dep_cascade_max_cluster()) return;
+    if (want_grid && dep_heads > grid) return;
     std::vector<DepOp> ops;
     auto add = [&](const QMatDesc &W, int kind, int layer, int step, const float *gamma) {
         DepOp o{};
@@ -146,8 +149,14 @@ void Engine::setup_dep_cascade() {
             return;
         if (o.kind == kDepFfnIn && W.swiglu_f != dep_ffn) return;
         const int ng = KeyChains::of(W.cols / 32, W.cpt).groups();
-        const int max_loc = o.kind == kDepQKV ? 3 * dep_hd / kTileRows : (W.n_tiles + cs - 1) / cs;
-        if (max_loc * ng > dep_cascade_part_slots() || max_loc > dep_cascade_max_local_tiles()) return;
+        if (want_cluster) {
+            const int max_loc = o.kind == kDepQKV ? 3 * dep_hd / kTileRows : (W.n_tiles + grid - 1) / grid;
+            if (max_loc * ng > dep_cascade_part_slots() || max_loc > dep_cascade_max_local_tiles()) return;
+        } else {
+            const int max_loc = (W.n_tiles + grid - 1) / grid;
+            if (max_loc * ng > dep_cascade_ll_items() || max_loc > dep_cascade_ll_max_local_tiles()) return;
+            if (o.kind != kDepIn && W.cols > dep_cascade_ll_max_in()) return;
+        }
         if (o.gamma) {
             if (reinterpret_cast<uintptr_t>(o.gamma) & 15) return;
             o.norm_idx = static_cast<int>(norm_ops.size());
@@ -156,14 +165,32 @@ void Engine::setup_dep_cascade() {
     }
     for (size_t n = 0; n + 2 < norm_ops.size(); ++n) ops[norm_ops[n]].gamma_ahead = ops[norm_ops[n + 2]].gamma;
     if (dep_dim % 4 || n_embd % 32 || dep_ffn % 32) return;
-    const size_t smem = dep_cascade_smem_bytes(dep_dim, dep_ffn, n_embd, kDepLayers, dep_n_ctx);
-    if (dep_cascade_configure(cs, smem) < 1) return;
+    const int n_phases = dep_q * (2 + 5 * kDepLayers);
+    const int ll_stride = std::max(std::max(3 * dep_dim, dep_ffn), 2 * grid);
+    size_t smem = 0;
+    if (want_cluster) {
+        smem = dep_cascade_smem_bytes(dep_dim, dep_ffn, n_embd, kDepLayers, dep_n_ctx);
+        if (dep_cascade_configure(dep_heads, smem) < 1) return;
+    } else {
+        if (n_phases > dep_cascade_ll_phases() || 2 * grid > dep_cascade_ll_max_in() ||
+            static_cast<int>(ops.size()) > dep_cascade_ll_max_ops())
+            return;
+        // the input projection's activation (n_embd) is quantised through the chain buffers
+        const int rows = std::min((n_embd / 32 + 7) / 8, 32);
+        if (static_cast<size_t>(8 * (rows * 33 + 32)) * 4 > static_cast<size_t>(dep_cascade_ll_items()) * 2048) return;
+        smem = dep_cascade_ll_smem_bytes(dep_dim, dep_ffn, n_embd, kDepLayers, dep_n_ctx);
+        if (dep_cascade_ll_configure(smem, sm_count) < grid) return;
+    }
 
-    void *table = nullptr;
-    ck(cudaMalloc(&table, sizeof(DepOp) * ops.size()), "cudaMalloc depformer op table");
-    allocs_.push_back(table);
-    device_bytes += sizeof(DepOp) * ops.size();
-    dep_ops_d_ = static_cast<DepOp *>(table);
+    auto dalloc = [&](size_t bytes) -> void * {
+        void *q = nullptr;
+        ck(cudaMalloc(&q, std::max<size_t>(bytes, 16)), "cudaMalloc depformer cascade");
+        ck(cudaMemset(q, 0, std::max<size_t>(bytes, 16)), "cudaMemset depformer cascade");
+        allocs_.push_back(q);
+        device_bytes += bytes;
+        return q;
+    };
+    dep_ops_d_ = static_cast<DepOp *>(dalloc(sizeof(DepOp) * ops.size()));
     ck(cudaMemcpy(dep_ops_d_, ops.data(), sizeof(DepOp) * ops.size(), cudaMemcpyHostToDevice), "depformer op table");
     DepCascadeArgs &a = dep_args_;
     a = DepCascadeArgs{};
@@ -190,8 +217,18 @@ void Engine::setup_dep_cascade() {
     a.eps = norm_eps;
     a.scale = 1.0f / std::sqrt(static_cast<float>(dep_hd));
     a.status = status_;
+    if (want_grid) {
+        a.ll = static_cast<unsigned long long *>(dalloc(sizeof(unsigned long long) * n_phases * ll_stride));
+        a.ll_stride = ll_stride;
+        a.seq = static_cast<unsigned *>(dalloc(sizeof(unsigned)));
+        const unsigned one = 1;  // epoch 0 is what zeroed exchange words carry
+        ck(cudaMemcpy(a.seq, &one, sizeof one, cudaMemcpyHostToDevice), "depformer launch counter");
+        dep_grid_ctas_ = grid;
+        dep_grid_ = true;
+    } else {
+        dep_cluster_ = true;
+    }
     dep_smem_ = smem;
-    dep_cluster_ = true;
 }
 
 // The reference kernels' own fp32 order where everything on the path has a
@@ -1103,12 +1140,13 @@ void Engine::reset_depth_kv_async(cudaStream_t s) {
 }
 
 void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
-    if (dep_cluster_) {
+    if (dep_cluster_ || dep_grid_) {
         DepCascadeArgs a = dep_args_;
         a.z = z;
         a.first = first;
         a.first.tok_out = nullptr;
-        ck(launch_dep_cascade(a, dep_smem_, s, cfg_.pdl), "launch depformer cascade");
+        if (dep_grid_) ck(launch_dep_cascade_ll(a, dep_grid_ctas_, dep_smem_, s), "launch depformer cascade");
+        else ck(launch_dep_cascade(a, dep_smem_, s, cfg_.pdl), "launch depformer cascade");
         return;
     }
     reset_depth_kv_async(s);

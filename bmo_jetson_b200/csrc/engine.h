@@ -111,6 +111,7 @@ public:
     bool graphs_captured() const { return graphs_ready_; }
     bool ref_order() const { return ref_order_; }
     bool dep_cluster() const { return dep_cluster_; }
+    bool dep_grid() const { return dep_grid_; }
     bool tp_exchange() const { return tp_p2p_; }
 
     // ---- batched sessions: up to kBatchMax independent sessions stepped
@@ -259,8 +260,10 @@ private:
     // summation order of the single-session path (see the header comment)
     bool ref_order_ = false;
 
-    // the greedy cascade on one thread-block cluster (reference order)
-    bool dep_cluster_ = false;
+    // the greedy cascade as one launch (reference order): on one
+    // thread-block cluster, or over every SM with epoch-tagged exchanges
+    bool dep_cluster_ = false, dep_grid_ = false;
+    int dep_grid_ctas_ = 0;
     DepOp *dep_ops_d_ = nullptr;
     DepCascadeArgs dep_args_{};
     size_t dep_smem_ = 0;

@@ -53,6 +53,19 @@ int dep_cascade_part_slots();
 int dep_cascade_max_cluster();
 int dep_cascade_max_local_tiles();
 int dep_cascade_head_dim();
+// The same cascade as one cooperative launch over `grid` CTAs (one per SM)
+// exchanging op outputs through epoch-tagged words in global memory
+// (kernels/dep_cascade_ll.cu).
+cudaError_t launch_dep_cascade_ll(const DepCascadeArgs &a, int grid, size_t smem_bytes, cudaStream_t s);
+size_t dep_cascade_ll_smem_bytes(int dim, int ffn, int n_embd, int n_layers, int n_ctx);
+int dep_cascade_ll_configure(size_t smem_bytes, int sms);  // CTAs that can run co-resident (0: cannot run)
+int dep_cascade_ll_items();
+int dep_cascade_ll_max_local_tiles();
+int dep_cascade_ll_max_in();
+int dep_cascade_ll_head_dim();
+int dep_cascade_ll_phases();
+int dep_cascade_ll_max_grid();
+int dep_cascade_ll_max_ops();
 
 // Batched sessions (kernels/batch.cu).  Stage: per-session RMSNorm + Q8_1
 // into the block-major layout (and the embedding token); GEMM: the skinny

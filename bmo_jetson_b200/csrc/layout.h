@@ -239,6 +239,11 @@ struct DepCascadeArgs {
     int dep_q, n_layers, dim, ffn, heads, hd, n_ctx, argmax_limit;
     float eps, scale;
     int *status;
+    // grid-wide variant: two exchange buffers of ll_stride 64-bit words
+    // (epoch << 32 | value bits) and the launch counter that makes epochs unique
+    unsigned long long *ll;
+    int ll_stride;
+    unsigned int *seq;
 };
 
 // ---- batched sessions (config 4) ----

@@ -53,7 +53,7 @@ def lib() -> ctypes.CDLL:
     for name in ("bmo_get_n_layers", "bmo_get_n_embd", "bmo_get_n_codebooks", "bmo_get_dep_q", "bmo_get_text_vocab",
                  "bmo_get_audio_vocab", "bmo_get_n_attn_heads", "bmo_get_head_dim", "bmo_capture_graphs",
                  "bmo_has_cuda_graphs", "bmo_get_kv_type", "bmo_get_n_ctx", "bmo_get_n_kv_heads", "bmo_get_device",
-                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order", "bmo_get_dep_cluster"):
+                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order", "bmo_get_dep_mode"):
         fn = getattr(L, name)
         fn.argtypes = [vp]
         fn.restype = i
@@ -249,9 +249,10 @@ class BMOEngine:
         return bool(lib().bmo_get_ref_order(self._h))
 
     @property
-    def dep_cluster(self) -> bool:
-        """True when greedy depformer cascades run as one cluster launch."""
-        return bool(lib().bmo_get_dep_cluster(self._h))
+    def dep_mode(self) -> int:
+        """How greedy depformer cascades run: 0 one kernel per op, 1 one
+        cluster launch, 2 one cooperative launch over every SM."""
+        return int(lib().bmo_get_dep_mode(self._h))
 
     def forward_temporal(self, tokens: np.ndarray, copy: bool = False) -> Tuple[np.ndarray, np.ndarray]:
         assert tokens.dtype == np.int32 and tokens.shape == (self.n_codebooks,), (

@@ -54,9 +54,10 @@ BMO_API size_t bmo_get_device_bytes(bmo_handle_t *h);
 /* 1 when the handle computes in the reference kernels' fp32 order, 0 for
  * the exact-reduction order (see BMO_FLAG_EXACT). */
 BMO_API int bmo_get_ref_order(bmo_handle_t *h);
-/* 1 when greedy depformer cascades run as one cluster launch (see
- * BMO_FLAG_DEP_CLUSTER), 0 when they run one kernel per op. */
-BMO_API int bmo_get_dep_cluster(bmo_handle_t *h);
+/* How greedy depformer cascades run: 0 one kernel per op, 1 one launch on a
+ * thread-block cluster (BMO_FLAG_DEP_CLUSTER), 2 one cooperative launch over
+ * every SM exchanging op outputs through global memory. */
+BMO_API int bmo_get_dep_mode(bmo_handle_t *h);
 
 /* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
  * slots [slot0, slot0+n) of temporal layer `layer`; rows are

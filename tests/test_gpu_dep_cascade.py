@@ -1,11 +1,14 @@
-"""The greedy depformer cascade as one thread-block-cluster launch
-(kernels/dep_cascade.cu, opt-in with BMO_FLAG_DEP_CLUSTER) against the same
-cascade run one kernel per op (the default): both compute the reference kernels' fp32 operations
-in the reference's order, so the tokens and every step's audio logits must
-be identical bit for bit -- through bmo_forward_depth_cascade (host z and
+"""The greedy depformer cascade as one launch -- on a thread-block cluster
+(kernels/dep_cascade.cu, BMO_FLAG_DEP_CLUSTER) or as a cooperative launch
+over every SM (kernels/dep_cascade_ll.cu, BMO_DEP_GRID=1) -- against the same
+cascade run one kernel per op: all compute the reference kernels' fp32
+operations in the reference's order, so the tokens and every step's audio
+logits must be identical bit for bit -- through bmo_forward_depth_cascade (host z and
 text token), through the whole-frame graph (text token from the device text
 head), and with the per-step entry point afterwards (bmo_forward_depth keeps
 using the depformer K/V ring the cascade wrote)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -19,9 +22,16 @@ def model_dir(tmp_path_factory):
     return str(tmp_path_factory.mktemp("models"))
 
 
-def _pair(path, n_ctx):
-    a = engine.BMOEngine(path, n_ctx=n_ctx, device=0, kv_type=engine.KV_F16, flags=engine.FLAG_DEP_CLUSTER)
-    b = engine.BMOEngine(path, n_ctx=n_ctx, device=0, kv_type=engine.KV_F16)
+def _pair(path, n_ctx, mode):
+    """(engine running the cascade in `mode`, engine running it per op)."""
+    os.environ["BMO_DEP_GRID"] = "1" if mode == 2 else "0"
+    try:
+        a = engine.BMOEngine(path, n_ctx=n_ctx, device=0, kv_type=engine.KV_F16,
+                             flags=engine.FLAG_DEP_CLUSTER if mode == 1 else 0)
+        os.environ["BMO_DEP_GRID"] = "0"
+        b = engine.BMOEngine(path, n_ctx=n_ctx, device=0, kv_type=engine.KV_F16)
+    finally:
+        os.environ.pop("BMO_DEP_GRID", None)
     return a, b
 
 
@@ -29,14 +39,15 @@ def _bits(x):
     return np.ascontiguousarray(x, np.float32).view(np.uint32)
 
 
+@pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("preset", ["tiny", "tiny17", "config2"])
-def test_cluster_cascade_equals_per_op_cascade(preset, model_dir):
+def test_one_launch_cascade_equals_per_op_cascade(preset, mode, model_dir):
     path = synth.ensure_model(preset, model_dir)
-    a, b = _pair(path, 64)
+    a, b = _pair(path, 64, mode)
     try:
         assert a.ref_order and b.ref_order
-        assert a.dep_cluster, "the cascade kernel should run this depformer"
-        assert not b.dep_cluster
+        assert a.dep_mode == mode, "the cascade kernel should run this depformer"
+        assert b.dep_mode == 0
         rng = np.random.default_rng(5)
         for trial in range(3):
             z = rng.standard_normal(a.n_embd).astype(np.float32) * (1.0 + trial)
@@ -61,10 +72,11 @@ def test_cluster_cascade_equals_per_op_cascade(preset, model_dir):
         del a, b
 
 
+@pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("preset", ["tiny", "config2"])
-def test_cluster_cascade_in_the_frame_graph(preset, model_dir):
+def test_one_launch_cascade_in_the_frame_graph(preset, mode, model_dir):
     path = synth.ensure_model(preset, model_dir)
-    a, b = _pair(path, 64)
+    a, b = _pair(path, 64, mode)
     try:
         rng = np.random.default_rng(9)
         w = a.n_kv_heads * a.head_dim
