@@ -305,21 +305,33 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_ref_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 cudaError_t configure_gemv_ref();
 
+// Shared memory a launch asks for: a grid no larger than the SM count asks
+// for more than half an SM, so that no SM holds two of its CTAs (the
+// scheduler otherwise packed pairs onto SMs its predecessor had left while
+// others stayed idle: 383 vs 376 frames/s on B200); larger grids run two per
+// SM (gemv_ref_grid).
+constexpr size_t kSpreadSmemBytes = 118 * 1024;
+static_assert(sizeof(GemvRefSmem) <= kSpreadSmemBytes, "the spread request covers the kernel's layout");
+
 template <int PRO, int EPI>
 static cudaError_t launch_ref_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
-    // The shared-memory opt-in is per device; the first launch on a device sets it.
+    // The shared-memory opt-in is per device; the first launch on a device
+    // sets it and records the device's SM count.
     static unsigned long long configured = 0;
+    static int sm_count[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !(configured & (1ull << dev))) {
-        const cudaError_t e = configure_gemv_ref();
+        cudaError_t e = configure_gemv_ref();
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         configured |= 1ull << dev;
     }
+    const bool spread = dev < 64 && grid <= sm_count[dev];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sizeof(GemvRefSmem);
+    cfg.dynamicSmemBytes = spread ? kSpreadSmemBytes : sizeof(GemvRefSmem);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -345,7 +357,7 @@ cudaError_t configure_gemv_ref() {
     cudaError_t e = cudaSuccess;
 #define BMO_GEMV_REF_CFG(P, E)                                                                              \
     if ((e = cudaFuncSetAttribute(gemv_ref_kernel<P, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                  static_cast<int>(sizeof(GemvRefSmem)))) != cudaSuccess)                   \
+                                  static_cast<int>(kSpreadSmemBytes))) != cudaSuccess)                      \
         return e;
     BMO_GEMV_REF_VARIANTS(BMO_GEMV_REF_CFG)
 #undef BMO_GEMV_REF_CFG
