@@ -1066,6 +1066,12 @@ void Engine::ops_cascade(std::vector<FramePhase> &v, const float *z, const Token
 
 // Per-op path: one kernel per entry, chained by programmatic dependent launch.
 void Engine::enqueue_ops(cudaStream_t s, const std::vector<FramePhase> &ops) {
+    // The peer-memory exchange lets its dependent launch start early; that is
+    // safe only when the next kernel is a GEMV, which waits (griddepcontrol)
+    // before it reads the exchange's output or rewrites its partial buffer.
+    for (size_t k = 0; k < ops.size(); ++k)
+        if (ops[k].kind == kPhTpExchange && k + 1 < ops.size() && ops[k + 1].kind != kPhGemv)
+            throw std::runtime_error("internal: a tensor-parallel exchange must be followed by a GEMV");
     for (const FramePhase &op : ops) {
         switch (op.kind) {
         case kPhGemv: {
