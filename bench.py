@@ -766,7 +766,7 @@ def main():
     # ---- roofline of the dominant kernel ----
     rl = gemv_roofline(local, peak)
     total_b, temporal_b, dep_b, kv_b = frame_bytes(e)
-    launches_per_frame = 1 + e.n_layers * 5 + 1 + e.dep_q * (1 + 6 * 5 + 1) + 1
+    launches_per_frame = e.frame_launches
 
     e.close()
     batch = None

@@ -234,6 +234,17 @@ int bmo_has_cuda_graphs(bmo_handle_t *h) { return (h && h->eng->graphs_captured(
 
 int bmo_get_ref_order(bmo_handle_t *h) { return (h && h->eng->ref_order()) ? 1 : 0; }
 
+int bmo_get_frame_launches(bmo_handle_t *h) {
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    try {
+        return h->eng->frame_launches();
+    } catch (const std::exception &e) {
+        h->last_error = e.what();
+        return -1;
+    }
+}
+
 int bmo_get_dep_mode(bmo_handle_t *h) {
     if (!h) return 0;
     return h->eng->dep_grid() ? 2 : h->eng->dep_cluster() ? 1 : 0;

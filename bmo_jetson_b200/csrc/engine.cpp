@@ -94,6 +94,21 @@ Engine::Engine(const std::string &gguf_path, const EngineConfig &cfg) : cfg_(cfg
     setup_dep_cascade();
 }
 
+int Engine::frame_launches() const {
+    int n = 1 + static_cast<int>(ops_temporal().size());  // embed + temporal ops + text head
+    if (has_dep_tables && dep_dim > 0 && dep_q > 0) {
+        if (dep_cluster_ || dep_grid_) {
+            n += 1;
+        } else {
+            std::vector<FramePhase> v;
+            ops_cascade(v, z_, TokenSrc{});
+            n += static_cast<int>(v.size());
+        }
+    }
+    return n;
+}
+
+
 // The greedy cascade as one launch when the depformer fits the kernels'
 // design (reference order, one GPU, 64-dimension heads, the shared-memory
 // and per-op tile limits) and the device can run it; otherwise the per-op

@@ -111,6 +111,7 @@ public:
     bool graphs_captured() const { return graphs_ready_; }
     bool ref_order() const { return ref_order_; }
     bool dep_cluster() const { return dep_cluster_; }
+    int frame_launches() const;  // kernels one greedy frame launches (embed, temporal ops, cascade)
     bool dep_grid() const { return dep_grid_; }
     bool tp_exchange() const { return tp_p2p_; }
 

@@ -58,6 +58,9 @@ BMO_API int bmo_get_ref_order(bmo_handle_t *h);
  * thread-block cluster (BMO_FLAG_DEP_CLUSTER), 2 one cooperative launch over
  * every SM exchanging op outputs through global memory. */
 BMO_API int bmo_get_dep_mode(bmo_handle_t *h);
+/* Kernels one greedy frame (bmo_forward_frame_greedy / bmo_enqueue_frame)
+ * launches on the device, or -1. */
+BMO_API int bmo_get_frame_launches(bmo_handle_t *h);
 
 /* Writes fp32 K/V rows (already rotated, as the ring stores them) into ring
  * slots [slot0, slot0+n) of temporal layer `layer`; rows are
