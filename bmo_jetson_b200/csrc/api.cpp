@@ -245,6 +245,64 @@ int bmo_get_frame_launches(bmo_handle_t *h) {
     }
 }
 
+int bmo_loop_reset(bmo_handle_t *h, uint32_t seed) {
+    if (!h) return 1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    bmo::Engine *e = h->eng.get();
+    if (!e->loop_supported()) {
+        h->last_error = "bmo_loop_reset: the model has no frame loop (text head, 8 depformer steps, 9 or 17 channels, one GPU)";
+        return 3;
+    }
+    try {
+        e->loop_reset(seed);
+    } catch (const std::exception &ex) {
+        h->last_error = ex.what();
+        return 9;
+    }
+    h->last_error.clear();
+    return 0;
+}
+
+int bmo_loop_run(bmo_handle_t *h, int n_frames, const int32_t *user_tokens, int use_sampling, float temp_text,
+                 int top_k_text, float temp_audio, int top_k_audio, int32_t *out) {
+    if (!h || !out) return 1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    bmo::Engine *e = h->eng.get();
+    if (n_frames < 1 || n_frames > bmo::kLoopRing) {
+        h->last_error = "bmo_loop_run: 1 to 64 frames per call";
+        return 2;
+    }
+    if (e->loop_frame() < 0 || !e->loop_supported()) return 4;
+    bmo::LoopParams in[bmo::kLoopRing] = {};
+    for (int i = 0; i < n_frames; ++i) {
+        in[i].sampling = use_sampling ? 1 : 0;
+        in[i].temp_text = temp_text;
+        in[i].temp_audio = temp_audio;
+        in[i].top_k_text = top_k_text;
+        in[i].top_k_audio = top_k_audio;
+        in[i].user_valid = user_tokens ? 1 : 0;
+        for (int c = 0; c < bmo::kLoopCb; ++c) in[i].user[c] = user_tokens ? user_tokens[i * bmo::kLoopCb + c] : 0;
+    }
+    if (!e->loop_params_ok(in[0])) {
+        h->last_error = "bmo_loop_run: top_k above 2048 over more than 2048 logits";
+        return 2;
+    }
+    try {
+        e->loop_run(n_frames, in, out);
+    } catch (const std::exception &ex) {
+        h->last_error = ex.what();
+        return std::strstr(ex.what(), "not reset") ? 4 : 9;
+    }
+    h->last_error.clear();
+    return 0;
+}
+
+int bmo_loop_frame(bmo_handle_t *h) {
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    return h->eng->loop_frame();
+}
+
 int bmo_get_dep_mode(bmo_handle_t *h) {
     if (!h) return 0;
     return h->eng->dep_grid() ? 2 : h->eng->dep_cluster() ? 1 : 0;

@@ -277,12 +277,13 @@ Engine::~Engine() {
     drop(g_cascade_z_);
     drop(g_cascade_);
     drop(g_frame_);
+    drop(g_loop_);
     for (auto &g : g_depth_) drop(g);
     teardown_tp_exchange();
     tp_comm_.reset();
     for (void *p : allocs_) cudaFree(p);
     for (void *p : {(void *)fin_h_, (void *)z_h_, (void *)logits_h_, (void *)zin_h_, (void *)dlogits_h_,
-                    (void *)tok_h_, (void *)status_h_})
+                    (void *)tok_h_, (void *)status_h_, (void *)loop_in_h_, (void *)loop_out_h_})
         if (p) cudaFreeHost(p);
     if (stream) cudaStreamDestroy(stream);
 }
@@ -1360,6 +1361,112 @@ void Engine::enqueue_cascade_device(int32_t text_token) {
         t.tok = &fin_d_->prev_token;
         enqueue_cascade(s, z_, t);
     });
+}
+
+// ---------------------------------------------------------------------------
+// the caller's frame loop on the device
+// ---------------------------------------------------------------------------
+bool Engine::loop_supported() const {
+    return has_text_head && has_dep_tables && dep_dim > 0 && dep_q == kLoopCb && !tensor_parallel &&
+           (num_codebooks == 1 + kLoopCb || num_codebooks == 1 + 2 * kLoopCb);
+}
+
+// The daemon's start state (bmo_daemon.cpp:641-647): text pad, audio pads,
+// codebook-0 token 1049, std::mt19937 seeded with `seed`.
+void Engine::loop_reset(uint32_t seed) {
+    if (!loop_supported())
+        throw std::runtime_error("frame loop needs a text head, 8 depformer steps, 9 or 17 input channels, one GPU");
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    if (!loop_st_) {
+        void *p = nullptr;
+        ck(cudaMalloc(&p, sizeof(LoopState)), "cudaMalloc loop state");
+        allocs_.push_back(p);
+        loop_st_ = static_cast<LoopState *>(p);
+        ck(cudaMallocHost(&loop_in_h_, sizeof(LoopParams) * kLoopRing), "cudaMallocHost loop");
+        ck(cudaMallocHost(&loop_out_h_, sizeof(int32_t) * kLoopRing * kLoopOut), "cudaMallocHost loop");
+    }
+    auto st = std::make_unique<LoopState>();
+    std::memset(st.get(), 0, sizeof(LoopState));
+    st->prev_text = text_vocab;
+    for (int i = 0; i < kLoopCb; ++i) st->prev_audio[i] = st->prev_user[i] = audio_vocab;
+    st->prev_cb0 = 1049;
+    st->mt[0] = seed;
+    for (int i = 1; i < 624; ++i) st->mt[i] = 1812433253u * (st->mt[i - 1] ^ (st->mt[i - 1] >> 30)) + static_cast<unsigned>(i);
+    st->mti = 624;
+    ck(cudaMemcpy(loop_st_, st.get(), sizeof(LoopState), cudaMemcpyHostToDevice), "loop state copy");
+    loop_frame_ = 0;
+    reset_kv();
+}
+
+bool Engine::loop_params_ok(const LoopParams &in) const {
+    if (!in.sampling) return true;
+    return std::min(in.top_k_text, std::min(text_vocab, 32000)) <= kLoopTopKMax &&
+           std::min(in.top_k_audio, std::min(audio_vocab, 2048)) <= kLoopTopKMax;
+}
+
+void Engine::enqueue_loop_frame(cudaStream_t s) {
+    LoopConfig c{};
+    c.text_n = std::min(text_vocab, 32000);
+    c.audio_n = std::min(audio_vocab, 2048);
+    c.text_pad = text_vocab;
+    c.audio_pad = audio_vocab;
+    c.n_tok = num_codebooks;
+    ck(launch_loop_begin(loop_st_, c, fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, s), "launch loop begin");
+    enqueue_temporal(s);
+    SampleArgs sa{};
+    sa.st = loop_st_;
+    sa.mt = loop_st_->mt;
+    sa.mti = &loop_st_->mti;
+    sa.logits = logits_;
+    sa.n = c.text_n;
+    sa.text = 1;
+    sa.out = &loop_st_->next_text;
+    ck(launch_sample(sa, s), "launch text sample");
+    reset_depth_kv_async(s);
+    for (int cb = 0; cb < dep_q; ++cb) {
+        TokenSrc t{};
+        t.tok = cb == 0 ? &loop_st_->next_text : &loop_st_->audio[cb - 1];
+        enqueue_depth_step(s, cb, z_, t);
+        sa.logits = dlogits_ + static_cast<size_t>(cb) * audio_vocab;
+        sa.n = c.audio_n;
+        sa.text = 0;
+        sa.out = &loop_st_->audio[cb];
+        ck(launch_sample(sa, s), "launch audio sample");
+    }
+    ck(launch_loop_end(loop_st_, s), "launch loop end");
+}
+
+void Engine::loop_run(int n, const LoopParams *in, int32_t *out) {
+    if (!loop_st_) throw std::runtime_error("frame loop not reset");
+    if (n < 1 || n > kLoopRing) throw std::runtime_error("frame loop: 1 to 64 frames per call");
+    for (int i = 0; i < n; ++i)
+        if (!loop_params_ok(in[i])) throw std::runtime_error("frame loop: top-k above 2048");
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    const int f0 = loop_frame_;
+    // this call's inputs into their ring rows (one copy, two when the rows wrap)
+    const int r0 = f0 % kLoopRing, first = std::min(n, kLoopRing - r0);
+    std::memcpy(loop_in_h_ + r0, in, sizeof(LoopParams) * static_cast<size_t>(first));
+    std::memcpy(loop_in_h_, in + first, sizeof(LoopParams) * static_cast<size_t>(n - first));
+    ck(cudaMemcpyAsync(loop_st_->in + r0, loop_in_h_ + r0, sizeof(LoopParams) * static_cast<size_t>(first),
+                       cudaMemcpyHostToDevice, stream),
+       "loop input copy");
+    if (n > first)
+        ck(cudaMemcpyAsync(loop_st_->in, loop_in_h_, sizeof(LoopParams) * static_cast<size_t>(n - first),
+                           cudaMemcpyHostToDevice, stream),
+           "loop input copy");
+    for (int i = 0; i < n; ++i) launch(g_loop_, [this](cudaStream_t s) { enqueue_loop_frame(s); });
+    ck(cudaMemcpyAsync(loop_out_h_ + static_cast<size_t>(r0) * kLoopOut, loop_st_->out[r0],
+                       sizeof(int32_t) * kLoopOut * static_cast<size_t>(first), cudaMemcpyDeviceToHost, stream),
+       "loop output copy");
+    if (n > first)
+        ck(cudaMemcpyAsync(loop_out_h_, loop_st_->out[0], sizeof(int32_t) * kLoopOut * static_cast<size_t>(n - first),
+                           cudaMemcpyDeviceToHost, stream),
+           "loop output copy");
+    finish_call();
+    loop_frame_ = f0 + n;
+    std::memcpy(out, loop_out_h_ + static_cast<size_t>(r0) * kLoopOut, sizeof(int32_t) * kLoopOut * static_cast<size_t>(first));
+    std::memcpy(out + static_cast<size_t>(first) * kLoopOut, loop_out_h_,
+                sizeof(int32_t) * kLoopOut * static_cast<size_t>(n - first));
 }
 
 int Engine::sync_status() {

@@ -115,6 +115,18 @@ public:
     bool dep_grid() const { return dep_grid_; }
     bool tp_exchange() const { return tp_p2p_; }
 
+    // ---- the caller's frame loop on the device (bmo_daemon.cpp:641-816):
+    // interleave, temporal step, text sample, dep_q depformer steps with
+    // their audio samples and the codec input of each frame, as one graph ----
+    bool loop_supported() const;  // a text head, 8 depformer steps, 9 or 17 input channels, one GPU
+    void loop_reset(uint32_t seed);  // frame 0, the daemon's start state, mt19937(seed), fresh KV rings
+    // top-k values the device sampler takes: min(top_k, logits considered) <= kLoopTopKMax
+    bool loop_params_ok(const LoopParams &in) const;
+    // Frames f .. f + n - 1 (n <= kLoopRing) with in[i] as frame f + i's
+    // inputs; out[i][kLoopOut] their results.  One host synchronisation.
+    void loop_run(int n, const LoopParams *in, int32_t *out);
+    int loop_frame() const { return loop_st_ ? loop_frame_ : -1; }  // -1 before loop_reset
+
     // ---- batched sessions: up to kBatchMax independent sessions stepped
     // together, each with its own temporal ring, sharing one weight stream ----
     int batch_init(int n_sessions);  // allocates the rings once (0 ok, 1 bad count, 3 already other size)
@@ -200,6 +212,14 @@ private:
     void batch_gemm(cudaStream_t s, const BatchGemmArgs &a, int epi);
     int kv_import_into(void *kc, void *vc, uint8_t *ks, uint8_t *vs, int layer, int slot0, int n, const float *k_rows,
                        const float *v_rows);
+
+    // frame loop (kernels/loop.cu)
+    LoopState *loop_st_ = nullptr;
+    LoopParams *loop_in_h_ = nullptr;  // pinned [kLoopRing]
+    int32_t *loop_out_h_ = nullptr;    // pinned [kLoopRing][kLoopOut]
+    int loop_frame_ = 0;
+    cudaGraphExec_t g_loop_ = nullptr;
+    void enqueue_loop_frame(cudaStream_t s);
 
     cudaGraphExec_t capture(const std::function<void(cudaStream_t)> &fn);
     void launch(cudaGraphExec_t &g, const std::function<void(cudaStream_t)> &fn);

@@ -335,4 +335,21 @@ int bmo_k_tp_exchange(const double *const *parts, unsigned long long *const *fla
     return static_cast<int>(launch_tp_exchange(a, static_cast<cudaStream_t>(stream), false));
 }
 
+int bmo_k_sample_token(const float *logits_dev, int n, float temp, int top_k, int pause_rule, uint32_t *rng_dev,
+                       int32_t *out_dev, void *stream) {
+    if (!logits_dev || !rng_dev || !out_dev || n <= 0 || (top_k < n ? top_k : n) > kLoopTopKMax)
+        return static_cast<int>(cudaErrorInvalidValue);
+    SampleArgs a{};
+    a.logits = logits_dev;
+    a.n = n;
+    a.text = pause_rule ? 1 : 0;
+    a.sampling = 1;
+    a.top_k = top_k;
+    a.temp = temp;
+    a.mt = rng_dev;
+    a.mti = reinterpret_cast<int *>(rng_dev + 624);
+    a.out = out_dev;
+    return static_cast<int>(launch_sample(a, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

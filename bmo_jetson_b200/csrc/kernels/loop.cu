@@ -1,0 +1,329 @@
+// loop.cu -- the caller's frame loop on the device: the 17-channel
+// interleave and delay of bmo_daemon.cpp:727-742, its token samplers
+// (sample_token_cpp, :147-175, with the loop's one std::mt19937) and its
+// per-frame state update (:811-816), so that a whole conversational frame --
+// interleave, temporal step, text sample, 8 depformer steps each with its
+// audio sample, codec tokens -- is one CUDA graph with no host round trip.
+//
+//   frame 0:   [pad_text, pad_audio x 16]
+//   frame 1:   [prev_text, prev_audio[0], pad_audio x 7, user[0], pad_audio x 7]
+//   frame >1:  [prev_text, prev_audio[0..7], user[0], prev_user[1..7]]
+//   text:      top1 = first argmax; a pause (3 or 0) or greedy mode keeps top1,
+//              else top-k / temperature sampling
+//   audio:     per step, first argmax (greedy) or top-k / temperature sampling
+//   codec:     [prev_cb0, audio[1..7]]; then prev_cb0 = audio[0],
+//              prev_audio = audio, prev_user = user, prev_text = text.
+//
+// The sampler reproduces sample_token_cpp's arithmetic: the top_k logits in
+// descending order (ties by lower index: std::partial_sort leaves the order of
+// equal logits unspecified), probs_i = exp(l_i / temp - l_0 / temp) in float
+// (the exponential evaluated in double and rounded once), their float sum
+// checked for zero or NaN, then std::discrete_distribution's draw -- the
+// probabilities widened to double, divided by their sequential double sum,
+// the running sums as the cumulative table with its last entry 1, u =
+// generate_canonical<double, 53> from two 32-bit outputs, the first index
+// whose cumulative value is >= u.  The generator is the standard's mt19937.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv_dev.cuh"
+#include "../launch.h"
+
+namespace bmo {
+
+namespace {
+
+constexpr int kSampleThreads = 1024;
+constexpr unsigned kMtUpper = 0x80000000u, kMtLower = 0x7fffffffu, kMtMatrix = 0x9908b0dfu;
+
+// The standard's mt19937 (state in shared memory, one thread).
+__device__ unsigned mt_next(unsigned *mt, int &mti) {
+    if (mti >= 624) {
+        for (int i = 0; i < 624; ++i) {
+            const unsigned y = (mt[i] & kMtUpper) | (mt[(i + 1) % 624] & kMtLower);
+            mt[i] = mt[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? kMtMatrix : 0u);
+        }
+        mti = 0;
+    }
+    unsigned y = mt[mti++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+}  // namespace
+
+// Builds this frame's input tokens and position from the loop state.
+__global__ void loop_begin_kernel(LoopState *st, LoopConfig cfg, int *tokens, int *n_tok, int *pos) {
+    if (threadIdx.x != 0) return;
+    // the daemon's silence tokens when the caller has no user audio
+    const int silence[kLoopCb] = {1049, 243, 783, 1562, 340, 2010, 183, 1665};
+    const int f = st->frame;
+    const LoopParams &in = st->in[f % kLoopRing];
+    for (int i = 0; i < kLoopCb; ++i) st->user[i] = in.user_valid ? in.user[i] : silence[i];
+    int t[1 + 2 * kLoopCb];
+    if (f == 0) {
+        t[0] = cfg.text_pad;
+        for (int i = 1; i <= 2 * kLoopCb; ++i) t[i] = cfg.audio_pad;
+    } else if (f == 1) {
+        t[0] = st->prev_text;
+        t[1] = st->prev_audio[0];
+        for (int i = 2; i <= kLoopCb; ++i) t[i] = cfg.audio_pad;
+        t[1 + kLoopCb] = st->user[0];
+        for (int i = 2 + kLoopCb; i <= 2 * kLoopCb; ++i) t[i] = cfg.audio_pad;
+    } else {
+        t[0] = st->prev_text;
+        for (int i = 0; i < kLoopCb; ++i) t[1 + i] = st->prev_audio[i];
+        t[1 + kLoopCb] = st->user[0];
+        for (int i = 1; i < kLoopCb; ++i) t[1 + kLoopCb + i] = st->prev_user[i];
+    }
+    for (int i = 0; i < cfg.n_tok; ++i) tokens[i] = t[i];
+    *n_tok = cfg.n_tok;
+    *pos = f;
+}
+
+// Codec input, state update, and the frame's results in row frame % kLoopRing
+// of st->out: [0] text token, [1..8] audio tokens, [9..16] codec input
+// (meaningful from frame 1 on: the daemon decodes nothing at frame 0).
+__global__ void loop_end_kernel(LoopState *st) {
+    if (threadIdx.x != 0) return;
+    int *out = st->out[st->frame % kLoopRing];
+    out[0] = st->next_text;
+    out[1 + kLoopCb] = st->prev_cb0;
+    for (int i = 0; i < kLoopCb; ++i) out[1 + i] = st->audio[i];
+    for (int i = 1; i < kLoopCb; ++i) out[1 + kLoopCb + i] = st->audio[i];
+    st->prev_cb0 = st->audio[0];
+    for (int i = 0; i < kLoopCb; ++i) {
+        st->prev_audio[i] = st->audio[i];
+        st->prev_user[i] = st->user[i];
+    }
+    st->prev_text = st->next_text;
+    st->frame += 1;
+}
+
+namespace {
+
+// Order-preserving key of a float (larger float, larger key; no NaNs).
+__device__ __forceinline__ unsigned fkey(float v) {
+    const unsigned u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+struct SampleSmem {
+    unsigned long long sel[kLoopTopKMax];  // (key << 32) | (~index): descending = value desc, index asc
+    float prob[kLoopTopKMax];
+    double cum[kLoopTopKMax];
+    unsigned mt[624];
+    int hist[256];
+    float red_v[32];
+    int red_i[32];
+    int warp_cnt[32];
+    int n_sel, n_eq_taken, tok;
+    unsigned prefix;
+    int kk;
+};
+
+}  // namespace
+
+// One token draw (the daemon's sample_token_cpp; first argmax when greedy).
+// One CTA of kSampleThreads threads.
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
+    __shared__ SampleSmem S;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int kWarpsS = kSampleThreads / 32;
+
+    // ---- first argmax (std::max_element) ----
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < a.n; i += kSampleThreads) argmax_merge(bv, bi, __ldcg(a.logits + i), i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+    }
+    if (lane == 0) {
+        S.red_v[warp] = bv;
+        S.red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float fv = S.red_v[0];
+        int fi = S.red_i[0];
+        for (int w = 1; w < kWarpsS; ++w) argmax_merge(fv, fi, S.red_v[w], S.red_i[w]);
+        S.tok = fi;
+    }
+    __syncthreads();
+    const int top1 = S.tok;
+    int sampling = a.sampling, top_k = a.top_k;
+    float temp = a.temp;
+    if (a.st) {
+        const LoopParams &in = a.st->in[a.st->frame % kLoopRing];
+        sampling = in.sampling;
+        top_k = a.text ? in.top_k_text : in.top_k_audio;
+        temp = a.text ? in.temp_text : in.temp_audio;
+    }
+    const bool greedy = !sampling || top_k <= 0 || temp <= 1e-4f || (a.text && (top1 == 3 || top1 == 0));
+    if (greedy) {
+        if (tid == 0) *a.out = top1;
+        return;
+    }
+    const int k = min(min(top_k, a.n), kLoopTopKMax);  // the host keeps top_k within kLoopTopKMax
+
+    // ---- the k-th largest key (radix select, 8 bits per pass) ----
+    unsigned prefix = 0, mask = 0;
+    int kk = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += kSampleThreads) S.hist[b] = 0;
+        __syncthreads();
+        for (int i = tid; i < a.n; i += kSampleThreads) {
+            const unsigned key = fkey(__ldcg(a.logits + i));
+            if ((key & mask) == prefix) atomicAdd(&S.hist[(key >> shift) & 255], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int cum = 0, b = 255;
+            for (; b > 0; --b) {
+                if (cum + S.hist[b] >= kk) break;
+                cum += S.hist[b];
+            }
+            S.kk = kk - cum;
+            S.prefix = prefix | (static_cast<unsigned>(b) << shift);
+        }
+        __syncthreads();
+        kk = S.kk;
+        prefix = S.prefix;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    const unsigned thr = prefix;  // keys above it are all taken; kk of those equal to it, lowest indices first
+
+    // ---- gather the k entries ----
+    if (tid == 0) {
+        S.n_sel = 0;
+        S.n_eq_taken = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < a.n; base += kSampleThreads) {
+        const int i = base + tid;
+        unsigned key = 0;
+        bool gt = false, eq = false;
+        if (i < a.n) {
+            key = fkey(__ldcg(a.logits + i));
+            gt = key > thr;
+            eq = key == thr;
+        }
+        if (gt) S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(key) << 32) | (~static_cast<unsigned>(i));
+        // equal keys in index order: a block-wide exclusive scan of `eq`
+        const unsigned bal = __ballot_sync(0xffffffffu, eq);
+        if (lane == 0) S.warp_cnt[warp] = __popc(bal);
+        __syncthreads();
+        int before = S.n_eq_taken;
+        for (int w = 0; w < warp; ++w) before += S.warp_cnt[w];
+        before += __popc(bal & ((1u << lane) - 1u));
+        if (eq && before < kk) S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(key) << 32) | (~static_cast<unsigned>(i));
+        __syncthreads();
+        if (tid == 0) {
+            int t = 0;
+            for (int w = 0; w < kWarpsS; ++w) t += S.warp_cnt[w];
+            S.n_eq_taken += t;
+        }
+        __syncthreads();
+    }
+    // ---- sort them (bitonic, descending; padding entries are 0) ----
+    for (int i = S.n_sel + tid; i < kLoopTopKMax; i += kSampleThreads) S.sel[i] = 0;
+    __syncthreads();
+    for (int size = 2; size <= kLoopTopKMax; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < kLoopTopKMax; i += kSampleThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long x = S.sel[i], y = S.sel[j];
+                    if (desc ? (x < y) : (x > y)) {
+                        S.sel[i] = y;
+                        S.sel[j] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- probabilities: exp(l_i / temp - l_0 / temp) in float ----
+    const int tok0 = static_cast<int>(~static_cast<unsigned>(S.sel[0]));
+    const float max_l = __fdiv_rn(__ldcg(a.logits + tok0), temp);
+    for (int i = tid; i < k; i += kSampleThreads) {
+        const float li = __ldcg(a.logits + (~static_cast<unsigned>(S.sel[i])));
+        S.prob[i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(__fdiv_rn(li, temp), max_l))));
+    }
+    __syncthreads();
+    // their float sum must be positive; std::discrete_distribution normalises
+    // by the sequential double sum and draws nothing for a single weight
+    if (tid == 0) {
+        float sum_p = 0.0f;
+        for (int i = 0; i < k; ++i) sum_p = __fadd_rn(sum_p, S.prob[i]);
+        const bool draw = sum_p > 0.0f && !isnan(sum_p) && k >= 2;
+        double total = 0.0;
+        if (draw)
+            for (int i = 0; i < k; ++i) total = __dadd_rn(total, static_cast<double>(S.prob[i]));
+        S.cum[0] = total;
+        S.tok = draw ? 1 : 0;
+    }
+    __syncthreads();
+    if (!S.tok) {
+        if (tid == 0) *a.out = tok0;
+        return;
+    }
+    const double total = S.cum[0];
+    __syncthreads();
+    for (int i = tid; i < k; i += kSampleThreads) S.cum[i] = __ddiv_rn(static_cast<double>(S.prob[i]), total);
+    for (int i = tid; i < 624; i += kSampleThreads) S.mt[i] = a.mt[i];
+    __syncthreads();
+    if (tid == 0) {
+        int mti = *a.mti;
+        const unsigned g1 = mt_next(S.mt, mti);
+        const unsigned g2 = mt_next(S.mt, mti);
+        double u = __dadd_rn(static_cast<double>(g1), __dmul_rn(static_cast<double>(g2), 4294967296.0));
+        u = __ddiv_rn(u, 18446744073709551616.0);
+        if (u >= 1.0) u = 0x1.fffffffffffffp-1;  // the largest double below 1
+        // the first running sum >= u (the last one counts as 1)
+        double run = 0.0;
+        int pick = k - 1;
+        for (int i = 0; i < k - 1; ++i) {
+            run = __dadd_rn(run, S.cum[i]);
+            if (run >= u) {
+                pick = i;
+                break;
+            }
+        }
+        *a.out = static_cast<int>(~static_cast<unsigned>(S.sel[pick]));
+        *a.mti = mti;
+    }
+    __syncthreads();
+    for (int i = tid; i < 624; i += kSampleThreads) a.mt[i] = S.mt[i];
+}
+
+cudaError_t launch_loop_begin(LoopState *st, const LoopConfig &cfg, int *tokens, int *n_tok, int *pos,
+                              cudaStream_t s) {
+    loop_begin_kernel<<<1, 32, 0, s>>>(st, cfg, tokens, n_tok, pos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_loop_end(LoopState *st, cudaStream_t s) {
+    loop_end_kernel<<<1, 32, 0, s>>>(st);
+    return cudaGetLastError();
+}
+
+// The sampler takes min(top_k, n) up to kLoopTopKMax; the host checks the
+// caller's values before they reach the device.
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s) {
+    if (a.n <= 0 || !a.logits || !a.mt || !a.mti || !a.out || (!a.st && a.sampling && std::min(a.top_k, a.n) > kLoopTopKMax))
+        return cudaErrorInvalidValue;
+    sample_kernel<<<1, kSampleThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace bmo

@@ -111,6 +111,12 @@ cudaError_t launch_set_frame(int *fin_tokens, int *fin_n_tok, int *fin_pos, cons
 cudaError_t launch_set_int(int *dst, int v, cudaStream_t s);
 cudaError_t launch_finalize_token(const float2 *pairs, int n, int *out, cudaStream_t s, bool pdl);
 // Sets the shared-memory opt-in of every kernel variant on the current device.
+// The caller's frame loop on the device (kernels/loop.cu).
+cudaError_t launch_loop_begin(LoopState *st, const LoopConfig &cfg, int *tokens, int *n_tok, int *pos,
+                              cudaStream_t s);
+cudaError_t launch_loop_end(LoopState *st, cudaStream_t s);
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s);
+
 cudaError_t configure_kernels();
 cudaError_t launch_repack_q4_0(const void *src, void *dst, int rows, int cols, const QMatDesc &m, cudaStream_t s);
 cudaError_t launch_quantize_q8_1(const float *x, void *out, int n, cudaStream_t s);

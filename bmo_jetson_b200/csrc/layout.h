@@ -246,6 +246,56 @@ struct DepCascadeArgs {
     unsigned int *seq;
 };
 
+// ---- the caller's frame loop on the device (bmo_daemon.cpp:641-816) ----
+// The daemon's per-frame state: the tokens fed back into the next frame, the
+// std::mt19937 its samplers share, and this frame's results.
+constexpr int kLoopCb = 8;          // audio codebooks of an agent (and of the user)
+constexpr int kLoopTopKMax = 2048;  // largest top-k the device sampler takes (the audio vocabulary)
+constexpr int kLoopOut = 1 + 2 * kLoopCb;  // a frame's results: text, audio[8], codec input[8]
+constexpr int kLoopRing = 64;       // frames of results kept on the device
+// The caller's per-frame inputs, copied to the device before each frame.
+struct LoopParams {
+    int sampling;               // 0: greedy everywhere (the daemon without --sampling)
+    float temp_text, temp_audio;
+    int top_k_text, top_k_audio;
+    int user_valid;             // 0: the daemon's silence tokens stand for the user
+    int user[kLoopCb];          // the user's audio tokens of this frame
+};
+struct LoopState {
+    LoopParams in[kLoopRing];   // frame f's inputs in row f % kLoopRing
+    int frame;                  // frames decoded so far (the temporal position)
+    int prev_text;              // the text channel's token for the next frame
+    int prev_audio[kLoopCb];    // the agent's audio tokens of the last frame
+    int prev_user[kLoopCb];     // the user's audio tokens of the last frame
+    int prev_cb0;               // the agent's codebook-0 token of the last frame
+    int user[kLoopCb];          // this frame's user tokens
+    int next_text;              // this frame's text token
+    int audio[kLoopCb];         // this frame's audio tokens
+    int mti;                    // std::mt19937 position
+    unsigned mt[624];           // std::mt19937 state
+    int out[kLoopRing][kLoopOut];  // frame f's results in row f % kLoopRing
+};
+// Fixed by the model.
+struct LoopConfig {
+    int text_n, audio_n;        // logits the samplers consider (32000, 2048 for Moshi)
+    int text_pad, audio_pad;    // the channels' "no token yet" ids (32000, 2048)
+    int n_tok;                  // input channels: 1 + 8 agent (+ 8 user when 17)
+};
+// One draw from logits[0, n): the text draw (`text` != 0) stays greedy when
+// the first argmax is a pause token (3 or 0).  Its parameters are the frame
+// loop's (st->in[st->frame % kLoopRing]) when st is set, else the fields
+// here; mt[624] and *mti are the std::mt19937 state it advances.
+struct SampleArgs {
+    const float *logits;
+    int n, text;
+    const LoopState *st;
+    int sampling, top_k;
+    float temp;
+    unsigned *mt;
+    int *mti;
+    int *out;
+};
+
 // ---- batched sessions (config 4) ----
 // Q8_1 activations of S sessions, block-major, padded to P = S rounded up to
 // 16 sessions, laid out as the tensor core's B operand with the two half

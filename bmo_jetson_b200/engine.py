@@ -111,6 +111,12 @@ def lib() -> ctypes.CDLL:
     L.bmo_batch_kv_import_f32.restype = i
     L.bmo_batch_reset.argtypes = [vp, i]
     L.bmo_batch_reset.restype = i
+    L.bmo_loop_reset.argtypes = [vp, ctypes.c_uint32]
+    L.bmo_loop_reset.restype = i
+    L.bmo_loop_run.argtypes = [vp, i, _c_i32p, i, f, i, f, i, _c_i32p]
+    L.bmo_loop_run.restype = i
+    L.bmo_loop_frame.argtypes = [vp]
+    L.bmo_loop_frame.restype = i
     L.bmo_last_error.argtypes = [vp]
     L.bmo_last_error.restype = ctypes.c_char_p
     L.bmo_rvq_decode.argtypes = [vp, vp, vp, vp]
@@ -135,6 +141,8 @@ def lib() -> ctypes.CDLL:
     L.bmo_k_gemv_q4_0_ref.restype = i
     L.bmo_k_decode_attention_ref.argtypes = [vp] * 6 + [i] * 4 + [vp, i, vp]
     L.bmo_k_decode_attention_ref.restype = i
+    L.bmo_k_sample_token.argtypes = [vp, i, f, i, i, vp, vp, vp]
+    L.bmo_k_sample_token.restype = i
     L.bmo_k_batch_gemm_scratch_bytes.argtypes = [i, i, i, i, i]
     L.bmo_k_batch_gemm_scratch_bytes.restype = sz
     L.bmo_k_batch_gemm_q4_0.argtypes = [vp, i, i, i, i, vp, vp, f, vp, vp, i, i, vp, sz, vp]
@@ -258,6 +266,38 @@ class BMOEngine:
         """How greedy depformer cascades run: 0 one kernel per op, 1 one
         cluster launch, 2 one cooperative launch over every SM."""
         return int(lib().bmo_get_dep_mode(self._h))
+
+    # ---- the caller's frame loop on the device ----
+    LOOP_OUT = 17  # per frame: text token, 8 audio tokens, 8 codec tokens
+
+    def loop_reset(self, seed: int = 1337) -> None:
+        """Starts a conversation at frame 0 with the daemon's start state and
+        its sampler generator std::mt19937(seed)."""
+        rc = lib().bmo_loop_reset(self._h, int(seed) & 0xFFFFFFFF)
+        if rc != 0:
+            raise RuntimeError(f"loop_reset rc={rc}: {_err(self._h)}")
+
+    def loop_run(self, n_frames: int, user_tokens: Optional[np.ndarray] = None, sampling: bool = False,
+                 temp_text: float = 0.7, top_k_text: int = 25, temp_audio: float = 0.8,
+                 top_k_audio: int = 250) -> np.ndarray:
+        """Runs n_frames (1..64) frames on the device; user_tokens [n][8] or
+        None for the daemon's silence tokens.  Returns int32 [n][17]."""
+        out = np.zeros((int(n_frames), self.LOOP_OUT), np.int32)
+        up = None
+        if user_tokens is not None:
+            user_tokens = np.ascontiguousarray(user_tokens, dtype=np.int32)
+            assert user_tokens.shape == (n_frames, 8), user_tokens.shape
+            up = user_tokens.ctypes.data_as(_c_i32p)
+        rc = lib().bmo_loop_run(self._h, int(n_frames), up, 1 if sampling else 0, float(temp_text), int(top_k_text),
+                                float(temp_audio), int(top_k_audio), out.ctypes.data_as(_c_i32p))
+        if rc != 0:
+            raise RuntimeError(f"loop_run rc={rc}: {_err(self._h)}")
+        return out
+
+    @property
+    def loop_frame(self) -> int:
+        """Frames run since loop_reset (-1 before it)."""
+        return int(lib().bmo_loop_frame(self._h))
 
     def forward_temporal(self, tokens: np.ndarray, copy: bool = False) -> Tuple[np.ndarray, np.ndarray]:
         assert tokens.dtype == np.int32 and tokens.shape == (self.n_codebooks,), (

@@ -167,6 +167,31 @@ BMO_API int bmo_batch_kv_import_f32(bmo_handle_t *h, int session, int layer, int
 /* Empties one session's ring (session < 0: all).  Returns 0, 2 for a bad id. */
 BMO_API int bmo_batch_reset(bmo_handle_t *h, int session);
 
+/* ---- the caller's frame loop on the device (replaces the per-frame host
+ * logic of bmo_daemon.cpp:727-816: the 17-channel interleave with its delay,
+ * bmo_forward_temporal, the text sample with pause tokens 3 and 0 kept
+ * greedy, 8 x bmo_forward_depth each followed by its audio sample, the codec
+ * input and the delay-line update).  Each frame is one CUDA graph; a call
+ * of n frames synchronises with the host once. ---- */
+/* Starts a conversation: frame 0, empty KV rings, the daemon's delay-line
+ * start state and its sampler generator std::mt19937(seed) (the daemon seeds
+ * 1337).  Returns 0; 3 when the model has no text head or depformer, its
+ * depformer takes other than 8 steps, it reads other than 9 or 17 input
+ * channels, or the handle is tensor parallel; 9 on a device error. */
+BMO_API int bmo_loop_reset(bmo_handle_t *h, uint32_t seed);
+/* Runs n_frames (1 to 64) frames.  user_tokens: [n_frames][8] the user's
+ * audio tokens, or NULL for the daemon's silence tokens.  use_sampling 0:
+ * first argmax everywhere; otherwise sample_token_cpp's top-k / temperature
+ * draw (min(top_k, logits drawn from) up to 2048; top_k <= 0 or temp <=
+ * 1e-4 is greedy).  out:
+ * [n_frames][17] = text token, 8 audio tokens, 8 codec tokens (the daemon
+ * decodes nothing at frame 0).  Returns 0; 1 null pointer; 2 bad count or
+ * top_k; 4 not reset; 9 device error. */
+BMO_API int bmo_loop_run(bmo_handle_t *h, int n_frames, const int32_t *user_tokens, int use_sampling,
+                         float temp_text, int top_k_text, float temp_audio, int top_k_audio, int32_t *out);
+/* Frames run since bmo_loop_reset, or -1. */
+BMO_API int bmo_loop_frame(bmo_handle_t *h);
+
 /* Waits for the handle's stream; returns the device status word (0 = ok). */
 BMO_API int bmo_sync(bmo_handle_t *h);
 

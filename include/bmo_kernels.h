@@ -148,6 +148,18 @@ BMO_API int bmo_k_tp_exchange(const double *const *parts, unsigned long long *co
                               const float *resid_dev, float *y_dev, int *status_dev, int rank, int size, int n,
                               void *stream);
 
+/* One draw of the daemon's token sampler (sample_token_cpp,
+ * bmo_daemon.cpp:147-175) over logits_dev[0, n) on the device: first argmax
+ * when top_k <= 0 or temp <= 1e-4, else the top_k logits (ties by lower
+ * index), exp(l_i / temp - l_0 / temp) in float and std::discrete_distribution's
+ * draw from std::mt19937.  pause_rule 1 adds the daemon's text rule
+ * (:758-762): a first argmax of 3 or 0 is kept without a draw.  rng_dev holds
+ * 625 words, the generator's 624 state words then its position (624 right
+ * after seeding), and is advanced in place.  min(top_k, n) <= 2048.  One
+ * CTA. */
+BMO_API int bmo_k_sample_token(const float *logits_dev, int n, float temp, int top_k, int pause_rule,
+                               uint32_t *rng_dev, int32_t *out_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

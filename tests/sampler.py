@@ -1,8 +1,9 @@
 """An independent restatement of the reference's depformer token sampler
 (utkarshyadav009/bmo_jetson src/bmo_api.cpp:638-666, sample_token_internal,
 called by bmo_forward_depth_cascade :668-743 with a per-thread
-``std::mt19937 rng(42)`` that lives as long as the thread), for checking the
-library's sampler token for token.  TEST INFRASTRUCTURE.
+``std::mt19937 rng(42)`` that lives as long as the thread; the daemon's
+sample_token_cpp, src/bmo_daemon.cpp:147-175, is the same arithmetic), for
+checking the library's samplers token for token.  TEST INFRASTRUCTURE.
 
 Greedy (first maximum) when top_k <= 0 or temp <= 1e-4.  Otherwise the top_k
 logits in descending order, probs_i = expf(l_i / temp - l_0 / temp) in
@@ -75,6 +76,8 @@ def sample(logits: np.ndarray, temp: float, top_k: int, rng: MT19937) -> int:
         sum_p = np.float32(sum_p + np.float32(p))
     if sum_p <= 0.0 or np.isnan(sum_p):
         return int(top[0])
+    if k < 2:  # libstdc++'s discrete_distribution keeps no table for one weight and draws nothing
+        return int(top[0])
     total = 0.0
     for p in probs:
         total += float(p)
@@ -85,3 +88,13 @@ def sample(logits: np.ndarray, temp: float, top_k: int, rng: MT19937) -> int:
     cum[-1] = 1.0
     u = generate_canonical(rng)
     return int(top[int(np.searchsorted(np.array(cum), u, side="left"))])
+
+
+def daemon_text(logits: np.ndarray, sampling: bool, temp: float, top_k: int, rng: MT19937) -> int:
+    """The daemon's text token (bmo_daemon.cpp:755-762): the first argmax,
+    kept when it is a pause token (3 or 0) or sampling is off, else one
+    draw of the sampler."""
+    top1 = int(np.argmax(np.asarray(logits, np.float32)))
+    if top1 in (3, 0) or not sampling:
+        return top1
+    return sample(logits, temp, top_k, rng)
