@@ -570,6 +570,52 @@ def ref_kernel_timing(peak_gbs, iters=20, flush_bytes=256 << 20):
     return out
 
 
+def loop_measure(e, steps, warmup, tokens):
+    """The daemon's whole frame (bmo_daemon.cpp:727-816: interleave, temporal
+    step, text draw, 8 depformer steps each with its audio draw at the
+    daemon's defaults temp 0.7 / top-k 25 and 0.8 / 250, codec input) through
+    bmo_loop_run, up to 64 frames per call, wall clock around the calls (the
+    host copies of inputs and results included), from frame 0 as the daemon
+    starts.  Beside it the same library driven the daemon's way: per frame
+    bmo_forward_temporal, the text argmax on the host, then
+    bmo_forward_depth_cascade with its host sampler (eight logits round
+    trips)."""
+    params = (0.7, 25, 0.8, 250)
+
+    def run_loop(sampling):
+        e.loop_reset(1337)
+        e.loop_run(max(warmup, 3), None, sampling, *params)
+        done, t0 = 0, time.perf_counter()
+        while done < steps:
+            n = min(64, steps - done)
+            e.loop_run(n, None, sampling, *params)
+            done += n
+        return steps / (time.perf_counter() - t0)
+
+    sampled = run_loop(True)
+    greedy = run_loop(False)
+    e.reset()
+    K, pos = e.n_codebooks, 0
+    for i in range(max(warmup, 3)):
+        e.pos = pos
+        z, lg = e.forward_temporal(tokens[i % len(tokens)][:K])
+        e.forward_depth_cascade(int(np.argmax(lg[:32000])), z, 0.8, 250)
+        pos += 1
+    t0 = time.perf_counter()
+    for i in range(steps):
+        e.pos = pos
+        z, lg = e.forward_temporal(tokens[i % len(tokens)][:K])
+        e.forward_depth_cascade(int(np.argmax(lg[:32000])), z, 0.8, 250)
+        pos += 1
+    host = steps / (time.perf_counter() - t0)
+    return {"value": sampled, "unit": "frames/s", "greedy_value": greedy,
+            "path": "bmo_loop_run (one graph per frame, daemon sampling defaults), wall clock",
+            "h2d_bytes_per_step": 60, "d2h_bytes_per_step": 68 + 4,
+            "host_driven": {"value": host, "unit": "frames/s",
+                            "path": "bmo_forward_temporal + host text argmax + bmo_forward_depth_cascade "
+                                    "(host top-k sampling, temp 0.8, top-k 250), wall clock"}}
+
+
 def workload_config(kv, world):
     """The `config` object both arms print (the same workload, same keys)."""
     return {"workload": "config2+3: 32-layer temporal (d4096, 32x128, FFN 11264) + 32000 text head + greedy 8-step "
@@ -767,6 +813,7 @@ def main():
     rl = gemv_roofline(local, peak)
     total_b, temporal_b, dep_b, kv_b = frame_bytes(e)
     launches_per_frame = e.frame_launches
+    loop = loop_measure(e, args.steps, args.warmup, toks) if e.loop_supported else None
 
     e.close()
     batch = None
@@ -815,6 +862,7 @@ def main():
                     "path": "bmo_forward_temporal + host argmax + bmo_forward_depth_cascade (greedy), wall clock"},
             "gpu_launches": launches_per_frame * args.steps,
             "clocks": clocks.summary(),
+            "loop": loop,
             "batch": batch,
             "batch_split": batch_split,
             "tp": tp,

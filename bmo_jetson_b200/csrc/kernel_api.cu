@@ -337,7 +337,7 @@ int bmo_k_tp_exchange(const double *const *parts, unsigned long long *const *fla
 
 int bmo_k_sample_token(const float *logits_dev, int n, float temp, int top_k, int pause_rule, uint32_t *rng_dev,
                        int32_t *out_dev, void *stream) {
-    if (!logits_dev || !rng_dev || !out_dev || n <= 0 || (top_k < n ? top_k : n) > kLoopTopKMax)
+    if (!logits_dev || !rng_dev || !out_dev || n <= 0 || n > kSampleMaxN || (top_k < n ? top_k : n) > kLoopTopKMax)
         return static_cast<int>(cudaErrorInvalidValue);
     SampleArgs a{};
     a.logits = logits_dev;

@@ -36,7 +36,17 @@ namespace {
 constexpr int kSampleThreads = 1024;
 constexpr unsigned kMtUpper = 0x80000000u, kMtLower = 0x7fffffffu, kMtMatrix = 0x9908b0dfu;
 
-// The standard's mt19937 (state in shared memory, one thread).
+// The standard's mt19937: the output transform of one state word, and the
+// next output (state in shared memory, one thread).
+__device__ __forceinline__ unsigned mt_temper(unsigned y) {
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+
 __device__ unsigned mt_next(unsigned *mt, int &mti) {
     if (mti >= 624) {
         for (int i = 0; i < 624; ++i) {
@@ -45,12 +55,7 @@ __device__ unsigned mt_next(unsigned *mt, int &mti) {
         }
         mti = 0;
     }
-    unsigned y = mt[mti++];
-    y ^= y >> 11;
-    y ^= (y << 7) & 0x9d2c5680u;
-    y ^= (y << 15) & 0xefc60000u;
-    y ^= y >> 18;
-    return y;
+    return mt_temper(mt[mti++]);
 }
 
 }  // namespace
@@ -105,39 +110,68 @@ __global__ void loop_end_kernel(LoopState *st) {
 
 namespace {
 
-// Order-preserving key of a float (larger float, larger key; no NaNs).
+// Order-preserving key of a float (larger float, larger key; no NaNs) and back.
 __device__ __forceinline__ unsigned fkey(float v) {
     const unsigned u = __float_as_uint(v);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+__device__ __forceinline__ float fkey_value(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
-struct SampleSmem {
-    unsigned long long sel[kLoopTopKMax];  // (key << 32) | (~index): descending = value desc, index asc
-    float prob[kLoopTopKMax];
-    double cum[kLoopTopKMax];
+struct alignas(16) SampleSmem {
+    // selected entries as (key << 32) | ~index -- descending order = value
+    // descending, index ascending -- then, after the sort, p_i / total
+    union alignas(16) {
+        unsigned long long sel[kLoopTopKMax + 2];
+        double q[kLoopTopKMax];
+    };
+    unsigned long long srt[kLoopTopKMax];  // the entries in descending order
+    alignas(16) float prob[kLoopTopKMax];
     unsigned mt[624];
     int hist[256];
+    int wsum[32];
     float red_v[32];
     int red_i[32];
-    int warp_cnt[32];
-    int n_sel, n_eq_taken, tok;
+    int n_sel, n_eq_taken, n_eq, kk, tok, draw, mti;
     unsigned prefix;
-    int kk;
+    double total;
 };
+
+// Adds 1 to bin `b` for every lane with `take`, one atomic per distinct bin
+// of the warp.
+__device__ __forceinline__ void hist_add(int *hist, bool take, unsigned b) {
+    const unsigned act = __ballot_sync(0xffffffffu, take);
+    if (!take) return;
+    const unsigned same = __match_any_sync(act, b);
+    if ((threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[b], __popc(same));
+}
 
 }  // namespace
 
 // One token draw (the daemon's sample_token_cpp; first argmax when greedy).
-// One CTA of kSampleThreads threads.
+// One CTA of kSampleThreads threads; thread t holds elements t + j *
+// kSampleThreads, j < ITEMS, as keys in registers.
+template <int ITEMS>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     __shared__ SampleSmem S;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kWarpsS = kSampleThreads / 32;
 
-    // ---- first argmax (std::max_element) ----
+    // ---- the logits as keys, and the first argmax (std::max_element) ----
+    unsigned key[ITEMS];
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = tid; i < a.n; i += kSampleThreads) argmax_merge(bv, bi, __ldcg(a.logits + i), i);
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const int i = tid + j * kSampleThreads;
+        key[j] = 0;
+        if (i < a.n) {
+            const float v = __ldcg(a.logits + i);
+            key[j] = fkey(v);
+            argmax_merge(bv, bi, v, i);
+        }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -172,33 +206,43 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     }
     const int k = min(min(top_k, a.n), kLoopTopKMax);  // the host keeps top_k within kLoopTopKMax
 
-    // ---- the k-th largest key (radix select, 8 bits per pass) ----
+    // ---- the k-th largest key: radix select, 8 bits per pass; the bin is
+    // found by a suffix sum over the 256 bins (threads 0..255) ----
     unsigned prefix = 0, mask = 0;
     int kk = k;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int b = tid; b < 256; b += kSampleThreads) S.hist[b] = 0;
+        if (tid < 256) S.hist[tid] = 0;
         __syncthreads();
-        for (int i = tid; i < a.n; i += kSampleThreads) {
-            const unsigned key = fkey(__ldcg(a.logits + i));
-            if ((key & mask) == prefix) atomicAdd(&S.hist[(key >> shift) & 255], 1);
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const bool take = (tid + j * kSampleThreads < a.n) && (key[j] & mask) == prefix;
+            hist_add(S.hist, take, (key[j] >> shift) & 255u);
         }
         __syncthreads();
-        if (tid == 0) {
-            int cum = 0, b = 255;
-            for (; b > 0; --b) {
-                if (cum + S.hist[b] >= kk) break;
-                cum += S.hist[b];
+        if (tid < 256) {
+            // suffix sum s(b) = sum of hist[b'] over b' >= b
+            const int h = S.hist[tid];
+            int s = h;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_down_sync(0xffffffffu, s, o);
+                if (lane + o < 32) s += t;
             }
-            S.kk = kk - cum;
-            S.prefix = prefix | (static_cast<unsigned>(b) << shift);
+            if (lane == 0) S.wsum[warp] = s;
+            named_sync(1, 256);
+            for (int w = warp + 1; w < 8; ++w) s += S.wsum[w];
+            if (s >= kk && s - h < kk) {  // exactly one bin
+                S.kk = kk - (s - h);
+                S.n_eq = h;
+                S.prefix = prefix | (static_cast<unsigned>(tid) << shift);
+            }
         }
         __syncthreads();
         kk = S.kk;
         prefix = S.prefix;
         mask |= 255u << shift;
-        __syncthreads();
     }
-    const unsigned thr = prefix;  // keys above it are all taken; kk of those equal to it, lowest indices first
+    const unsigned thr = prefix;  // every key above it is taken, and the kk lowest-index keys equal to it
 
     // ---- gather the k entries ----
     if (tid == 0) {
@@ -206,86 +250,112 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
         S.n_eq_taken = 0;
     }
     __syncthreads();
-    for (int base = 0; base < a.n; base += kSampleThreads) {
-        const int i = base + tid;
-        unsigned key = 0;
-        bool gt = false, eq = false;
-        if (i < a.n) {
-            key = fkey(__ldcg(a.logits + i));
-            gt = key > thr;
-            eq = key == thr;
-        }
-        if (gt) S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(key) << 32) | (~static_cast<unsigned>(i));
-        // equal keys in index order: a block-wide exclusive scan of `eq`
-        const unsigned bal = __ballot_sync(0xffffffffu, eq);
-        if (lane == 0) S.warp_cnt[warp] = __popc(bal);
-        __syncthreads();
-        int before = S.n_eq_taken;
-        for (int w = 0; w < warp; ++w) before += S.warp_cnt[w];
-        before += __popc(bal & ((1u << lane) - 1u));
-        if (eq && before < kk) S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(key) << 32) | (~static_cast<unsigned>(i));
-        __syncthreads();
-        if (tid == 0) {
-            int t = 0;
-            for (int w = 0; w < kWarpsS; ++w) t += S.warp_cnt[w];
-            S.n_eq_taken += t;
-        }
-        __syncthreads();
+    const bool all_eq = S.n_eq == kk;  // no tie to break at the threshold (the usual case)
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const int i = tid + j * kSampleThreads;
+        const bool take = i < a.n && (key[j] > thr || (all_eq && key[j] == thr));
+        const unsigned act = __ballot_sync(0xffffffffu, take);
+        int base = 0;
+        if (lane == 0 && act) base = atomicAdd(&S.n_sel, __popc(act));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take)
+            S.sel[base + __popc(act & ((1u << lane) - 1u))] =
+                (static_cast<unsigned long long>(key[j]) << 32) | (~static_cast<unsigned>(i));
     }
-    // ---- sort them (bitonic, descending; padding entries are 0) ----
-    for (int i = S.n_sel + tid; i < kLoopTopKMax; i += kSampleThreads) S.sel[i] = 0;
-    __syncthreads();
-    for (int size = 2; size <= kLoopTopKMax; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < kLoopTopKMax; i += kSampleThreads) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const unsigned long long x = S.sel[i], y = S.sel[j];
-                    if (desc ? (x < y) : (x > y)) {
-                        S.sel[i] = y;
-                        S.sel[j] = x;
-                    }
-                }
+    if (!all_eq) {
+        // keys equal to the threshold in index order: element chunks of
+        // kSampleThreads, each scanned block-wide
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const int i = tid + j * kSampleThreads;
+            const bool eq = i < a.n && key[j] == thr;
+            const unsigned bal = __ballot_sync(0xffffffffu, eq);
+            if (lane == 0) S.wsum[warp] = __popc(bal);
+            __syncthreads();
+            int before = S.n_eq_taken;
+            for (int w = 0; w < warp; ++w) before += S.wsum[w];
+            before += __popc(bal & ((1u << lane) - 1u));
+            if (eq && before < kk)
+                S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(thr) << 32) | (~static_cast<unsigned>(i));
+            __syncthreads();
+            if (tid == 0) {
+                int t = 0;
+                for (int w = 0; w < kWarpsS; ++w) t += S.wsum[w];
+                S.n_eq_taken += t;
             }
             __syncthreads();
         }
     }
-
-    // ---- probabilities: exp(l_i / temp - l_0 / temp) in float ----
-    const int tok0 = static_cast<int>(~static_cast<unsigned>(S.sel[0]));
-    const float max_l = __fdiv_rn(__ldcg(a.logits + tok0), temp);
+    __syncthreads();
+    // ---- sort them: each entry's rank is the number of larger entries ----
+    if (tid < 2) S.sel[k + tid] = 0;  // padding below every entry
+    __syncthreads();
     for (int i = tid; i < k; i += kSampleThreads) {
-        const float li = __ldcg(a.logits + (~static_cast<unsigned>(S.sel[i])));
+        const unsigned long long x = S.sel[i];
+        int r = 0;
+        const ulonglong2 *p2 = reinterpret_cast<const ulonglong2 *>(S.sel);
+        for (int j = 0; j < (k + 1) / 2; ++j) {
+            const ulonglong2 y = p2[j];
+            r += (y.x > x) + (y.y > x);
+        }
+        S.srt[r] = x;
+    }
+    __syncthreads();
+
+    // ---- probabilities: exp(l_i / temp - l_0 / temp), rounded to float ----
+    const float max_l = __fdiv_rn(fkey_value(static_cast<unsigned>(S.srt[0] >> 32)), temp);
+    for (int i = tid; i < k; i += kSampleThreads) {
+        const float li = fkey_value(static_cast<unsigned>(S.srt[i] >> 32));
         S.prob[i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(__fdiv_rn(li, temp), max_l))));
     }
     __syncthreads();
-    // their float sum must be positive; std::discrete_distribution normalises
-    // by the sequential double sum and draws nothing for a single weight
+    // their float sum in order must be positive; std::discrete_distribution
+    // normalises by the double sum in order and draws nothing for one weight
     if (tid == 0) {
         float sum_p = 0.0f;
-        for (int i = 0; i < k; ++i) sum_p = __fadd_rn(sum_p, S.prob[i]);
-        const bool draw = sum_p > 0.0f && !isnan(sum_p) && k >= 2;
         double total = 0.0;
-        if (draw)
-            for (int i = 0; i < k; ++i) total = __dadd_rn(total, static_cast<double>(S.prob[i]));
-        S.cum[0] = total;
-        S.tok = draw ? 1 : 0;
+        int i = 0;
+        for (; i + 4 <= k; i += 4) {
+            const float4 p = *reinterpret_cast<const float4 *>(S.prob + i);
+            sum_p = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum_p, p.x), p.y), p.z), p.w);
+            total = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(total, static_cast<double>(p.x)), static_cast<double>(p.y)),
+                                        static_cast<double>(p.z)),
+                              static_cast<double>(p.w));
+        }
+        for (; i < k; ++i) {
+            sum_p = __fadd_rn(sum_p, S.prob[i]);
+            total = __dadd_rn(total, static_cast<double>(S.prob[i]));
+        }
+        S.draw = sum_p > 0.0f && !isnan(sum_p) && k >= 2;
+        S.total = total;
+        S.mti = *a.mti;
     }
     __syncthreads();
-    if (!S.tok) {
+    const int tok0 = static_cast<int>(~static_cast<unsigned>(S.srt[0]));
+    if (!S.draw) {
         if (tid == 0) *a.out = tok0;
         return;
     }
-    const double total = S.cum[0];
-    __syncthreads();
-    for (int i = tid; i < k; i += kSampleThreads) S.cum[i] = __ddiv_rn(static_cast<double>(S.prob[i]), total);
-    for (int i = tid; i < 624; i += kSampleThreads) S.mt[i] = a.mt[i];
+    const double total = S.total;
+    for (int i = tid; i < k; i += kSampleThreads) S.q[i] = __ddiv_rn(static_cast<double>(S.prob[i]), total);
+    // the generator: two outputs; its 624 words pass through shared memory
+    // only when they are regenerated (every 312 draws)
+    const bool twist = S.mti + 2 > 624;
+    if (twist)
+        for (int i = tid; i < 624; i += kSampleThreads) S.mt[i] = a.mt[i];
     __syncthreads();
     if (tid == 0) {
-        int mti = *a.mti;
-        const unsigned g1 = mt_next(S.mt, mti);
-        const unsigned g2 = mt_next(S.mt, mti);
+        int mti = S.mti;
+        unsigned g1, g2;
+        if (twist) {
+            g1 = mt_next(S.mt, mti);
+            g2 = mt_next(S.mt, mti);
+        } else {
+            g1 = mt_temper(a.mt[mti]);
+            g2 = mt_temper(a.mt[mti + 1]);
+            mti += 2;
+        }
         double u = __dadd_rn(static_cast<double>(g1), __dmul_rn(static_cast<double>(g2), 4294967296.0));
         u = __ddiv_rn(u, 18446744073709551616.0);
         if (u >= 1.0) u = 0x1.fffffffffffffp-1;  // the largest double below 1
@@ -293,17 +363,19 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
         double run = 0.0;
         int pick = k - 1;
         for (int i = 0; i < k - 1; ++i) {
-            run = __dadd_rn(run, S.cum[i]);
+            run = __dadd_rn(run, S.q[i]);
             if (run >= u) {
                 pick = i;
                 break;
             }
         }
-        *a.out = static_cast<int>(~static_cast<unsigned>(S.sel[pick]));
+        *a.out = static_cast<int>(~static_cast<unsigned>(S.srt[pick]));
         *a.mti = mti;
     }
-    __syncthreads();
-    for (int i = tid; i < 624; i += kSampleThreads) a.mt[i] = S.mt[i];
+    if (twist) {
+        __syncthreads();
+        for (int i = tid; i < 624; i += kSampleThreads) a.mt[i] = S.mt[i];
+    }
 }
 
 cudaError_t launch_loop_begin(LoopState *st, const LoopConfig &cfg, int *tokens, int *n_tok, int *pos,
@@ -317,12 +389,15 @@ cudaError_t launch_loop_end(LoopState *st, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-// The sampler takes min(top_k, n) up to kLoopTopKMax; the host checks the
-// caller's values before they reach the device.
+// The sampler takes n up to kSampleMaxN and min(top_k, n) up to
+// kLoopTopKMax; the host checks the caller's values before they reach the
+// device.
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s) {
-    if (a.n <= 0 || !a.logits || !a.mt || !a.mti || !a.out || (!a.st && a.sampling && std::min(a.top_k, a.n) > kLoopTopKMax))
+    if (a.n <= 0 || a.n > kSampleMaxN || !a.logits || !a.mt || !a.mti || !a.out ||
+        (!a.st && a.sampling && std::min(a.top_k, a.n) > kLoopTopKMax))
         return cudaErrorInvalidValue;
-    sample_kernel<<<1, kSampleThreads, 0, s>>>(a);
+    if (a.n <= 2 * kSampleThreads) sample_kernel<2><<<1, kSampleThreads, 0, s>>>(a);
+    else sample_kernel<kSampleMaxN / kSampleThreads><<<1, kSampleThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -251,6 +251,7 @@ struct DepCascadeArgs {
 // std::mt19937 its samplers share, and this frame's results.
 constexpr int kLoopCb = 8;          // audio codebooks of an agent (and of the user)
 constexpr int kLoopTopKMax = 2048;  // largest top-k the device sampler takes (the audio vocabulary)
+constexpr int kSampleMaxN = 32768;  // most logits the device sampler draws from (Moshi text: 32000)
 constexpr int kLoopOut = 1 + 2 * kLoopCb;  // a frame's results: text, audio[8], codec input[8]
 constexpr int kLoopRing = 64;       // frames of results kept on the device
 // The caller's per-frame inputs, copied to the device before each frame.

@@ -117,6 +117,8 @@ def lib() -> ctypes.CDLL:
     L.bmo_loop_run.restype = i
     L.bmo_loop_frame.argtypes = [vp]
     L.bmo_loop_frame.restype = i
+    L.bmo_loop_supported.argtypes = [vp]
+    L.bmo_loop_supported.restype = i
     L.bmo_last_error.argtypes = [vp]
     L.bmo_last_error.restype = ctypes.c_char_p
     L.bmo_rvq_decode.argtypes = [vp, vp, vp, vp]
@@ -293,6 +295,12 @@ class BMOEngine:
         if rc != 0:
             raise RuntimeError(f"loop_run rc={rc}: {_err(self._h)}")
         return out
+
+    @property
+    def loop_supported(self) -> bool:
+        """True when the model runs the daemon's frame loop on the device
+        (text head, 8 depformer steps, 9 or 17 input channels, one GPU)."""
+        return bool(lib().bmo_loop_supported(self._h))
 
     @property
     def loop_frame(self) -> int:

@@ -189,6 +189,8 @@ BMO_API int bmo_loop_reset(bmo_handle_t *h, uint32_t seed);
  * top_k; 4 not reset; 9 device error. */
 BMO_API int bmo_loop_run(bmo_handle_t *h, int n_frames, const int32_t *user_tokens, int use_sampling,
                          float temp_text, int top_k_text, float temp_audio, int top_k_audio, int32_t *out);
+/* 1 when the model runs the frame loop (the conditions of bmo_loop_reset). */
+BMO_API int bmo_loop_supported(bmo_handle_t *h);
 /* Frames run since bmo_loop_reset, or -1. */
 BMO_API int bmo_loop_frame(bmo_handle_t *h);
 

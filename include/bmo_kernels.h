@@ -155,8 +155,8 @@ BMO_API int bmo_k_tp_exchange(const double *const *parts, unsigned long long *co
  * draw from std::mt19937.  pause_rule 1 adds the daemon's text rule
  * (:758-762): a first argmax of 3 or 0 is kept without a draw.  rng_dev holds
  * 625 words, the generator's 624 state words then its position (624 right
- * after seeding), and is advanced in place.  min(top_k, n) <= 2048.  One
- * CTA. */
+ * after seeding), and is advanced in place.  n <= 32768, min(top_k, n) <=
+ * 2048.  One CTA. */
 BMO_API int bmo_k_sample_token(const float *logits_dev, int n, float temp, int top_k, int pause_rule,
                                uint32_t *rng_dev, int32_t *out_dev, void *stream);
 
