@@ -297,6 +297,8 @@ int bmo_loop_run(bmo_handle_t *h, int n_frames, const int32_t *user_tokens, int 
     return 0;
 }
 
+int bmo_get_tiled_weights(bmo_handle_t *h) { return h ? h->eng->tiled_weights() : 0; }
+
 int bmo_loop_supported(bmo_handle_t *h) { return (h && h->eng->loop_supported()) ? 1 : 0; }
 
 int bmo_loop_frame(bmo_handle_t *h) {

@@ -308,6 +308,22 @@ QMatDesc Engine::upload_q4(const GgufTensor *t, int perm, int swiglu_f, int64_t 
     if (cols % 32) throw std::runtime_error("weight " + t->name + ": row length not a multiple of 32");
     if (rows < 0) rows = t->rows() - row0;
     if (row0 + rows > t->rows()) throw std::runtime_error("weight " + t->name + ": row slice out of range");
+    // a repacked file's tiles, when the slice is whole row tiles of the stored form
+    if (t->tiled && t->tiled_perm == perm) {
+        const bool whole = row0 == 0 && rows == t->rows();
+        const bool ok = perm == kPermSwiGLU
+                            ? whole && t->tiled_f == swiglu_f
+                            : row0 % kTileRows == 0 && (rows % kTileRows == 0 || row0 + rows == t->rows());
+        if (ok) {
+            const size_t tile_bytes = static_cast<size_t>(round_up(static_cast<size_t>(cols / 32), kChunkBlocks) /
+                                                          kChunkBlocks) * kChunkBytes;
+            return upload_q4_tiled(t->name, t->tiled + static_cast<size_t>(row0 / kTileRows) * tile_bytes, rows, cols,
+                                   perm, swiglu_f);
+        }
+    }
+    if (!t->data)
+        throw std::runtime_error("weight " + t->name + ": this slice needs the raw Q4_0 rows, which the repacked file "
+                                 "does not keep (repack with --keep-raw)");
     const size_t row_bytes = static_cast<size_t>(cols / 32) * 18;
     return upload_q4_raw(t->name, t->data + static_cast<size_t>(row0) * row_bytes, rows, cols, perm, swiglu_f);
 }
@@ -319,6 +335,9 @@ QMatDesc Engine::upload_q4_sel(const GgufTensor *t, int perm, int swiglu_f,
     const int64_t cols = t->ne[0];
     if (cols % 32 || col0 % 32 || ncols % 32 || col0 < 0 || ncols <= 0 || col0 + ncols > cols)
         throw std::runtime_error("weight " + t->name + ": column slice not on 32-column blocks");
+    if (!t->data)
+        throw std::runtime_error("weight " + t->name + ": tensor-parallel shards need the raw Q4_0 rows, which the "
+                                 "repacked file does not keep (repack with --keep-raw)");
     int64_t rows = 0;
     for (const auto &r : row_ranges) {
         if (r.first < 0 || r.second <= 0 || r.first + r.second > t->rows())
@@ -358,9 +377,30 @@ QMatDesc Engine::upload_q4_raw(const std::string &name, const uint8_t *src, int6
     return m;
 }
 
+// A matrix already in the row-tile layout (a repacked file): one copy.
+QMatDesc Engine::upload_q4_tiled(const std::string &name, const uint8_t *tiles, int64_t rows, int64_t cols, int perm,
+                                 int swiglu_f) {
+    QMatDesc m{};
+    m.rows = static_cast<int>(perm == kPermSwiGLU ? 2 * swiglu_f : rows);
+    m.cols = static_cast<int>(cols);
+    m.nbx = static_cast<int>(round_up(static_cast<size_t>(cols / 32), kChunkBlocks));
+    m.cpt = m.nbx / kChunkBlocks;
+    m.perm = perm;
+    m.swiglu_f = swiglu_f;
+    m.n_tiles = static_cast<int>(perm == kPermSwiGLU ? swiglu_f / 16 : (rows + kTileRows - 1) / kTileRows);
+    if (m.nbx > gemv_max_nbx()) throw std::runtime_error("weight " + name + ": row length exceeds the GEMV limit");
+    const size_t bytes = static_cast<size_t>(m.n_tiles) * m.cpt * kChunkBytes;
+    void *dst = arena(bytes);
+    m.tiles = static_cast<const uint8_t *>(dst);
+    ck(cudaMemcpy(dst, tiles, bytes, cudaMemcpyHostToDevice), "upload tiled weight");
+    ++tiled_weights_;
+    return m;
+}
+
 float *Engine::upload_f32(const GgufTensor *t, int64_t n) {
     if (!t) return nullptr;
     if (t->type != kTF32) throw std::runtime_error("tensor " + t->name + " must be F32");
+    if (!t->data) throw std::runtime_error("tensor " + t->name + " has no data in the file");
     if (static_cast<int64_t>(t->nbytes / 4) < n) throw std::runtime_error("tensor " + t->name + " is too short");
     float *d = static_cast<float *>(arena(static_cast<size_t>(n) * 4));
     ck(cudaMemcpy(d, t->data, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "upload f32");
@@ -374,6 +414,7 @@ EmbTable Engine::upload_table(const GgufTensor *t) {
     case kTF32: case kTF16: case kTBF16: case kTQ4_0: case kTQ8_0: break;
     default: throw std::runtime_error("embedding table " + t->name + " has an unsupported type");
     }
+    if (!t->data) throw std::runtime_error("embedding table " + t->name + " has no raw rows in the file");
     void *d = arena(t->nbytes);
     ck(cudaMemcpy(d, t->data, t->nbytes, cudaMemcpyHostToDevice), "upload table");
     e.data = d;

@@ -114,6 +114,7 @@ public:
     int frame_launches() const;  // kernels one greedy frame launches (embed, temporal ops, cascade)
     bool dep_grid() const { return dep_grid_; }
     bool tp_exchange() const { return tp_p2p_; }
+    int tiled_weights() const { return tiled_weights_; }  // weights copied from a repacked file's tiles
 
     // ---- the caller's frame loop on the device (bmo_daemon.cpp:641-816):
     // interleave, temporal step, text sample, dep_q depformer steps with
@@ -162,6 +163,9 @@ private:
                            const std::vector<std::pair<int64_t, int64_t>> &row_ranges, int64_t col0, int64_t ncols);
     QMatDesc upload_q4_raw(const std::string &name, const uint8_t *src, int64_t rows, int64_t cols, int perm,
                            int swiglu_f);
+    QMatDesc upload_q4_tiled(const std::string &name, const uint8_t *tiles, int64_t rows, int64_t cols, int perm,
+                             int swiglu_f);
+    int tiled_weights_ = 0;
     float *upload_f32(const GgufTensor *t, int64_t n);
     EmbTable upload_table(const GgufTensor *t);
     GemvArgs gemv_base(const QMatDesc &m) const;

@@ -12,6 +12,8 @@
 
 namespace bmo {
 
+size_t q4_0_tiled_bytes_host(int64_t rows, int64_t cols, int perm, int swiglu_f);  // tiling.cpp
+
 namespace {
 
 enum : uint32_t {
@@ -101,6 +103,11 @@ void GgufFile::open(const std::string &path) {
         if (key == "general.alignment" && type == kU32) {
             alignment = r.get<uint32_t>();
             if (alignment == 0 || (alignment & (alignment - 1))) throw std::runtime_error("gguf: bad alignment");
+        } else if (key == "bmo.tiled.version" && type == kU32) {
+            tiled_version_ = r.get<uint32_t>();
+            if (tiled_version_ != 1)
+                throw std::runtime_error("gguf: repacked with tiled layout version " + std::to_string(tiled_version_) +
+                                         "; this build reads version 1");
         } else {
             r.skip_value(type);
         }
@@ -130,20 +137,68 @@ void GgufFile::open(const std::string &path) {
         }
         index_[t.name] = i;
     }
+    if (tiled_version_) attach_tiled();
+}
+
+// Pairs each "bmo.tiled:N" with its descriptor and hangs it on N, adding N
+// (without raw rows) when the file dropped them.
+void GgufFile::attach_tiled() {
+    static const std::string kTiled = "bmo.tiled:", kDesc = "bmo.tiled_desc:";
+    const size_t n0 = tensors_.size();
+    std::vector<GgufTensor> added;
+    for (size_t i = 0; i < n0; ++i) {
+        const GgufTensor &tt = tensors_[i];
+        if (tt.name.compare(0, kTiled.size(), kTiled) != 0) continue;
+        const std::string name = tt.name.substr(kTiled.size());
+        auto di = index_.find(kDesc + name);
+        if (tt.type != 24 || !tt.data || di == index_.end())
+            throw std::runtime_error("gguf: tiled tensor without its descriptor: " + name);
+        const GgufTensor &d = tensors_[di->second];
+        if (d.type != 26 || !d.data || d.ne[0] != 4) throw std::runtime_error("gguf: bad tiled descriptor: " + name);
+        int32_t v[4];
+        std::memcpy(v, d.data, sizeof(v));
+        const int64_t cols = v[0], rows = v[1];
+        const int perm = v[2], f = v[3];
+        const size_t want = q4_0_tiled_bytes_host(rows, cols, perm, f);
+        if (want == 0 || want != tt.nbytes) throw std::runtime_error("gguf: tiled tensor size does not match its shape: " + name);
+        auto ri = index_.find(name);
+        GgufTensor *raw = ri == index_.end() ? nullptr : &tensors_[ri->second];
+        if (raw && (raw->type != 2 || raw->ne[0] != cols || raw->rows() != rows))
+            throw std::runtime_error("gguf: tiled tensor does not match its raw rows: " + name);
+        GgufTensor v2;
+        GgufTensor &t = raw ? *raw : v2;
+        if (!raw) {
+            t.name = name;
+            t.type = 2;  // Q4_0
+            t.n_dims = 2;
+            t.ne[0] = cols;
+            t.ne[1] = rows;
+            t.nbytes = static_cast<size_t>(rows * (cols / 32) * 18);
+        }
+        t.tiled = tt.data;
+        t.tiled_bytes = tt.nbytes;
+        t.tiled_perm = perm;
+        t.tiled_f = f;
+        if (!raw) added.push_back(t);
+    }
+    for (auto &t : added) {
+        index_[t.name] = tensors_.size();
+        tensors_.push_back(t);
+    }
 }
 
 const GgufTensor *GgufFile::find(const std::string &name) const {
     auto it = index_.find(name);
     if (it == index_.end()) return nullptr;
     const GgufTensor *t = &tensors_[it->second];
-    return t->data ? t : nullptr;
+    return (t->data || t->tiled) ? t : nullptr;
 }
 
 int32_t GgufFile::scalar_i32(const std::string &name, int32_t fallback) const {
     // Like the reference loader (bmo.cpp:62-70) the first four bytes are read
     // whatever the element type.
     const GgufTensor *t = find(name);
-    if (!t || t->nbytes < 4) return fallback;
+    if (!t || !t->data || t->nbytes < 4) return fallback;
     int32_t v;
     std::memcpy(&v, t->data, 4);
     return v;
@@ -151,7 +206,7 @@ int32_t GgufFile::scalar_i32(const std::string &name, int32_t fallback) const {
 
 float GgufFile::scalar_f32(const std::string &name, float fallback) const {
     const GgufTensor *t = find(name);
-    if (!t || t->nbytes < 4) return fallback;
+    if (!t || !t->data || t->nbytes < 4) return fallback;
     float v;
     std::memcpy(&v, t->data, 4);
     return v;

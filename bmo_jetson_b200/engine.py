@@ -53,7 +53,8 @@ def lib() -> ctypes.CDLL:
     for name in ("bmo_get_n_layers", "bmo_get_n_embd", "bmo_get_n_codebooks", "bmo_get_dep_q", "bmo_get_text_vocab",
                  "bmo_get_audio_vocab", "bmo_get_n_attn_heads", "bmo_get_head_dim", "bmo_capture_graphs",
                  "bmo_has_cuda_graphs", "bmo_get_kv_type", "bmo_get_n_ctx", "bmo_get_n_kv_heads", "bmo_get_device",
-                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order", "bmo_get_dep_mode", "bmo_get_frame_launches"):
+                 "bmo_get_pos", "bmo_sync", "bmo_get_ref_order", "bmo_get_dep_mode", "bmo_get_frame_launches",
+                 "bmo_get_tiled_weights"):
         fn = getattr(L, name)
         fn.argtypes = [vp]
         fn.restype = i
@@ -262,6 +263,11 @@ class BMOEngine:
     def frame_launches(self) -> int:
         """Kernels one greedy frame launches on the device."""
         return int(lib().bmo_get_frame_launches(self._h))
+
+    @property
+    def tiled_weights(self) -> int:
+        """GEMV weights copied from a repacked file's tiles (0 for a plain GGUF)."""
+        return int(lib().bmo_get_tiled_weights(self._h))
 
     @property
     def dep_mode(self) -> int:

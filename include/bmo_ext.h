@@ -207,6 +207,24 @@ BMO_API void bmo_synth_q4_0(uint64_t seed, uint64_t stream, long long rows, long
 /* ggml Q4_0 reference quantiser (18-byte blocks) over n floats. */
 BMO_API void bmo_quantize_q4_0_ref(const float *x, long long n, uint8_t *out);
 
+/* ---- offline repacking (bmo_jetson_b200/repack.py) ----
+ * A repacked GGUF carries the key bmo.tiled.version = 1 and, for each Q4_0
+ * matrix N, the I8 tensor "bmo.tiled:N" holding N in the device's row-tile
+ * layout and the I32 tensor "bmo.tiled_desc:N" = {cols, rows, perm,
+ * swiglu_f} (perm 0 rows in order, 1 the SwiGLU gate/up pairing with
+ * F = swiglu_f); N itself is dropped unless the file was repacked with its
+ * raw rows kept.  The loader copies such tiles into the weight arena as they
+ * are (no staging, no repack kernel); slices that are not whole row tiles of
+ * the stored form (tensor-parallel shards) need the raw rows. */
+/* Tiles a rows x cols Q4_0 matrix (ggml's row-major 18-byte blocks) on the
+ * host into the layout the load-time repack produces on the device, byte for
+ * byte.  dst NULL: returns the bytes needed.  Returns the bytes written, or
+ * -1 for a shape the GEMV does not take. */
+BMO_API long long bmo_q4_0_tile_host(const uint8_t *raw, long long rows, long long cols, int perm, int swiglu_f,
+                                     uint8_t *dst);
+/* Weights of the handle's model that were loaded from pre-tiled tensors. */
+BMO_API int bmo_get_tiled_weights(bmo_handle_t *h);
+
 #ifdef __cplusplus
 }
 #endif
