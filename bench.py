@@ -693,6 +693,8 @@ def main():
                     help="config 5: one session tensor-parallel over the --gpus ranks (prints its own line)")
     ap.add_argument("--tp-frames", type=int, default=3000,
                     help="N > 1: frames of the tensor-parallel session measured after the data-parallel one (0: skip)")
+    ap.add_argument("--loop-only", action="store_true",
+                    help="only the frame loop on the device (bmo_loop_run, daemon sampling) and its host-driven twin")
     ap.add_argument("--profile-frames", type=int, default=0,
                     help="profiling: run --warmup frames then this many device-resident frames, print nothing else")
     args = ap.parse_args()
@@ -732,6 +734,16 @@ def main():
     fill_history(e)
     assert e.capture_graphs() == 0
     K = e.n_codebooks
+    if args.loop_only:
+        toks = frame_tokens(max(args.steps, 8), K, e.text_vocab, e.audio_vocab)
+        r = loop_measure(e, args.steps, args.warmup, toks)
+        e.close()
+        if rank == 0:
+            print(json.dumps({"loop": r, "steps": args.steps, "warmup": args.warmup,
+                              "config": workload_config(args.kv, world)}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
     if args.profile_frames > 0:
         n = args.warmup + args.profile_frames
         toks = torch.from_numpy(frame_tokens(n, K, e.text_vocab, e.audio_vocab)).to(torch.device("cuda", local))

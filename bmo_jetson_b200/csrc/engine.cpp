@@ -1202,7 +1202,19 @@ void Engine::reset_depth_kv_async(cudaStream_t s) {
     ck(cudaMemsetAsync(dv_cache_, 0, dkv_bytes_, s), "reset depth kv");
 }
 
-void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first) {
+// One greedy frame: the depformer rings are emptied first, so that kernels
+// alone run from the text head into the cascade (programmatic launches chain
+// them), then the temporal step and the cascade on its hidden state.
+void Engine::enqueue_frame_greedy(cudaStream_t s) {
+    reset_depth_kv_async(s);
+    enqueue_temporal(s);
+    TokenSrc t{};
+    t.pairs = tpairs_;
+    t.n_pairs = text_head_.n_tiles;
+    enqueue_cascade(s, z_, t, false);
+}
+
+void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first, bool reset_kv) {
     if (dep_cluster_ || dep_grid_) {
         DepCascadeArgs a = dep_args_;
         a.z = z;
@@ -1212,7 +1224,7 @@ void Engine::enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &fir
         else ck(launch_dep_cascade(a, dep_smem_, s, cfg_.pdl), "launch depformer cascade");
         return;
     }
-    reset_depth_kv_async(s);
+    if (reset_kv) reset_depth_kv_async(s);
     std::vector<FramePhase> v;
     ops_cascade(v, z, first);
     enqueue_ops(s, v);
@@ -1357,13 +1369,7 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
     fin_h_->n_tok = K;
     fin_h_->pos = pos;
     ck(cudaMemcpyAsync(fin_d_, fin_h_, sizeof(FrameIn), cudaMemcpyHostToDevice, stream), "input copy");
-    launch(g_frame_, [this](cudaStream_t s) {
-        enqueue_temporal(s);
-        TokenSrc t{};
-        t.pairs = tpairs_;
-        t.n_pairs = text_head_.n_tiles;
-        enqueue_cascade(s, z_, t);
-    });
+    launch(g_frame_, [this](cudaStream_t s) { enqueue_frame_greedy(s); });
     ck(cudaMemcpyAsync(z_h_, z_, sizeof(float) * n_embd, cudaMemcpyDeviceToHost, stream), "z copy");
     ck(cudaMemcpyAsync(logits_h_, logits_, sizeof(float) * text_vocab, cudaMemcpyDeviceToHost, stream), "logits copy");
     ck(cudaMemcpyAsync(tok_h_, tok_out_, sizeof(int) * (1 + kDepQMax), cudaMemcpyDeviceToHost, stream), "tokens copy");
@@ -1376,13 +1382,7 @@ void Engine::run_frame_greedy(const int32_t *tokens, int K, int pos, int32_t *ou
 void Engine::enqueue_frame_device(const int32_t *tokens_dev, int K, int pos, int32_t *out_tokens_dev) {
     ck(cudaSetDevice(device), "cudaSetDevice");
     ck(launch_set_frame(fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, tokens_dev, K, pos, stream), "set frame");
-    launch(g_frame_, [this](cudaStream_t s) {
-        enqueue_temporal(s);
-        TokenSrc t{};
-        t.pairs = tpairs_;
-        t.n_pairs = text_head_.n_tiles;
-        enqueue_cascade(s, z_, t);
-    });
+    launch(g_frame_, [this](cudaStream_t s) { enqueue_frame_greedy(s); });
     if (out_tokens_dev)
         ck(cudaMemcpyAsync(out_tokens_dev, tok_out_, sizeof(int) * (1 + dep_q), cudaMemcpyDeviceToDevice, stream),
            "tokens copy");
@@ -1453,6 +1453,9 @@ void Engine::enqueue_loop_frame(cudaStream_t s) {
     c.audio_pad = audio_vocab;
     c.n_tok = num_codebooks;
     ck(launch_loop_begin(loop_st_, c, fin_d_->tokens, &fin_d_->n_tok, &fin_d_->pos, s), "launch loop begin");
+    // the depformer rings are emptied here, so that kernels alone run from the
+    // text head to the last audio draw (programmatic launches chain them)
+    reset_depth_kv_async(s);
     enqueue_temporal(s);
     SampleArgs sa{};
     sa.st = loop_st_;
@@ -1462,8 +1465,7 @@ void Engine::enqueue_loop_frame(cudaStream_t s) {
     sa.n = c.text_n;
     sa.text = 1;
     sa.out = &loop_st_->next_text;
-    ck(launch_sample(sa, s), "launch text sample");
-    reset_depth_kv_async(s);
+    ck(launch_sample(sa, s, cfg_.pdl), "launch text sample");
     for (int cb = 0; cb < dep_q; ++cb) {
         TokenSrc t{};
         t.tok = cb == 0 ? &loop_st_->next_text : &loop_st_->audio[cb - 1];
@@ -1472,7 +1474,7 @@ void Engine::enqueue_loop_frame(cudaStream_t s) {
         sa.n = c.audio_n;
         sa.text = 0;
         sa.out = &loop_st_->audio[cb];
-        ck(launch_sample(sa, s), "launch audio sample");
+        ck(launch_sample(sa, s, cfg_.pdl), "launch audio sample");
     }
     ck(launch_loop_end(loop_st_, s), "launch loop end");
 }
@@ -1541,13 +1543,7 @@ void Engine::capture_all() {
                 enqueue_cascade(s, dz_, t);
             });
         if (!g_frame_ && has_text_head)
-            g_frame_ = capture([this](cudaStream_t s) {
-                enqueue_temporal(s);
-                TokenSrc t{};
-                t.pairs = tpairs_;
-                t.n_pairs = text_head_.n_tiles;
-                enqueue_cascade(s, z_, t);
-            });
+            g_frame_ = capture([this](cudaStream_t s) { enqueue_frame_greedy(s); });
     }
     graphs_ready_ = true;
 }

@@ -182,7 +182,8 @@ private:
     void enqueue_temporal(cudaStream_t s);
     void enqueue_layer(cudaStream_t s, int l);
     void enqueue_depth_step(cudaStream_t s, int cb, const float *z, const TokenSrc &tok);
-    void enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first);
+    void enqueue_cascade(cudaStream_t s, const float *z, const TokenSrc &first, bool reset_kv = true);
+    void enqueue_frame_greedy(cudaStream_t s);
     void reset_depth_kv_async(cudaStream_t s);
     void choose_semantics(int want);
     // tensor parallel

@@ -349,7 +349,7 @@ int bmo_k_sample_token(const float *logits_dev, int n, float temp, int top_k, in
     a.mt = rng_dev;
     a.mti = reinterpret_cast<int *>(rng_dev + 624);
     a.out = out_dev;
-    return static_cast<int>(launch_sample(a, static_cast<cudaStream_t>(stream)));
+    return static_cast<int>(launch_sample(a, static_cast<cudaStream_t>(stream), false));
 }
 
 }  // extern "C"

@@ -157,6 +157,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     __shared__ SampleSmem S;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kWarpsS = kSampleThreads / 32;
+    // Launched as a programmatic dependent of the logits' GEMV: wait for it,
+    // then let the next step's kernels launch and stage their weights while
+    // the draw runs (they wait for this grid before reading its token).
+    pdl_wait();
+    pdl_launch_dependents();
 
     // ---- the logits as keys, and the first argmax (std::max_element) ----
     unsigned key[ITEMS];
@@ -392,13 +397,21 @@ cudaError_t launch_loop_end(LoopState *st, cudaStream_t s) {
 // The sampler takes n up to kSampleMaxN and min(top_k, n) up to
 // kLoopTopKMax; the host checks the caller's values before they reach the
 // device.
-cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s) {
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl) {
     if (a.n <= 0 || a.n > kSampleMaxN || !a.logits || !a.mt || !a.mti || !a.out ||
         (!a.st && a.sampling && std::min(a.top_k, a.n) > kLoopTopKMax))
         return cudaErrorInvalidValue;
-    if (a.n <= 2 * kSampleThreads) sample_kernel<2><<<1, kSampleThreads, 0, s>>>(a);
-    else sample_kernel<kSampleMaxN / kSampleThreads><<<1, kSampleThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kSampleThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (a.n <= 2 * kSampleThreads) return cudaLaunchKernelEx(&cfg, sample_kernel<2>, a);
+    return cudaLaunchKernelEx(&cfg, sample_kernel<kSampleMaxN / kSampleThreads>, a);
 }
 
 }  // namespace bmo

@@ -115,7 +115,7 @@ cudaError_t launch_finalize_token(const float2 *pairs, int n, int *out, cudaStre
 cudaError_t launch_loop_begin(LoopState *st, const LoopConfig &cfg, int *tokens, int *n_tok, int *pos,
                               cudaStream_t s);
 cudaError_t launch_loop_end(LoopState *st, cudaStream_t s);
-cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s);
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl);
 
 cudaError_t configure_kernels();
 cudaError_t launch_repack_q4_0(const void *src, void *dst, int rows, int cols, const QMatDesc &m, cudaStream_t s);
