@@ -134,6 +134,7 @@ struct alignas(16) SampleSmem {
     float red_v[32];
     int red_i[32];
     int n_sel, n_eq_taken, n_eq, kk, tok, draw, mti;
+    unsigned long long units;
     unsigned prefix;
     double total;
 };
@@ -147,34 +148,130 @@ __device__ __forceinline__ void hist_add(int *hist, bool take, unsigned b) {
     if ((threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[b], __popc(same));
 }
 
+// The kk-th largest (1-based) of the keys the block offers, by radix select
+// over 8-bit digits: `each(f)` calls f(valid, key) for each of the calling
+// thread's keys.  Returns the key; *n_eq is the number of offered keys equal
+// to it and *kk_eq how many of those the kk largest take.  All threads call.
+template <class Each>
+__device__ unsigned radix_kth(SampleSmem &S, int kk, Each each, int *n_eq, int *kk_eq) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned prefix = 0, mask = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        if (tid < 256) S.hist[tid] = 0;
+        __syncthreads();
+        each([&](bool valid, unsigned key) { hist_add(S.hist, valid && (key & mask) == prefix, (key >> shift) & 255u); });
+        __syncthreads();
+        if (tid < 256) {
+            // suffix sum s(b) = sum of hist[b'] over b' >= b; the bin with
+            // s(b + 1) < kk <= s(b) holds the kk-th largest
+            const int h = S.hist[tid];
+            int s = h;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_down_sync(0xffffffffu, s, o);
+                if (lane + o < 32) s += t;
+            }
+            if (lane == 0) S.wsum[warp] = s;
+            named_sync(1, 256);
+            for (int w = warp + 1; w < 8; ++w) s += S.wsum[w];
+            if (s >= kk && s - h < kk) {
+                S.kk = kk - (s - h);
+                S.n_eq = h;
+                S.prefix = prefix | (static_cast<unsigned>(tid) << shift);
+            }
+        }
+        __syncthreads();
+        kk = S.kk;
+        prefix = S.prefix;
+        mask |= 255u << shift;
+    }
+    *n_eq = S.n_eq;
+    *kk_eq = kk;
+    return prefix;
+}
+
+// Appends the keys for which `take` holds to S.sel as (key << 32) | ~index
+// (one atomic per warp and call).
+__device__ __forceinline__ void sel_push(SampleSmem &S, bool take, unsigned key, int i) {
+    const int lane = threadIdx.x & 31;
+    const unsigned act = __ballot_sync(0xffffffffu, take);
+    int base = 0;
+    if (lane == 0 && act) base = atomicAdd(&S.n_sel, __popc(act));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    const int at = base + __popc(act & ((1u << lane) - 1u));
+    if (take && at < kLoopTopKMax)
+        S.sel[at] = (static_cast<unsigned long long>(key) << 32) | (~static_cast<unsigned>(i));
+}
+
+// Ranks the m entries of S.sel (each one's rank is the number of larger
+// entries) and writes those of rank < k to S.srt in order.  (Measured on
+// B200 for 250 entries: 2.3 µs; a warp per entry 4.6 µs, 4 threads per entry
+// 3.1 µs.)
+__device__ __forceinline__ void rank_sort(SampleSmem &S, int m, int k) {
+    const int tid = threadIdx.x;
+    if (tid < 2) S.sel[m + tid] = 0;  // padding below every entry
+    __syncthreads();
+    const ulonglong2 *p2 = reinterpret_cast<const ulonglong2 *>(S.sel);
+    for (int i = tid; i < m; i += kSampleThreads) {
+        const unsigned long long x = S.sel[i];
+        int r = 0;
+#pragma unroll 4
+        for (int j = 0; j < (m + 1) / 2; ++j) {
+            const ulonglong2 y = p2[j];
+            r += (y.x > x) + (y.y > x);
+        }
+        if (r < k) S.srt[r] = x;
+    }
+    __syncthreads();
+}
+
 }  // namespace
 
 // One token draw (the daemon's sample_token_cpp; first argmax when greedy).
-// One CTA of kSampleThreads threads; thread t holds elements t + j *
-// kSampleThreads, j < ITEMS, as keys in registers.
+// One CTA of kSampleThreads threads; thread t takes elements t + j *
+// kSampleThreads, j < ITEMS.  With ITEMS = 2 (the audio logits) the keys stay
+// in registers; with more (the text logits) each thread keeps only its
+// largest key: the k-th largest of those 1024 maxima bounds the k largest
+// logits from below (k of them reach it), so only the logits at or above it
+// -- a few more than k for any spread of values -- are ranked.  The full
+// radix select over every logit remains for k above 1024 or more than 2048
+// such candidates (many equal logits).
 template <int ITEMS>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     __shared__ SampleSmem S;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int kWarpsS = kSampleThreads / 32;
+    constexpr bool kRegs = ITEMS <= 2;
+    constexpr int kRollU = kRegs ? ITEMS : 1;  // register-held keys need unrolled loops; reloaded ones do not
     // Launched as a programmatic dependent of the logits' GEMV: wait for it,
     // then let the next step's kernels launch and stage their weights while
     // the draw runs (they wait for this grid before reading its token).
     pdl_wait();
     pdl_launch_dependents();
 
-    // ---- the logits as keys, and the first argmax (std::max_element) ----
-    unsigned key[ITEMS];
+    // ---- the first argmax (std::max_element), the keys or their maximum ----
+    unsigned key[kRegs ? ITEMS : 1];
+    unsigned kmax = 0;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
+    // in groups of up to 8 loads issued together: a fully unrolled loop over
+    // 32 elements measured slower (its code is fetched cold on every launch)
+    constexpr int kG = ITEMS < 8 ? ITEMS : 8;
+#pragma unroll 1
+    for (int j0 = 0; j0 < ITEMS; j0 += kG) {
+        float v[kG];
 #pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        const int i = tid + j * kSampleThreads;
-        key[j] = 0;
-        if (i < a.n) {
-            const float v = __ldcg(a.logits + i);
-            key[j] = fkey(v);
-            argmax_merge(bv, bi, v, i);
+        for (int j = 0; j < kG; ++j) {
+            const int i = tid + (j0 + j) * kSampleThreads;
+            v[j] = i < a.n ? __ldcg(a.logits + i) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            const int i = tid + (j0 + j) * kSampleThreads;
+            const unsigned kj = i < a.n ? fkey(v[j]) : 0u;
+            if (i < a.n) argmax_merge(bv, bi, v[j], i);
+            if constexpr (kRegs) key[j0 + j] = kj;
+            kmax = kj > kmax ? kj : kmax;
         }
     }
 #pragma unroll
@@ -193,6 +290,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
         int fi = S.red_i[0];
         for (int w = 1; w < kWarpsS; ++w) argmax_merge(fv, fi, S.red_v[w], S.red_i[w]);
         S.tok = fi;
+        S.n_sel = 0;
+        S.units = 0;
+        S.mti = *a.mti;
     }
     __syncthreads();
     const int top1 = S.tok;
@@ -210,138 +310,144 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
         return;
     }
     const int k = min(min(top_k, a.n), kLoopTopKMax);  // the host keeps top_k within kLoopTopKMax
+    auto key_at = [&](int j) -> unsigned {
+        if constexpr (kRegs) return key[j];
+        else return fkey(__ldcg(a.logits + tid + j * kSampleThreads));
+    };
+    int n_eq, kk;
 
-    // ---- the k-th largest key: radix select, 8 bits per pass; the bin is
-    // found by a suffix sum over the 256 bins (threads 0..255) ----
-    unsigned prefix = 0, mask = 0;
-    int kk = k;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        if (tid < 256) S.hist[tid] = 0;
-        __syncthreads();
+    // ---- the k largest logits, in order, into S.srt ----
+    bool done = false;
+    if constexpr (!kRegs) {
+        if (k <= kSampleThreads) {
+            const unsigned lb = radix_kth(S, k, [&](auto f) { f(true, kmax); }, &n_eq, &kk);
+#pragma unroll 1
+            for (int j0 = 0; j0 < ITEMS; j0 += kG) {
+                unsigned kv[kG];
 #pragma unroll
-        for (int j = 0; j < ITEMS; ++j) {
-            const bool take = (tid + j * kSampleThreads < a.n) && (key[j] & mask) == prefix;
-            hist_add(S.hist, take, (key[j] >> shift) & 255u);
-        }
-        __syncthreads();
-        if (tid < 256) {
-            // suffix sum s(b) = sum of hist[b'] over b' >= b
-            const int h = S.hist[tid];
-            int s = h;
+                for (int j = 0; j < kG; ++j) kv[j] = tid + (j0 + j) * kSampleThreads < a.n ? key_at(j0 + j) : 0u;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_down_sync(0xffffffffu, s, o);
-                if (lane + o < 32) s += t;
+                for (int j = 0; j < kG; ++j) {
+                    const int i = tid + (j0 + j) * kSampleThreads;
+                    sel_push(S, i < a.n && kv[j] >= lb, kv[j], i);
+                }
             }
-            if (lane == 0) S.wsum[warp] = s;
-            named_sync(1, 256);
-            for (int w = warp + 1; w < 8; ++w) s += S.wsum[w];
-            if (s >= kk && s - h < kk) {  // exactly one bin
-                S.kk = kk - (s - h);
-                S.n_eq = h;
-                S.prefix = prefix | (static_cast<unsigned>(tid) << shift);
+            __syncthreads();
+            const int m = S.n_sel;
+            if (m <= kLoopTopKMax) {
+                rank_sort(S, m, k);
+                done = true;
             }
+            __syncthreads();
+            if (tid == 0) S.n_sel = 0;
+            __syncthreads();
         }
-        __syncthreads();
-        kk = S.kk;
-        prefix = S.prefix;
-        mask |= 255u << shift;
     }
-    const unsigned thr = prefix;  // every key above it is taken, and the kk lowest-index keys equal to it
-
-    // ---- gather the k entries ----
-    if (tid == 0) {
-        S.n_sel = 0;
-        S.n_eq_taken = 0;
-    }
-    __syncthreads();
-    const bool all_eq = S.n_eq == kk;  // no tie to break at the threshold (the usual case)
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-        const int i = tid + j * kSampleThreads;
-        const bool take = i < a.n && (key[j] > thr || (all_eq && key[j] == thr));
-        const unsigned act = __ballot_sync(0xffffffffu, take);
-        int base = 0;
-        if (lane == 0 && act) base = atomicAdd(&S.n_sel, __popc(act));
-        base = __shfl_sync(0xffffffffu, base, 0);
-        if (take)
-            S.sel[base + __popc(act & ((1u << lane) - 1u))] =
-                (static_cast<unsigned long long>(key[j]) << 32) | (~static_cast<unsigned>(i));
-    }
-    if (!all_eq) {
-        // keys equal to the threshold in index order: element chunks of
-        // kSampleThreads, each scanned block-wide
-#pragma unroll
+    if (!done) {
+        // every key above the k-th largest, and of those equal to it the
+        // lowest-index ones (block-scanned in index order only when the
+        // threshold value occurs more often than it is needed)
+        const unsigned thr = radix_kth(
+            S, k,
+            [&](auto f) {
+#pragma unroll kRollU
+                for (int j = 0; j < ITEMS; ++j) {
+                    const bool valid = tid + j * kSampleThreads < a.n;
+                    f(valid, valid ? key_at(j) : 0u);
+                }
+            },
+            &n_eq, &kk);
+        const bool all_eq = n_eq == kk;
+#pragma unroll kRollU
         for (int j = 0; j < ITEMS; ++j) {
             const int i = tid + j * kSampleThreads;
-            const bool eq = i < a.n && key[j] == thr;
-            const unsigned bal = __ballot_sync(0xffffffffu, eq);
-            if (lane == 0) S.wsum[warp] = __popc(bal);
+            const unsigned kj = i < a.n ? key_at(j) : 0u;
+            sel_push(S, i < a.n && (kj > thr || (all_eq && kj == thr)), kj, i);
+        }
+        if (!all_eq) {
+            if (tid == 0) S.n_eq_taken = 0;
             __syncthreads();
-            int before = S.n_eq_taken;
-            for (int w = 0; w < warp; ++w) before += S.wsum[w];
-            before += __popc(bal & ((1u << lane) - 1u));
-            if (eq && before < kk)
-                S.sel[atomicAdd(&S.n_sel, 1)] = (static_cast<unsigned long long>(thr) << 32) | (~static_cast<unsigned>(i));
-            __syncthreads();
-            if (tid == 0) {
-                int t = 0;
-                for (int w = 0; w < kWarpsS; ++w) t += S.wsum[w];
-                S.n_eq_taken += t;
+#pragma unroll 1
+            for (int j = 0; j < ITEMS; ++j) {
+                const int i = tid + j * kSampleThreads;
+                const bool eq = i < a.n && key_at(j) == thr;
+                const unsigned bal = __ballot_sync(0xffffffffu, eq);
+                if (lane == 0) S.wsum[warp] = __popc(bal);
+                __syncthreads();
+                int before = S.n_eq_taken;
+                for (int w = 0; w < warp; ++w) before += S.wsum[w];
+                before += __popc(bal & ((1u << lane) - 1u));
+                if (eq && before < kk)
+                    S.sel[atomicAdd(&S.n_sel, 1)] =
+                        (static_cast<unsigned long long>(thr) << 32) | (~static_cast<unsigned>(i));
+                __syncthreads();
+                if (tid == 0) {
+                    int t = 0;
+                    for (int w = 0; w < kWarpsS; ++w) t += S.wsum[w];
+                    S.n_eq_taken += t;
+                }
+                __syncthreads();
             }
-            __syncthreads();
         }
+        __syncthreads();
+        rank_sort(S, k, k);
     }
-    __syncthreads();
-    // ---- sort them: each entry's rank is the number of larger entries ----
-    if (tid < 2) S.sel[k + tid] = 0;  // padding below every entry
-    __syncthreads();
-    for (int i = tid; i < k; i += kSampleThreads) {
-        const unsigned long long x = S.sel[i];
-        int r = 0;
-        const ulonglong2 *p2 = reinterpret_cast<const ulonglong2 *>(S.sel);
-        for (int j = 0; j < (k + 1) / 2; ++j) {
-            const ulonglong2 y = p2[j];
-            r += (y.x > x) + (y.y > x);
-        }
-        S.srt[r] = x;
-    }
-    __syncthreads();
 
     // ---- probabilities: exp(l_i / temp - l_0 / temp), rounded to float ----
+    // p_0 is exactly 1, so their float sum in order is positive unless a
+    // term is NaN (a NaN or infinite logit): then the reference keeps the
+    // first entry.  std::discrete_distribution normalises by the double sum
+    // in order and draws nothing for one weight.
     const float max_l = __fdiv_rn(fkey_value(static_cast<unsigned>(S.srt[0] >> 32)), temp);
+    bool nan_p = false;
     for (int i = tid; i < k; i += kSampleThreads) {
         const float li = fkey_value(static_cast<unsigned>(S.srt[i] >> 32));
-        S.prob[i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(__fdiv_rn(li, temp), max_l))));
+        const float p = static_cast<float>(exp(static_cast<double>(__fsub_rn(__fdiv_rn(li, temp), max_l))));
+        S.prob[i] = p;
+        nan_p |= isnan(p);
+    }
+    const bool any_nan = __syncthreads_or(nan_p);
+    const int tok0 = static_cast<int>(~static_cast<unsigned>(S.srt[0]));
+    if (any_nan || k < 2) {
+        if (tid == 0) *a.out = tok0;
+        return;
+    }
+    // The double sum in order.  Every partial sum is below 2^e, e = bits of
+    // k (p_i <= 1); when every p_i is zero or a multiple of 2^(e - 53) (its
+    // exponent at least e - 30), every partial sum is a multiple of 2^(e - 53)
+    // below 2^e, hence exact, and the sum in order is the exact sum: then it
+    // is formed in parallel as an integer count of 2^(e - 53).  Otherwise
+    // one thread adds in order.
+    const int e = 32 - __clz(k);
+    const double unit = ldexp(1.0, e - 53);
+    bool on_grid = true;
+    unsigned long long units = 0;
+    for (int i = tid; i < k; i += kSampleThreads) {
+        const float p = S.prob[i];
+        const int ex = static_cast<int>((__float_as_uint(p) >> 23) & 255u) - 127;
+        if (p != 0.0f && ex < e - 30) on_grid = false;
+        units += static_cast<unsigned long long>(__dmul_rn(static_cast<double>(p), ldexp(1.0, 53 - e)));
+    }
+    const bool exact = __syncthreads_and(on_grid);
+    if (exact) {
+        for (int o = 16; o > 0; o >>= 1) units += __shfl_xor_sync(0xffffffffu, units, o);
+        if (lane == 0) atomicAdd(&S.units, units);
     }
     __syncthreads();
-    // their float sum in order must be positive; std::discrete_distribution
-    // normalises by the double sum in order and draws nothing for one weight
-    if (tid == 0) {
-        float sum_p = 0.0f;
+    if (exact && tid == 0) S.total = __dmul_rn(static_cast<double>(S.units), unit);  // below 2^53 units: exact
+    if (!exact && tid == 0) {
         double total = 0.0;
         int i = 0;
         for (; i + 4 <= k; i += 4) {
             const float4 p = *reinterpret_cast<const float4 *>(S.prob + i);
-            sum_p = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum_p, p.x), p.y), p.z), p.w);
             total = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(total, static_cast<double>(p.x)), static_cast<double>(p.y)),
                                         static_cast<double>(p.z)),
                               static_cast<double>(p.w));
         }
-        for (; i < k; ++i) {
-            sum_p = __fadd_rn(sum_p, S.prob[i]);
-            total = __dadd_rn(total, static_cast<double>(S.prob[i]));
-        }
-        S.draw = sum_p > 0.0f && !isnan(sum_p) && k >= 2;
+        for (; i < k; ++i) total = __dadd_rn(total, static_cast<double>(S.prob[i]));
         S.total = total;
-        S.mti = *a.mti;
     }
     __syncthreads();
-    const int tok0 = static_cast<int>(~static_cast<unsigned>(S.srt[0]));
-    if (!S.draw) {
-        if (tid == 0) *a.out = tok0;
-        return;
-    }
     const double total = S.total;
     for (int i = tid; i < k; i += kSampleThreads) S.q[i] = __ddiv_rn(static_cast<double>(S.prob[i]), total);
     // the generator: two outputs; its 624 words pass through shared memory

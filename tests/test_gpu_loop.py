@@ -52,6 +52,13 @@ def _tie_cases(seed=11):
     for n, k in [(2048, 250), (2048, 1024), (2048, 2048), (32000, 25), (32000, 2048), (777, 777)]:
         x = (np.round(r.normal(0, 2, n) * 2) / 2).astype(np.float32)
         out.append((n, 0.8, k, 0, x))
+    # more equal logits than the text sampler's candidate buffer holds: the full radix path
+    x = np.zeros(32000, np.float32)
+    x[r.choice(32000, 10, replace=False)] = r.normal(1, 0.5, 10).astype(np.float32) + 1
+    out.append((32000, 0.7, 25, 0, x))
+    out.append((32000, 0.7, 25, 0, np.full(32000, 0.25, np.float32)))
+    out.append((2048, 0.8, 250, 0, np.full(2048, -3.0, np.float32)))
+    out.append((32000, 0.7, 1024, 0, (np.round(r.normal(0, 2, 32000) * 4) / 4).astype(np.float32)))
     return out
 
 

@@ -60,6 +60,9 @@ def sampler_cases(seed=7):
     x = (r.permutation(2048).astype(np.float32) * np.float32(0.01)).astype(np.float32)
     x[2048 - 1000:] = np.float32(-1e9)
     out.append((2048, 0.8, 1024, 0, x))
+    x = ((r.permutation(2048) / 2048.0 * 2.0 - 1.0) * 8.0).astype(np.float32)
+    x[17] = np.float32(np.inf)                                 # an infinite logit: NaN weights, first entry kept
+    out.append((2048, 0.8, 250, 0, x))
     for pause in (3, 0):                                        # text rule: a pause token keeps the argmax
         x = (r.permutation(1000).astype(np.float32) * np.float32(0.01)).astype(np.float32)
         x[pause] = np.float32(50.0)
