@@ -16,13 +16,12 @@ import pytest
 
 from bmo_jetson_b200 import engine, synth
 from tests import sampler
+from tests.daemon import daemon_restated, fresh_state
 from tests.test_sampler import restated_draws, sampler_cases
 
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
-
-SILENCE = [1049, 243, 783, 1562, 340, 2010, 183, 1665]  # bmo_daemon.cpp's user silence tokens
 
 
 def _rng_words(g):
@@ -84,43 +83,6 @@ def test_device_sampler_generator_wraps():
     g = sampler.MT19937(99)
     assert toks == [sampler.sample(x, 0.8, 250, g) for _ in range(700)]
     np.testing.assert_array_equal(words, _rng_words(g))
-
-
-def daemon_restated(e, st, n_frames, users, sampling, tt, kt, ta, ka, rng):
-    """Frames of the daemon's loop on the library's per-step entry points.
-    `st` is the delay-line state (fresh_state() at frame 0, with `e`'s rings
-    empty); `users[i]` is call frame i's user tokens, or users is None for
-    silence."""
-    K = e.n_codebooks
-    tpad, apad = e.text_vocab, e.audio_vocab
-    tn, an = min(e.text_vocab, 32000), min(e.audio_vocab, 2048)
-    rows = []
-    for i in range(n_frames):
-        f = st["frame"]
-        u = list(users[i]) if users is not None else SILENCE
-        if f == 0:
-            t = [tpad] + [apad] * 16
-        elif f == 1:
-            t = [st["text"], st["audio"][0]] + [apad] * 7 + [u[0]] + [apad] * 7
-        else:
-            t = [st["text"]] + st["audio"] + [u[0]] + st["user"][1:]
-        e.pos = f
-        z, lg = e.forward_temporal(np.array(t[:K], np.int32), copy=True)
-        text = sampler.daemon_text(lg[:tn], sampling, tt, kt, rng)
-        prev, audio = text, []
-        for cb in range(8):
-            al = e.forward_depth(cb, prev, z, copy=True)[:an]
-            prev = sampler.sample(al, ta, ka, rng) if sampling else int(np.argmax(al))
-            audio.append(prev)
-        rows.append([text] + audio + [st["cb0"]] + audio[1:])
-        st.update(frame=f + 1, text=text, audio=audio, user=u, cb0=audio[0])
-    return np.array(rows, np.int32)
-
-
-def fresh_state(e):
-    """The daemon's start state (bmo_daemon.cpp:641-645) on an emptied engine."""
-    e.reset()
-    return dict(frame=0, text=e.text_vocab, audio=[e.audio_vocab] * 8, user=[e.audio_vocab] * 8, cb0=1049)
 
 
 CASES = {"tiny": 256, "tiny17": 256, "config2": 512}
