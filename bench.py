@@ -219,13 +219,14 @@ def frame_bytes(e):
     return temporal + 8 * dep_step + kv, temporal, 8 * dep_step, kv
 
 
-def gemv_roofline(local, peak_gbs, iters=40):
+def gemv_roofline(local, peak_gbs, iters=40, exact=False):
     """Times the dominant kernel of the default path (the reference-order Q4_0
     GEMV, FFN-in shape 22528x4096 with the fused RMSNorm + SwiGLU) on resident buffers: 8 distinct weight copies
     (415 MB > L2) rotated per launch, `iters` back-to-back launches captured in
     one CUDA graph (as the decode frame runs them), CUDA events on the
     replaying stream.  The same launches issued one by one from the host are
-    reported beside it (`eager_us_per_launch`)."""
+    reported beside it (`eager_us_per_launch`).  exact=True times the
+    exact-order GEMV (bmo_k_gemv_q4_0, double sums) on the same shape."""
     import torch
     from bmo_jetson_b200 import engine
     L = engine.lib()
@@ -239,10 +240,16 @@ def gemv_roofline(local, peak_gbs, iters=40):
     x = torch.randn(cols, device=dev)
     g = torch.ones(cols, device=dev)
     y = torch.empty(F, device=dev)
+    sbytes = L.bmo_k_gemv_scratch_bytes(rows, cols, 1, F)
+    scratch = torch.zeros(max(sbytes, 1), dtype=torch.uint8, device=dev)
 
     def launch(i, st):
-        rc = L.bmo_k_gemv_q4_0_ref(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8, None,
-                                   y.data_ptr(), None, None, None, st.cuda_stream)
+        if exact:
+            rc = L.bmo_k_gemv_q4_0(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8, None,
+                                   y.data_ptr(), None, None, scratch.data_ptr(), sbytes, 0, st.cuda_stream)
+        else:
+            rc = L.bmo_k_gemv_q4_0_ref(mats[i % 8].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8,
+                                       None, y.data_ptr(), None, None, None, st.cuda_stream)
         assert rc == 0, rc
 
     for i in range(8):
@@ -270,11 +277,99 @@ def gemv_roofline(local, peak_gbs, iters=40):
     del graph
     alg = rows * cols // 32 * 18 + cols * 4 * 2 + F * 4
     achieved = alg / (ms * 1e-3) / 1e9
-    return {"kernel": "gemv_ref_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0 in the reference's fp32 order, "
-                      "fused RMSNorm+Q8_1, SwiGLU)",
+    name = ("gemv_q4_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0, exact order" if exact else
+            "gemv_ref_kernel<kProNorm,kEpiSwiGLU> (FFN-in 22528x4096 Q4_0 in the reference's fp32 order")
+    return {"kernel": name + ", fused RMSNorm+Q8_1, SwiGLU)",
             "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": achieved,
             "eager_us_per_launch": eager_ms * 1e3, "timing": f"{iters} launches in one CUDA graph, weights rotated "
                                                            "over 8 copies (415 MB > L2)"}
+
+
+def batch_gemm_timing(local, peak_gbs, iters=20, sessions=64):
+    """--kernel batch_qkv: one batched GEMM through the kernel-level entry point
+    bmo_k_batch_gemm_q4_0 (tensor cores, exact form) on the temporal QKV shape
+    12288x4096 with the RMSNorm prologue, `sessions` sessions, weights rotated
+    over 8 copies (226 MB > L2) so each launch streams its weights from HBM;
+    CUDA events around `iters` back-to-back launches on the launching stream.
+    Each call is a stage kernel (norm + Q8_1 of every session) and the GEMM."""
+    import torch
+    from bmo_jetson_b200 import engine
+    L = engine.lib()
+    rows, cols = 12288, 4096
+    dev = torch.device("cuda", local)
+    s = torch.cuda.current_stream(dev)
+    nbytes = L.bmo_k_q4_0_tiled_bytes(rows, cols, 0, 0)
+    mats = [torch.randint(0, 255, (nbytes,), dtype=torch.uint8, device=dev) for _ in range(8)]
+    for m in mats:  # sane fp16 scales: 0x2000 ~ 0.0078
+        m.view(-1, 4608)[:, 4096:].fill_(0x20)
+    x = torch.randn(sessions, cols, device=dev)
+    g = torch.ones(cols, device=dev)
+    y = torch.empty(sessions, rows, device=dev)
+    sbytes = L.bmo_k_batch_gemm_scratch_bytes(rows, cols, 0, 0, sessions)
+    scratch = torch.zeros(max(sbytes, 1), dtype=torch.uint8, device=dev)
+
+    def launch(i):
+        rc = L.bmo_k_batch_gemm_q4_0(mats[i % 8].data_ptr(), rows, cols, 0, 0, x.data_ptr(), g.data_ptr(), 1e-8,
+                                     None, y.data_ptr(), sessions, 1, scratch.data_ptr(), sbytes, s.cuda_stream)
+        assert rc == 0, rc
+
+    for i in range(8):
+        launch(i)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(iters):
+        launch(i)
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / iters
+    alg = rows * cols // 32 * 18 + sessions * (cols + rows) * 4 + cols * 4
+    return {"kernel": f"batch_stage_kernel + batch_mma_kernel (QKV 12288x4096 Q4_0, {sessions} sessions, "
+                      "tensor cores, exact form, RMSNorm prologue)",
+            "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": alg / (ms * 1e-3) / 1e9,
+            "frac": alg / (ms * 1e-3) / 1e9 / peak_gbs,
+            "timing": f"{iters} eager launches, weights rotated over 8 copies (226 MB > L2)"}
+
+
+def attn_ref_timing(local, peak_gbs, iters=20, n_layers=32):
+    """--kernel attn_ref: the default path's temporal decode attention through
+    bmo_k_decode_attention_ref (32 heads x 128, fp16 ring of 512 slots, pos
+    700 so the ring has wrapped), the layer rotated over `n_layers` rings
+    (268 MB > L2) so each launch reads its K/V window from HBM; CUDA events
+    around `iters` back-to-back launches on the launching stream."""
+    import torch
+    from bmo_jetson_b200 import engine
+    L = engine.lib()
+    hd, nh, n_ctx, pos = 128, 32, N_CTX, START_POS
+    dev = torch.device("cuda", local)
+    s = torch.cuda.current_stream(dev)
+    q, k, v = (torch.randn(nh * hd, device=dev) for _ in range(3))
+    kc = (0.5 * torch.randn(n_layers * nh * n_ctx * hd, device=dev)).half()
+    vc = (0.5 * torch.randn(n_layers * nh * n_ctx * hd, device=dev)).half()
+    o = torch.empty(nh * hd, device=dev)
+    pos_d = torch.tensor([pos], dtype=torch.int32, device=dev)
+
+    def launch(i):
+        rc = L.bmo_k_decode_attention_ref(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                          o.data_ptr(), hd, nh, nh, n_ctx, pos_d.data_ptr(), i % n_layers,
+                                          s.cuda_stream)
+        assert rc == 0, rc
+
+    for i in range(n_layers):
+        launch(i)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(iters):
+        launch(i)
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / iters
+    alg = 2 * nh * n_ctx * hd * 2 + 4 * nh * hd * 4
+    return {"kernel": "attn_ref_kernel<128, 8> (32 heads x 128, fp16 ring of 512 slots, pos 700, reference order)",
+            "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": alg / (ms * 1e-3) / 1e9,
+            "frac": alg / (ms * 1e-3) / 1e9 / peak_gbs,
+            "timing": f"{iters} eager launches, layers rotated over {n_layers} rings (268 MB > L2)"}
 
 
 def bench_batch(path, local, dist, sessions, steps, warmup, rank):
@@ -683,7 +778,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kv", default="f16", choices=["f16", "q4_0"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-only", action="store_true", help="only the standalone GEMV timing (profiling)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only the standalone timing of one kernel (profiling); which one: --kernel")
+    ap.add_argument("--kernel", default="ffn_in", choices=["ffn_in", "ffn_in_exact", "batch_qkv", "attn_ref"],
+                    help="--kernel-only: FFN-in GEMV in the reference order (default) or the exact order, the "
+                         "batched 64-session QKV GEMM, or the reference-order temporal attention")
     ap.add_argument("--sessions", type=int, default=64,
                     help="config 4: sessions per GPU of the batched measurement (0: skip it)")
     ap.add_argument("--batch-only", action="store_true", help="only the batched-sessions measurement")
@@ -713,7 +812,13 @@ def main():
         return 0
     if args.kernel_only:
         torch.cuda.set_device(local)
-        r = gemv_roofline(local, peak, iters=max(args.steps, 1))
+        iters = max(args.steps, 1)
+        if args.kernel == "batch_qkv":
+            r = batch_gemm_timing(local, peak, iters=iters)
+        elif args.kernel == "attn_ref":
+            r = attn_ref_timing(local, peak, iters=iters)
+        else:
+            r = gemv_roofline(local, peak, iters=iters, exact=args.kernel == "ffn_in_exact")
         print(json.dumps(r), flush=True)
         return 0
 
