@@ -44,6 +44,7 @@ constexpr int kMaxCtxSingle = 64;   // one CTA per head (the depformer's short r
 template <int HD, int NSPLIT>
 struct RefAttnLayout {
     static constexpr int kDims = HD / NSPLIT;  // V dimensions per CTA
+    static constexpr int kKStride = HD + 8;    // halves per staged K row: rows 16 bytes apart in the banks
     int n_ctx, rows;                           // rows: positions scored per CTA
     size_t off_s, off_k, off_v, off_red, bytes;
     __host__ __device__ explicit RefAttnLayout(int n) : n_ctx(n), rows((n + NSPLIT - 1) / NSPLIT) {
@@ -52,7 +53,7 @@ struct RefAttnLayout {
         o += static_cast<size_t>(n) * 4;
         o = (o + 127) & ~static_cast<size_t>(127);
         off_k = o;
-        o += static_cast<size_t>(rows) * HD * 2;
+        o += static_cast<size_t>(rows) * kKStride * 2;
         off_v = o;
         o += static_cast<size_t>(n) * kDims * 2;
         off_red = o;
@@ -65,7 +66,7 @@ struct RefAttnLayout {
 template <int HD, int NSPLIT>
 __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constant__ AttnArgs a) {
     using Lay = RefAttnLayout<HD, NSPLIT>;
-    constexpr int kDims = Lay::kDims;
+    constexpr int kDims = Lay::kDims, kKS = Lay::kKStride;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Lay lay(a.n_ctx);
     float *sq = reinterpret_cast<float *>(smem_raw);
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constan
         for (int e = tid; e < nk; e += kThreads) {
             const int i = i0 + e / kKPieces, pc = e % kKPieces;
             const int slot = (start + i) % a.n_ctx;
-            cp_async16(kb + (i - i0) * HD + pc * 8, kc + static_cast<long long>(slot) * HD + pc * 8);
+            cp_async16(kb + (i - i0) * kKS + pc * 8, kc + static_cast<long long>(slot) * HD + pc * 8);
         }
         const int nv = (W - 1) * kVPieces;
         for (int e = tid; e < nv; e += kThreads) {
@@ -116,13 +117,13 @@ __global__ void __launch_bounds__(kThreads) attn_ref_kernel(const __grid_constan
     for (int d = tid; d < HD; d += kThreads) sq[d] = __ldcg(a.q + h * HD + d);
     const int cur = pos % a.n_ctx;
     if (i0 < i1 && i1 == W)
-        for (int d = tid; d < HD; d += kThreads) kb[(W - 1 - i0) * HD + d] = __ldcg(kc + static_cast<long long>(cur) * HD + d);
+        for (int d = tid; d < HD; d += kThreads) kb[(W - 1 - i0) * kKS + d] = __ldcg(kc + static_cast<long long>(cur) * HD + d);
     for (int d = tid; d < kDims; d += kThreads) vb[(W - 1) * kDims + d] = __ldcg(vc + static_cast<long long>(cur) * HD + d);
     cp_async_wait_all();
     __syncthreads();
 
     // ---- scores of positions [i0, i1): thread = (position, 32-dim group) ----
-    attn_ref_scores<HD, kThreads>(sq, kb, i0, i1, a.scale, tid, [&](int i, float s) {
+    attn_ref_scores<HD, kThreads, kKS>(sq, kb, i0, i1, a.scale, tid, [&](int i, float s) {
         if constexpr (NSPLIT == 1) {
             ss[i] = s;
         } else {

@@ -18,26 +18,37 @@
 
 namespace bmo {
 
-// Scores of positions [i0, i1): kb holds their K rows (row i - i0, HD fp16
-// values each), sq the query.  Each of the NT threads takes (position,
+// Scores of positions [i0, i1): kb holds their K rows (row i - i0 at kb +
+// (i - i0) * KS, HD fp16 values each; KS * 2 a multiple of 16 bytes), sq the
+// query (16-byte aligned).  Each of the NT threads takes (position,
 // 32-dimension group) tasks; all NT threads (whole warps) must call it.
-// emit(i, s) receives each score once.
-template <int HD, int NT, typename Emit>
+// emit(i, s) receives each score once.  With KS = HD + 8 the rows a warp
+// reads at once fall on distinct shared-memory banks (KS = HD puts every
+// row of a warp on the same banks).
+template <int HD, int NT, int KS, typename Emit>
 __device__ __forceinline__ void attn_ref_scores(const float *sq, const __half *kb, int i0, int i1, float scale,
                                                 int tid, Emit emit) {
+    static_assert(KS >= HD && KS % 8 == 0, "K rows: whole 16-byte pieces");
     constexpr int kGroups = HD / 32;
     const int lane = tid & 31;
     const int g = tid % kGroups;  // kGroups divides 32: a position's groups are adjacent lanes
     float qg[32];
+    const float4 *q4 = reinterpret_cast<const float4 *>(sq + 32 * g);
 #pragma unroll
-    for (int d = 0; d < 32; ++d) qg[d] = sq[32 * g + d];
+    for (int d = 0; d < 8; ++d) {
+        const float4 t = q4[d];
+        qg[4 * d] = t.x;
+        qg[4 * d + 1] = t.y;
+        qg[4 * d + 2] = t.z;
+        qg[4 * d + 3] = t.w;
+    }
     const int tasks = (i1 - i0) * kGroups;
     for (int u0 = 0; u0 < tasks; u0 += NT) {
         const int u = u0 + tid;
         const int i = i0 + u / kGroups;
         const bool on = u < tasks;
         float p[32];
-        const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (on ? (i - i0) : 0) * HD + 32 * g);
+        const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (on ? (i - i0) : 0) * KS + 32 * g);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint4 w = kr[j];

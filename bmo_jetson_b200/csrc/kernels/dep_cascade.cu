@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kCT, 1) dep_cascade_kernel(const __grid_consta
                     // positions 0..W-1 sit at slots 0..W-1 (the ring never wraps in a cascade)
                     const __half *kb = kk + op.layer * a.n_ctx * kHD;
                     const __half *vb = kv + op.layer * a.n_ctx * kHD;
-                    attn_ref_scores<kHD, kAttnThreads>(qv, kb, 0, W, a.scale, tid, [&](int i, float s) { ss[i] = s; });
+                    attn_ref_scores<kHD, kAttnThreads, kHD>(qv, kb, 0, W, a.scale, tid, [&](int i, float s) { ss[i] = s; });
                     named_sync(kBarAttn, kAttnThreads);
                     attn_ref_softmax<kHD, kAttnThreads>(ss, W, red, tid, [] { named_sync(kBarAttn, kAttnThreads); });
                     if (tid < kHD) bcast(cl, dst + tid, attn_ref_vchain(ss, vb + tid, W, kHD), cs);

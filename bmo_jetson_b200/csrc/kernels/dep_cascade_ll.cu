@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(kLT, 1) dep_cascade_ll_kernel(const __grid_con
                     } else {  // positions 0..W-1 sit at slots 0..W-1 (the ring never wraps in a cascade)
                         const __half *kb = kk + op.layer * a.n_ctx * kLHD;
                         const __half *vb = kv + op.layer * a.n_ctx * kLHD;
-                        attn_ref_scores<kLHD, kLAttnThreads>(qv, kb, 0, W, a.scale, tid,
+                        attn_ref_scores<kLHD, kLAttnThreads, kLHD>(qv, kb, 0, W, a.scale, tid,
                                                              [&](int i, float s) { ss[i] = s; });
                         named_sync(kLBarAttn, kLAttnThreads);
                         attn_ref_softmax<kLHD, kLAttnThreads>(ss, W, red, tid,
