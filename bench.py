@@ -285,6 +285,62 @@ def gemv_roofline(local, peak_gbs, iters=40, exact=False):
                                                            "over 8 copies (415 MB > L2)"}
 
 
+def dep_gemv_timing(local, peak_gbs, iters=40, copies=48):
+    """--kernel dep_ffn_in: a depformer GEMV alone, the FFN-in of one step
+    (5632x1024 Q4_0, fused RMSNorm + SwiGLU, reference order) through
+    bmo_k_gemv_q4_0_ref, weights rotated over `copies` copies (156 MB > L2)
+    so each launch streams its 3.2 MB from HBM; CUDA events around `iters`
+    back-to-back launches, eager and captured in one CUDA graph."""
+    import torch
+    from bmo_jetson_b200 import engine
+    L = engine.lib()
+    rows, cols, F = 5632, 1024, 2816
+    dev = torch.device("cuda", local)
+    s = torch.cuda.current_stream(dev)
+    nbytes = L.bmo_k_q4_0_tiled_bytes(rows, cols, 1, F)
+    mats = [torch.randint(0, 255, (nbytes,), dtype=torch.uint8, device=dev) for _ in range(copies)]
+    for m in mats:  # sane fp16 scales: 0x2000 ~ 0.0078
+        m.view(-1, 4608)[:, 4096:].fill_(0x20)
+    x = torch.randn(cols, device=dev)
+    g = torch.ones(cols, device=dev)
+    y = torch.empty(F, device=dev)
+
+    def launch(i, st):
+        rc = L.bmo_k_gemv_q4_0_ref(mats[i % copies].data_ptr(), rows, cols, 1, F, x.data_ptr(), g.data_ptr(), 1e-8,
+                                   None, y.data_ptr(), None, None, None, st.cuda_stream)
+        assert rc == 0, rc
+
+    for i in range(copies):
+        launch(i, s)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(iters):
+        launch(i, s)
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    eager_ms = a.elapsed_time(b) / iters
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(dev)
+    with torch.cuda.graph(graph, stream=cs):
+        for i in range(iters):
+            launch(i, cs)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    a.record(s)
+    graph.replay()
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / iters
+    del graph
+    alg = rows * cols // 32 * 18 + cols * 4 * 2 + F * 4
+    return {"kernel": "gemv_ref_kernel<kProNorm,kEpiSwiGLU> (depformer FFN-in 5632x1024 Q4_0, reference order, "
+                      "fused RMSNorm+Q8_1, SwiGLU)",
+            "bytes_per_launch": alg, "us_per_launch": ms * 1e3, "achieved_gbs": alg / (ms * 1e-3) / 1e9,
+            "frac": alg / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us_per_launch": eager_ms * 1e3,
+            "timing": f"{iters} launches in one CUDA graph, weights rotated over {copies} copies (156 MB > L2)"}
+
+
 def batch_gemm_timing(local, peak_gbs, iters=20, sessions=64):
     """--kernel batch_qkv: one batched GEMM through the kernel-level entry point
     bmo_k_batch_gemm_q4_0 (tensor cores, exact form) on the temporal QKV shape
@@ -780,9 +836,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the standalone timing of one kernel (profiling); which one: --kernel")
-    ap.add_argument("--kernel", default="ffn_in", choices=["ffn_in", "ffn_in_exact", "batch_qkv", "attn_ref"],
-                    help="--kernel-only: FFN-in GEMV in the reference order (default) or the exact order, the "
-                         "batched 64-session QKV GEMM, or the reference-order temporal attention")
+    ap.add_argument("--kernel", default="ffn_in",
+                    choices=["ffn_in", "ffn_in_exact", "dep_ffn_in", "batch_qkv", "attn_ref"],
+                    help="--kernel-only: FFN-in GEMV in the reference order (default) or the exact order, a "
+                         "depformer FFN-in GEMV, the batched 64-session QKV GEMM, or the reference-order temporal "
+                         "attention")
     ap.add_argument("--sessions", type=int, default=64,
                     help="config 4: sessions per GPU of the batched measurement (0: skip it)")
     ap.add_argument("--batch-only", action="store_true", help="only the batched-sessions measurement")
@@ -817,6 +875,8 @@ def main():
             r = batch_gemm_timing(local, peak, iters=iters)
         elif args.kernel == "attn_ref":
             r = attn_ref_timing(local, peak, iters=iters)
+        elif args.kernel == "dep_ffn_in":
+            r = dep_gemv_timing(local, peak, iters=iters)
         else:
             r = gemv_roofline(local, peak, iters=iters, exact=args.kernel == "ffn_in_exact")
         print(json.dumps(r), flush=True)
